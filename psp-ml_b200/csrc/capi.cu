@@ -1,0 +1,379 @@
+// capi.cu - C ABI: errors, contexts, pinned host memory, per-op int8 calls
+// and TMA descriptor encoding.
+#include <cudaTypedefs.h>
+
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+
+#include "kernels.h"
+#include "runtime.h"
+
+namespace pspml {
+
+namespace {
+thread_local std::string g_last_error;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+int set_error(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PSPML_OK;
+  cudaGetLastError();  // clear sticky-free errors so the next call starts clean
+  return set_error(e == cudaErrorMemoryAllocation ? PSPML_ERR_OOM : PSPML_ERR_CUDA,
+                   std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int validate_desc(const pspml_op_desc* d) {
+  if (d == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null op descriptor");
+  if (d->in_h <= 0 || d->in_w <= 0 || d->in_c <= 0 || d->out_h <= 0 || d->out_w <= 0 ||
+      d->out_c <= 0)
+    return set_error(PSPML_ERR_INVALID_ARG, "non-positive tensor dimension");
+  if (d->zp_in < -128 || d->zp_in > 127 || d->zp_out < -128 || d->zp_out > 127)
+    return set_error(PSPML_ERR_INVALID_ARG, "zero point outside int8");
+  if (d->act_min < -128 || d->act_max > 127 || d->act_min > d->act_max)
+    return set_error(PSPML_ERR_INVALID_ARG, "bad activation range");
+  const bool windowed = d->kind == PSPML_OP_CONV2D || d->kind == PSPML_OP_DEPTHWISE_CONV2D ||
+                        d->kind == PSPML_OP_MAX_POOL2D || d->kind == PSPML_OP_AVERAGE_POOL2D;
+  if (windowed) {
+    if (d->kernel_h <= 0 || d->kernel_w <= 0 || d->stride_h <= 0 || d->stride_w <= 0 ||
+        d->pad_top < 0 || d->pad_left < 0 || d->pad_bottom < 0 || d->pad_right < 0)
+      return set_error(PSPML_ERR_INVALID_ARG, "bad kernel / stride / padding");
+    const int64_t eh = (static_cast<int64_t>(d->in_h) + d->pad_top + d->pad_bottom -
+                        d->kernel_h) / d->stride_h + 1;
+    const int64_t ew = (static_cast<int64_t>(d->in_w) + d->pad_left + d->pad_right -
+                        d->kernel_w) / d->stride_w + 1;
+    if (eh != d->out_h || ew != d->out_w)
+      return set_error(PSPML_ERR_INVALID_ARG,
+                       "output size does not match input, kernel, stride and padding");
+  }
+  switch (d->kind) {
+    case PSPML_OP_CONV2D:
+      break;
+    case PSPML_OP_DEPTHWISE_CONV2D:
+      if (d->out_c != d->in_c)
+        return set_error(PSPML_ERR_UNSUPPORTED, "depthwise conv needs depth multiplier 1");
+      break;
+    case PSPML_OP_FULLY_CONNECTED:
+      if (d->out_h != 1 || d->out_w != 1)
+        return set_error(PSPML_ERR_INVALID_ARG, "fully connected output must be [1,1,N]");
+      break;
+    case PSPML_OP_MAX_POOL2D:
+    case PSPML_OP_AVERAGE_POOL2D:
+      if (d->out_c != d->in_c || d->zp_out != d->zp_in)
+        return set_error(PSPML_ERR_INVALID_ARG, "pooling keeps channels and quantisation");
+      break;
+    case PSPML_OP_RESHAPE:
+      if (static_cast<int64_t>(d->in_h) * d->in_w * d->in_c !=
+          static_cast<int64_t>(d->out_h) * d->out_w * d->out_c)
+        return set_error(PSPML_ERR_INVALID_ARG, "reshape changes the element count");
+      break;
+    default:
+      return set_error(PSPML_ERR_INVALID_ARG, "unknown op kind");
+  }
+  return PSPML_OK;
+}
+
+int wait_event(pspml_ctx* ctx, cudaEvent_t ev) {
+  if (ctx->timeout_ms <= 0) return cuda_status(cudaEventSynchronize(ev), "cudaEventSynchronize");
+  const auto deadline =
+      std::chrono::steady_clock::now() + std::chrono::milliseconds(ctx->timeout_ms);
+  while (true) {
+    const cudaError_t e = cudaEventQuery(ev);
+    if (e == cudaSuccess) return PSPML_OK;
+    if (e != cudaErrorNotReady) return cuda_status(e, "cudaEventQuery");
+    if (std::chrono::steady_clock::now() > deadline)
+      return set_error(PSPML_ERR_TIMEOUT, "device work did not finish before the deadline");
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+CUresult encode_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                           const uint64_t* strides_bytes, const uint32_t* box,
+                           const uint32_t* elem_strides, CUtensorMapSwizzle swizzle) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (fn == nullptr) return CUDA_ERROR_NOT_FOUND;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = elem_strides[i];
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<cuuint32_t>(rank),
+            const_cast<void*>(base), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+// Runs a conv or FC through the tensor-core path using `ws` for the folded
+// bias and border-class tables.
+int run_tc_with_workspace(pspml_ctx* ctx, const pspml_op_desc* d, GemmPath path, int64_t batch,
+                          const int8_t* in, const int8_t* filter, const int32_t* bias,
+                          const int32_t* mult, const int32_t* shift, int8_t* out,
+                          uint8_t* ws, size_t ws_bytes, cudaStream_t s) {
+  static thread_local BorderClasses bc;
+  if (path == GemmPath::kTc4d) {
+    if (!build_border_classes(*d, &bc))
+      return set_error(PSPML_ERR_UNSUPPORTED, "too many border classes");
+  } else {
+    bc.n_ycls = bc.n_xcls = 1;
+    bc.ymask[0] = bc.xmask[0] = 0xFFFFFFFFu;
+    bc.ycls[0] = bc.xcls[0] = 0;
+  }
+  FoldedBias fb;
+  fb.ncls = bc.n_ycls * bc.n_xcls;
+  fb.n_xcls = bc.n_xcls;
+  const size_t bias_bytes = align_up(static_cast<size_t>(fb.ncls) * d->out_c * 4, 256);
+  const size_t need = bias_bytes + align_up(d->out_h, 256) + align_up(d->out_w, 256);
+  if (need > ws_bytes) return set_error(PSPML_ERR_OOM, "workspace too small for folded bias");
+  fb.bias_eff = reinterpret_cast<int32_t*>(ws);
+  fb.ycls = ws + bias_bytes;
+  fb.xcls = fb.ycls + align_up(d->out_h, 256);
+  if (fb.ncls > 1) {
+    int st = cuda_status(cudaMemcpyAsync(fb.ycls, bc.ycls, d->out_h, cudaMemcpyHostToDevice, s),
+                         "class table upload");
+    if (st) return st;
+    st = cuda_status(cudaMemcpyAsync(fb.xcls, bc.xcls, d->out_w, cudaMemcpyHostToDevice, s),
+                     "class table upload");
+    if (st) return st;
+  }
+  int st = cuda_status(launch_fold_bias(*d, filter, bias, bc, fb.bias_eff, s), "fold bias");
+  if (st) return st;
+  return cuda_status(launch_tc_gemm(*d, path, batch, in, filter, fb, mult, shift, out,
+                                    ctx->dev_err, ctx->num_sms, s),
+                     "tensor-core gemm");
+}
+
+int check_op_ptrs(const pspml_ctx* ctx, const void* in, const void* out, int64_t batch) {
+  if (ctx == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null context");
+  if (in == nullptr || out == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null tensor");
+  if (batch < 0) return set_error(PSPML_ERR_INVALID_ARG, "negative batch");
+  return PSPML_OK;
+}
+
+int check_weight_ptrs(const void* filter, const void* mult, const void* shift) {
+  if (filter == nullptr || mult == nullptr || shift == nullptr)
+    return set_error(PSPML_ERR_INVALID_ARG, "null filter / multiplier / shift");
+  return PSPML_OK;
+}
+
+}  // namespace pspml
+
+using namespace pspml;
+
+extern "C" {
+
+const char* pspml_last_error(void) { return g_last_error.c_str(); }
+
+int32_t pspml_abi_version(void) { return PSPML_ABI_VERSION; }
+
+int pspml_device_count(int* count) {
+  if (count == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null count");
+  *count = 0;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return PSPML_OK;
+  }
+  int ok = 0;
+  for (int i = 0; i < n; ++i) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, i) == cudaSuccess && p.major == 10 && p.minor == 0) ++ok;
+  }
+  *count = ok;
+  return PSPML_OK;
+}
+
+int pspml_ctx_create(int device, size_t workspace_bytes, pspml_ctx** out) {
+  clear_error();
+  if (out == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null output pointer");
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    cudaGetLastError();
+    return set_error(PSPML_ERR_NO_DEVICE, "no such CUDA device");
+  }
+  cudaDeviceProp prop;
+  int st = cuda_status(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (st) return st;
+  if (prop.major != 10 || prop.minor != 0)
+    return set_error(PSPML_ERR_NO_DEVICE, "device is not sm_100 (B200 class)");
+  st = cuda_status(cudaSetDevice(device), "cudaSetDevice");
+  if (st) return st;
+  auto* ctx = new pspml_ctx();
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  ctx->workspace_bytes = workspace_bytes ? workspace_bytes : (64u << 20);
+  st = cuda_status(cudaMalloc(&ctx->dev_err, 256), "cudaMalloc(error word)");
+  if (!st) st = cuda_status(cudaMemset(ctx->dev_err, 0, 256), "cudaMemset");
+  if (!st)
+    st = cuda_status(cudaMalloc(&ctx->workspace, ctx->workspace_bytes), "cudaMalloc(workspace)");
+  if (!st)
+    st = cuda_status(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking),
+                     "cudaStreamCreate");
+  if (st) {
+    pspml_ctx_destroy(ctx);
+    return st;
+  }
+  *out = ctx;
+  return PSPML_OK;
+}
+
+int pspml_ctx_destroy(pspml_ctx* ctx) {
+  if (ctx == nullptr) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->workspace) cudaFree(ctx->workspace);
+  if (ctx->dev_err) cudaFree(ctx->dev_err);
+  delete ctx;
+  return PSPML_OK;
+}
+
+int pspml_ctx_set_timeout_ms(pspml_ctx* ctx, int64_t timeout_ms) {
+  if (ctx == nullptr || timeout_ms < 0) return set_error(PSPML_ERR_INVALID_ARG, "bad argument");
+  ctx->timeout_ms = timeout_ms;
+  return PSPML_OK;
+}
+
+int pspml_ctx_check_device(pspml_ctx* ctx) {
+  if (ctx == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null context");
+  cudaSetDevice(ctx->device);
+  unsigned v = 0;
+  int st = cuda_status(cudaMemcpy(&v, ctx->dev_err, sizeof(v), cudaMemcpyDeviceToHost),
+                       "read device error word");
+  if (st) return st;
+  if (v != 0) {
+    cudaMemset(ctx->dev_err, 0, sizeof(unsigned));
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "a kernel gave up on a bounded wait (code %u)", v);
+    return set_error(PSPML_ERR_DEVICE_WAIT, buf);
+  }
+  return PSPML_OK;
+}
+
+int pspml_host_alloc(size_t bytes, void** out) {
+  if (out == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null output pointer");
+  *out = nullptr;
+  if (bytes == 0) return PSPML_OK;
+  return cuda_status(cudaMallocHost(out, bytes), "cudaMallocHost");
+}
+
+int pspml_host_free(void* p) {
+  if (p == nullptr) return PSPML_OK;
+  return cuda_status(cudaFreeHost(p), "cudaFreeHost");
+}
+
+int pspml_conv2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch, const int8_t* in,
+                    const int8_t* filter, const int32_t* bias, const int32_t* mult,
+                    const int32_t* shift, int8_t* out, void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_CONV2D) return set_error(PSPML_ERR_INVALID_ARG, "not a CONV2D op");
+  if ((st = check_op_ptrs(ctx, in, out, batch)) || (st = check_weight_ptrs(filter, mult, shift)))
+    return st;
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  GemmPath path = choose_conv_path(*d);
+  if (path != GemmPath::kDirect && !(aligned16(in) && aligned16(out) && aligned16(filter)))
+    path = GemmPath::kDirect;
+  if (path == GemmPath::kDirect)
+    return cuda_status(launch_conv_direct(*d, batch, in, filter, bias, mult, shift, out, s),
+                       "direct conv");
+  return run_tc_with_workspace(ctx, d, path, batch, in, filter, bias, mult, shift, out,
+                               ctx->workspace, ctx->workspace_bytes, s);
+}
+
+int pspml_depthwise_conv2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
+                              const int8_t* in, const int8_t* filter, const int32_t* bias,
+                              const int32_t* mult, const int32_t* shift, int8_t* out,
+                              void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_DEPTHWISE_CONV2D)
+    return set_error(PSPML_ERR_INVALID_ARG, "not a DEPTHWISE_CONV2D op");
+  if ((st = check_op_ptrs(ctx, in, out, batch)) || (st = check_weight_ptrs(filter, mult, shift)))
+    return st;
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  return cuda_status(launch_dwconv(*d, batch, in, filter, bias, mult, shift, out,
+                                   static_cast<cudaStream_t>(stream)),
+                     "depthwise conv");
+}
+
+int pspml_fully_connected_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
+                             const int8_t* in, const int8_t* filter, const int32_t* bias,
+                             const int32_t* mult, const int32_t* shift, int8_t* out,
+                             void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_FULLY_CONNECTED)
+    return set_error(PSPML_ERR_INVALID_ARG, "not a FULLY_CONNECTED op");
+  if ((st = check_op_ptrs(ctx, in, out, batch)) || (st = check_weight_ptrs(filter, mult, shift)))
+    return st;
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  GemmPath path = choose_fc_path(*d);
+  if (path == GemmPath::kTc2d && !(aligned16(in) && aligned16(filter))) path = GemmPath::kFcWarp;
+  if (path == GemmPath::kFcWarp)
+    return cuda_status(launch_fc_warp(*d, batch, in, filter, bias, mult, shift, out, s),
+                       "fully connected");
+  return run_tc_with_workspace(ctx, d, path, batch, in, filter, bias, mult, shift, out,
+                               ctx->workspace, ctx->workspace_bytes, s);
+}
+
+int pspml_max_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch, const int8_t* in,
+                        int8_t* out, void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_MAX_POOL2D) return set_error(PSPML_ERR_INVALID_ARG, "not MAX_POOL2D");
+  if ((st = check_op_ptrs(ctx, in, out, batch))) return st;
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  return cuda_status(launch_maxpool(*d, batch, in, out, static_cast<cudaStream_t>(stream)),
+                     "max pool");
+}
+
+int pspml_average_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
+                            const int8_t* in, int8_t* out, void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_AVERAGE_POOL2D)
+    return set_error(PSPML_ERR_INVALID_ARG, "not AVERAGE_POOL2D");
+  if ((st = check_op_ptrs(ctx, in, out, batch))) return st;
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  return cuda_status(launch_avgpool(*d, batch, in, out, static_cast<cudaStream_t>(stream)),
+                     "average pool");
+}
+
+}  // extern "C"

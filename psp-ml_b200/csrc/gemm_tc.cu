@@ -1,0 +1,623 @@
+// gemm_tc.cu - int8 GEMM / implicit-GEMM conv on the 5th-generation tensor
+// cores (tcgen05.mma kind::i8, int32 accumulators in tensor memory), with
+// TFLite per-channel requantisation fused into the epilogue.
+//
+// Replaces the reference's im2col_padded -> matmul_bt_tiled -> bias_add ->
+// relu chain (psp-ml/src/kernels/mod.rs:215-479) and its FC loop
+// (psp-ml/src/kernels/naive.rs:147-184) for int8 tensors.
+//
+// Operands (both K-major, int8):
+//   A  activations.  2D: [rows][K] (FC rows = samples, 1x1 conv rows = pixels)
+//                    4D: the NHWC input itself; for filter tap (ky,kx) the
+//                    A tile of 128 output pixels is one TMA box at the
+//                    shifted position.  Out-of-image taps are zero-filled
+//                    by TMA; the folded bias of the pixel's border class
+//                    corrects for the input zero point there.
+//   B  weights [N][taps*Kc] exactly as TFLite stores them ([Co][KH][KW][Ci]).
+//
+// Persistent kernel, one CTA per SM, 6 warps:
+//   warp 0      TMA producer (one thread), STAGES-deep smem ring
+//   warp 1      tensor-memory allocator + MMA issuer (one thread)
+//   warps 2..5  epilogue: tcgen05.ld -> requant -> int8 stores
+// Two accumulator buffers in tensor memory let the epilogue of one tile run
+// under the MMAs of the next.
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+
+#include "kernels.h"
+#include "ptx.cuh"
+#include "requant.cuh"
+
+namespace pspml {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
+
+struct TcGemmArgs {
+  int64_t tiles_total;
+  int32_t tiles_n;
+  int32_t kblocks;     // channel blocks per tap
+  int32_t taps, kw;    // filter taps, filter width
+  int32_t pad_t, pad_l;
+  int32_t conv4d;
+  int32_t bw_log2, bh_log2, bi;
+  int32_t tiles_x, tiles_y;
+  int64_t rows;        // 2D: number of A rows
+  int32_t N;
+  int32_t Wo, Ho;
+  int64_t nimg;
+  int32_t Kc;          // channels per tap (column stride of a tap in B)
+  int8_t* out;
+  int64_t ldo;
+  const int32_t* bias;
+  const uint8_t* ycls;
+  const uint8_t* xcls;
+  int32_t n_xcls;
+  const int32_t* mult;
+  const int32_t* shift;
+  int32_t zp_out, act_min, act_max;
+  unsigned* err;
+  int32_t stages;
+};
+
+template <int BK>
+struct SwizzleFor;
+template <>
+struct SwizzleFor<128> {
+  static constexpr uint32_t kLayout = 2;  // 128B swizzle
+};
+template <>
+struct SwizzleFor<64> {
+  static constexpr uint32_t kLayout = 4;  // 64B swizzle
+};
+template <>
+struct SwizzleFor<32> {
+  static constexpr uint32_t kLayout = 6;  // 32B swizzle
+};
+
+__device__ __forceinline__ void record_error(unsigned* err, volatile int* abort_flag,
+                                             unsigned code) {
+  *abort_flag = 1;
+  if (err != nullptr) atomicCAS(err, 0u, code);
+}
+
+// Output-pixel coordinates of tile tm (4D path).
+struct TileOrigin {
+  int32_t x0, y0;
+  int64_t n0;
+};
+__device__ __forceinline__ TileOrigin tile_origin(const TcGemmArgs& p, int64_t tm) {
+  const int64_t per_img = static_cast<int64_t>(p.tiles_x) * p.tiles_y;
+  const int64_t ti = tm / per_img;
+  const int32_t rem = static_cast<int32_t>(tm - ti * per_img);
+  const int32_t ty = rem / p.tiles_x;
+  const int32_t tx = rem - ty * p.tiles_x;
+  TileOrigin o;
+  o.x0 = tx << p.bw_log2;
+  o.y0 = ty << p.bh_log2;
+  o.n0 = ti * p.bi;
+  return o;
+}
+
+// Requantises 32 accumulators of one output row and stores them.
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int8_t* dst,
+                                               const int32_t* bias, const int32_t* mult,
+                                               const int32_t* shift, int cnt,
+                                               const ActParams& ap) {
+  // mult/shift chunks start 128 B apart from a 256 B-aligned base; the
+  // folded bias row of a border class is 16 B aligned only when N % 4 == 0.
+  if (cnt == 32 && (reinterpret_cast<uintptr_t>(bias) & 15u) == 0) {
+    uint32_t packed[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const int4 b4 = __ldg(reinterpret_cast<const int4*>(bias) + g);
+      const int4 m4 = __ldg(reinterpret_cast<const int4*>(mult) + g);
+      const int4 s4 = __ldg(reinterpret_cast<const int4*>(shift) + g);
+      const int32_t r0 = finish_dev(static_cast<int32_t>(v[4 * g + 0]) + b4.x, m4.x, s4.x, ap);
+      const int32_t r1 = finish_dev(static_cast<int32_t>(v[4 * g + 1]) + b4.y, m4.y, s4.y, ap);
+      const int32_t r2 = finish_dev(static_cast<int32_t>(v[4 * g + 2]) + b4.z, m4.z, s4.z, ap);
+      const int32_t r3 = finish_dev(static_cast<int32_t>(v[4 * g + 3]) + b4.w, m4.w, s4.w, ap);
+      packed[g] = pack4_s8(r0, r1, r2, r3);
+    }
+    if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    } else if ((reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
+      uint32_t* d1 = reinterpret_cast<uint32_t*>(dst);
+#pragma unroll
+      for (int g = 0; g < 8; ++g) d1[g] = packed[g];
+    } else {
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[4 * g + j] = static_cast<int8_t>(packed[g] >> (8 * j));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < cnt) {
+        const int32_t r =
+            finish_dev(static_cast<int32_t>(v[j]) + __ldg(bias + j), __ldg(mult + j),
+                       __ldg(shift + j), ap);
+        dst[j] = static_cast<int8_t>(r);
+      }
+    }
+  }
+}
+
+template <int BN, int BK>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_s8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const TcGemmArgs p) {
+  constexpr int A_BYTES = kBM * BK;
+  constexpr int B_BYTES = BN * BK;
+  constexpr uint32_t kLayout = SwizzleFor<BK>::kLayout;
+  constexpr uint32_t kSbo = 8 * BK;  // bytes between 8-row groups
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int stages = p.stages;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + stages * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * B_BYTES);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int kiters = p.taps * p.kblocks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+        const int32_t tn = static_cast<int32_t>(t % p.tiles_n);
+        const int64_t tm = t / p.tiles_n;
+        TileOrigin o{0, 0, 0};
+        if (p.conv4d) o = tile_origin(p, tm);
+        for (int tap = 0; tap < p.taps && ok; ++tap) {
+          const int ky = tap / p.kw;
+          const int kx = tap - ky * p.kw;
+          for (int kb = 0; kb < p.kblocks; ++kb) {
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+              record_error(p.err, abort_flag, kDevErrTmaWait);
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+            if (p.conv4d)
+              tma_load_4d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
+                          o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
+            else
+              tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK,
+                          static_cast<int32_t>(tm * kBM));
+            tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
+            ++issued;
+            if (++s == stages) {
+              s = 0;
+              ph ^= 1u;
+            }
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA's smem goes away.
+        const int64_t first = issued > stages ? issued - stages : 0;
+        for (int64_t g = first; g < issued; ++g)
+          mbar_wait(&full[g % stages], static_cast<uint32_t>((g / stages) & 1), nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_s8(kBM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag)) {
+          record_error(p.err, abort_flag, kDevErrMmaWait);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int it = 0; it < kiters; ++it) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            record_error(p.err, abort_flag, kDevErrMmaWait);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t ad = make_sdesc(a0 + kk * 32, 16, kSbo, kLayout);
+            const uint64_t bd = make_sdesc(b0 + kk * 32, 16, kSbo, kLayout);
+            umma_i8(d_tmem, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1u;
+      }
+      // All MMAs issued by this thread complete before tensor memory is freed.
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr);
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;  // tensor-memory lane quarter this warp may read
+    const int row = q * 32 + lane;
+    const ActParams ap{p.zp_out, p.act_min, p.act_max};
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int64_t t = blockIdx.x; t < p.tiles_total; t += gridDim.x) {
+      int ready = 0;
+      if (lane == 0) {
+        ready = mbar_wait(&tfull[acc], aph, abort_flag) ? 1 : 0;
+        if (!ready) record_error(p.err, abort_flag, kDevErrEpiWait);
+      }
+      ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
+      if (!ready) break;
+      tc_fence_after();
+
+      const int32_t tn = static_cast<int32_t>(t % p.tiles_n);
+      const int64_t tm = t / p.tiles_n;
+      bool valid;
+      int8_t* orow;
+      const int32_t* brow = p.bias;
+      if (p.conv4d) {
+        const TileOrigin o = tile_origin(p, tm);
+        const int32_t x = o.x0 + (row & ((1 << p.bw_log2) - 1));
+        const int32_t y = o.y0 + ((row >> p.bw_log2) & ((1 << p.bh_log2) - 1));
+        const int64_t n = o.n0 + (row >> (p.bw_log2 + p.bh_log2));
+        valid = x < p.Wo && y < p.Ho && n < p.nimg;
+        orow = p.out + ((n * p.Ho + y) * p.Wo + x) * static_cast<int64_t>(p.N);
+        if (valid && p.ycls != nullptr)
+          brow = p.bias + static_cast<int64_t>(p.ycls[y] * p.n_xcls + p.xcls[x]) * p.N;
+      } else {
+        const int64_t r = tm * kBM + row;
+        valid = r < p.rows;
+        orow = p.out + r * p.ldo;
+      }
+      const int32_t n0 = tn * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                      static_cast<uint32_t>(acc * BN + c),
+                  v);
+        const int32_t nc = n0 + c;
+        if (valid && nc < p.N) {
+          const int cnt = min(32, p.N - nc);
+          epilogue_chunk(v, orow + nc, brow + nc, p.mult + nc, p.shift + nc, cnt, ap);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ----------------------------------------------------------- bias folding
+struct FoldArgs {
+  int32_t N, taps, kw, Kc;
+  int32_t n_ycls, n_xcls;
+  int32_t zp_in;
+  uint32_t ymask[64];
+  uint32_t xmask[64];
+};
+
+// One warp per output channel: per-tap weight sums, then one folded bias
+// per border class.
+__global__ void k_fold_bias(const int8_t* __restrict__ filter, const int32_t* __restrict__ bias,
+                            int32_t* __restrict__ bias_eff, const FoldArgs a) {
+  __shared__ int32_t wsum_s[8][64];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + w;
+  if (n >= a.N) return;
+  int32_t* wsum = wsum_s[w];
+  const int8_t* fr = filter + static_cast<int64_t>(n) * a.taps * a.Kc;
+  for (int tap = 0; tap < a.taps; ++tap) {
+    int32_t s = 0;
+    for (int c = lane; c < a.Kc; c += 32) s += fr[static_cast<int64_t>(tap) * a.Kc + c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    if (lane == 0) wsum[tap] = s;
+  }
+  __syncwarp();
+  const int32_t b = bias != nullptr ? bias[n] : 0;
+  const int ncls = a.n_ycls * a.n_xcls;
+  for (int cls = lane; cls < ncls; cls += 32) {
+    const uint32_t ym = a.ymask[cls / a.n_xcls];
+    const uint32_t xm = a.xmask[cls % a.n_xcls];
+    int32_t s = 0;
+    for (int tap = 0; tap < a.taps; ++tap) {
+      const int ky = tap / a.kw, kx = tap - (tap / a.kw) * a.kw;
+      if (((ym >> ky) & 1u) && ((xm >> kx) & 1u)) s += wsum[tap];
+    }
+    bias_eff[static_cast<int64_t>(cls) * a.N + n] =
+        static_cast<int32_t>(static_cast<uint32_t>(b) -
+                             static_cast<uint32_t>(a.zp_in) * static_cast<uint32_t>(s));
+  }
+}
+
+int ilog2_exact(int v) {
+  int l = 0;
+  while ((1 << l) < v) ++l;
+  return l;
+}
+
+int pow2_ceil(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+template <int BN, int BK>
+cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args, int num_sms,
+                   cudaStream_t s) {
+  constexpr int stage_bytes = kBM * BK + BN * BK;
+  constexpr int overhead = 1024 + 64 * 8 + 64;
+  int stages = (kSmemLimit - overhead) / stage_bytes;
+  stages = std::min(stages, kMaxStages);
+  // At least 120 KB so that a second CTA never shares the SM: the grid is
+  // one persistent CTA per SM.
+  const int smem = std::max(overhead + stages * stage_bytes, 120 * 1024);
+  args.stages = stages;
+  static std::atomic<uint32_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint32_t bit = 1u << (dev & 31);
+  if ((attr_set.load() & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<BN, BK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  const int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
+  if (grid <= 0) return cudaSuccess;
+  k_gemm_s8<BN, BK><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(ma, mb, args);
+  return cudaGetLastError();
+}
+
+template <int BK>
+cudaError_t run_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+                      const TcGemmArgs& args, int num_sms, cudaStream_t s) {
+  switch (bn) {
+    case 32: return run_tc<32, BK>(ma, mb, args, num_sms, s);
+    case 64: return run_tc<64, BK>(ma, mb, args, num_sms, s);
+    case 128: return run_tc<128, BK>(ma, mb, args, num_sms, s);
+    default: return run_tc<256, BK>(ma, mb, args, num_sms, s);
+  }
+}
+
+}  // namespace
+
+bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc) {
+  const int kh = d.kernel_h, kw = d.kernel_w;
+  if (d.out_h > 4096 || d.out_w > 4096 || kh > 32 || kw > 32) return false;
+  auto classify = [](int out, int in, int k, int stride, int pad, uint32_t* masks, int* nmask,
+                     uint8_t* cls) {
+    *nmask = 0;
+    for (int o = 0; o < out; ++o) {
+      uint32_t m = 0;
+      for (int t = 0; t < k; ++t) {
+        const int i = o * stride + t - pad;
+        if (i >= 0 && i < in) m |= 1u << t;
+      }
+      int found = -1;
+      for (int j = 0; j < *nmask; ++j)
+        if (masks[j] == m) found = j;
+      if (found < 0) {
+        if (*nmask >= 64) return false;
+        masks[*nmask] = m;
+        found = (*nmask)++;
+      }
+      cls[o] = static_cast<uint8_t>(found);
+    }
+    return true;
+  };
+  if (!classify(d.out_h, d.in_h, kh, d.stride_h, d.pad_top, bc->ymask, &bc->n_ycls, bc->ycls))
+    return false;
+  if (!classify(d.out_w, d.in_w, kw, d.stride_w, d.pad_left, bc->xmask, &bc->n_xcls, bc->xcls))
+    return false;
+  return true;
+}
+
+cudaError_t launch_fold_bias(const pspml_op_desc& d, const int8_t* filter, const int32_t* bias,
+                             const BorderClasses& bc, int32_t* bias_eff, cudaStream_t s) {
+  FoldArgs a{};
+  a.N = d.out_c;
+  if (d.kind == PSPML_OP_FULLY_CONNECTED) {
+    a.taps = 1;
+    a.kw = 1;
+    a.Kc = d.in_h * d.in_w * d.in_c;
+    a.n_ycls = 1;
+    a.n_xcls = 1;
+    a.ymask[0] = 1;
+    a.xmask[0] = 1;
+  } else {
+    a.taps = d.kernel_h * d.kernel_w;
+    a.kw = d.kernel_w;
+    a.Kc = d.in_c;
+    a.n_ycls = bc.n_ycls;
+    a.n_xcls = bc.n_xcls;
+    for (int i = 0; i < 64; ++i) {
+      a.ymask[i] = bc.ymask[i];
+      a.xmask[i] = bc.xmask[i];
+    }
+  }
+  if (a.taps > 64) return cudaErrorInvalidValue;
+  a.zp_in = d.zp_in;
+  const int blocks = (a.N + 7) / 8;
+  k_fold_bias<<<blocks, 256, 0, s>>>(filter, bias, bias_eff, a);
+  return cudaGetLastError();
+}
+
+GemmPath choose_fc_path(const pspml_op_desc& d) {
+  const int64_t K = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
+  return (K % 16 == 0) ? GemmPath::kTc2d : GemmPath::kFcWarp;
+}
+
+GemmPath choose_conv_path(const pspml_op_desc& d) {
+  if (d.in_c % 16 != 0) return GemmPath::kDirect;
+  if (d.kernel_h == 1 && d.kernel_w == 1 && d.stride_h == 1 && d.stride_w == 1 &&
+      d.pad_top == 0 && d.pad_left == 0 && d.out_h == d.in_h && d.out_w == d.in_w)
+    return GemmPath::kTc2d;
+  if (d.stride_h == 1 && d.stride_w == 1 && d.kernel_h * d.kernel_w <= 64 &&
+      d.kernel_h <= 32 && d.kernel_w <= 32 && d.out_w <= 4096 && d.out_h <= 4096)
+    return GemmPath::kTc4d;
+  return GemmPath::kDirect;
+}
+
+cudaError_t launch_tc_gemm(const pspml_op_desc& d, GemmPath path, int64_t batch,
+                           const int8_t* in, const int8_t* filter, const FoldedBias& fb,
+                           const int32_t* mult, const int32_t* shift, int8_t* out,
+                           unsigned* dev_err, int num_sms, cudaStream_t s) {
+  const int N = d.out_c;
+  const bool is_fc = d.kind == PSPML_OP_FULLY_CONNECTED;
+  const int Kc = is_fc ? d.in_h * d.in_w * d.in_c : d.in_c;
+  const int taps = is_fc ? 1 : d.kernel_h * d.kernel_w;
+  const int bn = N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
+  const int bk = Kc >= 128 ? 128 : (Kc > 32 ? 64 : 32);
+
+  TcGemmArgs a{};
+  a.tiles_n = (N + bn - 1) / bn;
+  a.kblocks = (Kc + bk - 1) / bk;
+  a.taps = taps;
+  a.kw = is_fc ? 1 : d.kernel_w;
+  a.pad_t = is_fc ? 0 : d.pad_top;
+  a.pad_l = is_fc ? 0 : d.pad_left;
+  a.N = N;
+  a.Kc = Kc;
+  a.out = out;
+  a.bias = fb.bias_eff;
+  a.ycls = fb.ncls > 1 ? fb.ycls : nullptr;
+  a.xcls = fb.ncls > 1 ? fb.xcls : nullptr;
+  a.n_xcls = fb.n_xcls;
+  a.mult = mult;
+  a.shift = shift;
+  a.zp_out = d.zp_out;
+  a.act_min = d.act_min;
+  a.act_max = d.act_max;
+  a.err = dev_err;
+
+  const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUtensorMap ma, mb;
+  const uint32_t estr[4] = {1, 1, 1, 1};
+  if (path == GemmPath::kTc4d) {
+    const int bw = std::min(pow2_ceil(d.out_w), 128);
+    const int bh = std::min(pow2_ceil(d.out_h), 128 / bw);
+    const int bi = 128 / (bw * bh);
+    a.conv4d = 1;
+    a.bw_log2 = ilog2_exact(bw);
+    a.bh_log2 = ilog2_exact(bh);
+    a.bi = bi;
+    a.tiles_x = (d.out_w + bw - 1) / bw;
+    a.tiles_y = (d.out_h + bh - 1) / bh;
+    a.Wo = d.out_w;
+    a.Ho = d.out_h;
+    a.nimg = batch;
+    const int64_t tiles_img = (batch + bi - 1) / bi;
+    const int64_t tiles_m = tiles_img * a.tiles_x * a.tiles_y;
+    a.tiles_total = tiles_m * a.tiles_n;
+    const uint64_t dims[4] = {static_cast<uint64_t>(d.in_c), static_cast<uint64_t>(d.in_w),
+                              static_cast<uint64_t>(d.in_h), static_cast<uint64_t>(batch)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(d.in_c),
+                                 static_cast<uint64_t>(d.in_w) * d.in_c,
+                                 static_cast<uint64_t>(d.in_h) * d.in_w * d.in_c};
+    const uint32_t box[4] = {static_cast<uint32_t>(bk), static_cast<uint32_t>(bw),
+                             static_cast<uint32_t>(bh), static_cast<uint32_t>(bi)};
+    if (encode_tensor_map(&ma, in, 4, dims, strides, box, estr, swz) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  } else {
+    const int64_t rows = is_fc ? batch : batch * d.out_h * d.out_w;
+    if (rows >= (1ll << 31) - kBM) return cudaErrorInvalidValue;
+    a.conv4d = 0;
+    a.rows = rows;
+    a.ldo = N;
+    a.tiles_total = ((rows + kBM - 1) / kBM) * a.tiles_n;
+    const uint64_t dims[2] = {static_cast<uint64_t>(Kc), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(Kc)};
+    const uint32_t box[2] = {static_cast<uint32_t>(bk), static_cast<uint32_t>(kBM)};
+    if (encode_tensor_map(&ma, in, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(taps) * Kc, static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(taps) * Kc};
+    const uint32_t box[2] = {static_cast<uint32_t>(bk), static_cast<uint32_t>(bn)};
+    if (encode_tensor_map(&mb, filter, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  switch (bk) {
+    case 128: return run_tc_bn<128>(bn, ma, mb, a, num_sms, s);
+    case 64: return run_tc_bn<64>(bn, ma, mb, a, num_sms, s);
+    default: return run_tc_bn<32>(bn, ma, mb, a, num_sms, s);
+  }
+}
+
+}  // namespace pspml

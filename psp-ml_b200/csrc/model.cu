@@ -1,0 +1,507 @@
+// model.cu - compiled-model runtime: weight upload and preparation, the
+// liveness-planned activation arena, device-resident and host-buffer
+// forwards (micro-batched, copies overlapped with compute), the batch-sliced
+// multi-device forward and the per-op timed forward.
+//
+// Replaces the generated forward()/forward_timed() of the reference
+// (examples/mnist-bench/src/generated.rs:8-294, emitted by
+// cargo-psp-ml/src/codegen/render.rs:14-73,446-472), whose intermediates are
+// one static buffer each (render.rs:153-180).
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "kernels.h"
+#include "runtime.h"
+
+namespace pspml {
+
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int64_t in_elems_of(const pspml_op_desc& d) {
+  return static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
+}
+int64_t out_elems_of(const pspml_op_desc& d) {
+  return static_cast<int64_t>(d.out_h) * d.out_w * d.out_c;
+}
+
+bool has_weights(const pspml_op_desc& d) {
+  return d.kind == PSPML_OP_CONV2D || d.kind == PSPML_OP_DEPTHWISE_CONV2D ||
+         d.kind == PSPML_OP_FULLY_CONNECTED;
+}
+
+int64_t filter_bytes_of(const pspml_op_desc& d) {
+  switch (d.kind) {
+    case PSPML_OP_CONV2D:
+      return static_cast<int64_t>(d.out_c) * d.kernel_h * d.kernel_w * d.in_c;
+    case PSPML_OP_DEPTHWISE_CONV2D:
+      return static_cast<int64_t>(d.kernel_h) * d.kernel_w * d.in_c;
+    case PSPML_OP_FULLY_CONNECTED:
+      return static_cast<int64_t>(d.out_c) * in_elems_of(d);
+    default:
+      return 0;
+  }
+}
+
+int run_op(pspml_model* m, const ModelOp& op, int64_t mb, const int8_t* src, int8_t* dst,
+           cudaStream_t s) {
+  const pspml_op_desc& d = op.d;
+  pspml_ctx* ctx = m->ctx;
+  cudaError_t e = cudaSuccess;
+  switch (d.kind) {
+    case PSPML_OP_CONV2D:
+      if (op.path == GemmPath::kDirect)
+        e = launch_conv_direct(d, mb, src, op.filter, op.bias, op.mult, op.shift, dst, s);
+      else
+        e = launch_tc_gemm(d, op.path, mb, src, op.filter, op.fb, op.mult, op.shift, dst,
+                           ctx->dev_err, ctx->num_sms, s);
+      break;
+    case PSPML_OP_FULLY_CONNECTED:
+      if (op.path == GemmPath::kFcWarp)
+        e = launch_fc_warp(d, mb, src, op.filter, op.bias, op.mult, op.shift, dst, s);
+      else
+        e = launch_tc_gemm(d, op.path, mb, src, op.filter, op.fb, op.mult, op.shift, dst,
+                           ctx->dev_err, ctx->num_sms, s);
+      break;
+    case PSPML_OP_DEPTHWISE_CONV2D:
+      e = launch_dwconv(d, mb, src, op.filter, op.bias, op.mult, op.shift, dst, s);
+      break;
+    case PSPML_OP_MAX_POOL2D:
+      e = launch_maxpool(d, mb, src, dst, s);
+      break;
+    case PSPML_OP_AVERAGE_POOL2D:
+      e = launch_avgpool(d, mb, src, dst, s);
+      break;
+    case PSPML_OP_RESHAPE:
+      if (dst != src)
+        e = cudaMemcpyAsync(dst, src, static_cast<size_t>(mb * op.out_elems),
+                            cudaMemcpyDeviceToDevice, s);
+      break;
+    default:
+      return set_error(PSPML_ERR_INVALID_ARG, "unknown op kind");
+  }
+  return cuda_status(e, "op launch");
+}
+
+// Output pointer of every op for one micro-batch.
+void op_pointers(pspml_model* m, const int8_t* in, int8_t* out, std::vector<int8_t*>* ptrs) {
+  const int n = static_cast<int>(m->ops.size());
+  ptrs->resize(n);
+  // The last non-reshape op (and everything after it) writes the output.
+  int last_real = n - 1;
+  while (last_real > 0 && m->ops[last_real].d.kind == PSPML_OP_RESHAPE) --last_real;
+  for (int i = 0; i < n; ++i) {
+    const ModelOp& op = m->ops[i];
+    if (i >= last_real) {
+      (*ptrs)[i] = out;
+    } else if (op.alias_input) {
+      (*ptrs)[i] = i == 0 ? const_cast<int8_t*>(in) : (*ptrs)[i - 1];
+    } else {
+      (*ptrs)[i] = reinterpret_cast<int8_t*>(m->arena + op.out_off);
+    }
+  }
+}
+
+int forward_chunk(pspml_model* m, const int8_t* in, int8_t* out, int64_t mb, cudaStream_t s,
+                  std::vector<cudaEvent_t>* events) {
+  std::vector<int8_t*> ptrs;
+  op_pointers(m, in, out, &ptrs);
+  if (events) cudaEventRecord((*events)[0], s);
+  for (size_t i = 0; i < m->ops.size(); ++i) {
+    const int8_t* src = i == 0 ? in : ptrs[i - 1];
+    const int st = run_op(m, m->ops[i], mb, src, ptrs[i], s);
+    if (st) return st;
+    if (events) cudaEventRecord((*events)[i + 1], s);
+  }
+  return PSPML_OK;
+}
+
+int ensure_pipeline(pspml_model* m) {
+  if (m->s_comp != nullptr) return PSPML_OK;
+  const size_t in_b = static_cast<size_t>(m->max_micro) * m->in_elems;
+  const size_t out_b = static_cast<size_t>(m->max_micro) * m->out_elems;
+  int st = PSPML_OK;
+  for (int k = 0; k < 2 && !st; ++k) {
+    st = cuda_status(cudaMalloc(&m->stage_in[k], align_up(in_b, 256)), "cudaMalloc(stage)");
+    if (!st)
+      st = cuda_status(cudaMalloc(&m->stage_out[k], align_up(out_b, 256)), "cudaMalloc(stage)");
+    for (cudaEvent_t* e : {&m->ev_in_ready[k], &m->ev_in_free[k], &m->ev_out_ready[k],
+                           &m->ev_out_free[k]})
+      if (!st) st = cuda_status(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event");
+  }
+  if (!st) st = cuda_status(cudaEventCreateWithFlags(&m->ev_done, cudaEventDisableTiming), "event");
+  for (cudaStream_t* s : {&m->s_h2d, &m->s_comp, &m->s_d2h})
+    if (!st) st = cuda_status(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), "stream");
+  return st;
+}
+
+}  // namespace
+
+}  // namespace pspml
+
+using namespace pspml;
+
+extern "C" {
+
+int pspml_model_destroy(pspml_model* m) {
+  if (m == nullptr) return PSPML_OK;
+  cudaSetDevice(m->ctx->device);
+  if (m->s_comp) cudaStreamSynchronize(m->s_comp);
+  if (m->s_h2d) cudaStreamSynchronize(m->s_h2d);
+  if (m->s_d2h) cudaStreamSynchronize(m->s_d2h);
+  for (int k = 0; k < 2; ++k) {
+    if (m->stage_in[k]) cudaFree(m->stage_in[k]);
+    if (m->stage_out[k]) cudaFree(m->stage_out[k]);
+    for (cudaEvent_t e : {m->ev_in_ready[k], m->ev_in_free[k], m->ev_out_ready[k],
+                          m->ev_out_free[k]})
+      if (e) cudaEventDestroy(e);
+  }
+  if (m->ev_done) cudaEventDestroy(m->ev_done);
+  for (cudaEvent_t e : m->op_events) cudaEventDestroy(e);
+  for (cudaStream_t s : {m->s_h2d, m->s_comp, m->s_d2h})
+    if (s) cudaStreamDestroy(s);
+  if (m->arena) cudaFree(m->arena);
+  if (m->weights) cudaFree(m->weights);
+  delete m;
+  return PSPML_OK;
+}
+
+int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
+                       const void* blob, size_t blob_bytes, int32_t max_micro_batch,
+                       pspml_model** out) {
+  clear_error();
+  if (out == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null output pointer");
+  *out = nullptr;
+  if (ctx == nullptr || ops == nullptr || n_ops <= 0 || max_micro_batch <= 0)
+    return set_error(PSPML_ERR_INVALID_ARG, "bad model arguments");
+  if (blob == nullptr && blob_bytes > 0) return set_error(PSPML_ERR_INVALID_ARG, "null blob");
+  for (int i = 0; i < n_ops; ++i) {
+    int st = validate_desc(&ops[i]);
+    if (st) return set_error(st, "op " + std::to_string(i) + ": " + pspml_last_error());
+    if (i > 0 && in_elems_of(ops[i]) != out_elems_of(ops[i - 1]))
+      return set_error(PSPML_ERR_INVALID_ARG,
+                       "op " + std::to_string(i) + " input size != op " +
+                           std::to_string(i - 1) + " output size");
+    if (i > 0 && ops[i].zp_in != ops[i - 1].zp_out)
+      return set_error(PSPML_ERR_INVALID_ARG,
+                       "op " + std::to_string(i) + " zero point differs from its producer's");
+    if (has_weights(ops[i])) {
+      const pspml_op_desc& d = ops[i];
+      const int64_t fb = filter_bytes_of(d);
+      const int64_t nch = d.out_c;
+      const struct {
+        int64_t off, bytes;
+        bool required;
+        const char* name;
+      } t[4] = {{d.filter_off, fb, true, "filter"},
+                {d.bias_off, nch * 4, false, "bias"},
+                {d.mult_off, nch * 4, true, "mult"},
+                {d.shift_off, nch * 4, true, "shift"}};
+      for (const auto& x : t) {
+        if (x.off < 0) {
+          if (x.required)
+            return set_error(PSPML_ERR_INVALID_ARG,
+                             "op " + std::to_string(i) + ": missing " + x.name);
+          continue;
+        }
+        if (x.off % 16 != 0 || static_cast<uint64_t>(x.off + x.bytes) > blob_bytes)
+          return set_error(PSPML_ERR_INVALID_ARG, "op " + std::to_string(i) + ": " + x.name +
+                                                      " offset unaligned or outside the blob");
+      }
+    }
+  }
+  int st = cuda_status(cudaSetDevice(ctx->device), "cudaSetDevice");
+  if (st) return st;
+
+  auto* m = new pspml_model();
+  m->ctx = ctx;
+  m->max_micro = max_micro_batch;
+  m->in_elems = in_elems_of(ops[0]);
+  m->out_elems = out_elems_of(ops[n_ops - 1]);
+  m->ops.resize(n_ops);
+
+  // Tables for the tensor-core ops go after the blob.
+  std::vector<BorderClasses> classes(n_ops);
+  std::vector<size_t> table_off(n_ops, 0);
+  size_t wbytes = align_up(blob_bytes, 256);
+  for (int i = 0; i < n_ops; ++i) {
+    ModelOp& op = m->ops[i];
+    op.d = ops[i];
+    op.in_elems = in_elems_of(ops[i]);
+    op.out_elems = out_elems_of(ops[i]);
+    if (op.d.kind == PSPML_OP_CONV2D) op.path = choose_conv_path(op.d);
+    if (op.d.kind == PSPML_OP_FULLY_CONNECTED) op.path = choose_fc_path(op.d);
+    const bool tc = (op.d.kind == PSPML_OP_CONV2D || op.d.kind == PSPML_OP_FULLY_CONNECTED) &&
+                    (op.path == GemmPath::kTc2d || op.path == GemmPath::kTc4d);
+    if (!tc) continue;
+    BorderClasses& bc = classes[i];
+    if (op.path == GemmPath::kTc4d) {
+      if (!build_border_classes(op.d, &bc)) {
+        op.path = GemmPath::kDirect;
+        continue;
+      }
+    } else {
+      bc.n_ycls = bc.n_xcls = 1;
+      bc.ymask[0] = bc.xmask[0] = 0xFFFFFFFFu;
+    }
+    op.fb.ncls = bc.n_ycls * bc.n_xcls;
+    op.fb.n_xcls = bc.n_xcls;
+    table_off[i] = wbytes;
+    wbytes += align_up(static_cast<size_t>(op.fb.ncls) * op.d.out_c * 4, 256) +
+              align_up(op.d.out_h, 256) + align_up(op.d.out_w, 256);
+  }
+  st = cuda_status(cudaMalloc(&m->weights, wbytes), "cudaMalloc(weights)");
+  if (!st && blob_bytes > 0)
+    st = cuda_status(cudaMemcpy(m->weights, blob, blob_bytes, cudaMemcpyHostToDevice),
+                     "weight upload");
+  for (int i = 0; i < n_ops && !st; ++i) {
+    ModelOp& op = m->ops[i];
+    const pspml_op_desc& d = op.d;
+    if (has_weights(d)) {
+      op.filter = reinterpret_cast<int8_t*>(m->weights + d.filter_off);
+      op.bias = d.bias_off >= 0 ? reinterpret_cast<int32_t*>(m->weights + d.bias_off) : nullptr;
+      op.mult = reinterpret_cast<int32_t*>(m->weights + d.mult_off);
+      op.shift = reinterpret_cast<int32_t*>(m->weights + d.shift_off);
+    }
+    if (table_off[i] == 0) continue;
+    uint8_t* t = m->weights + table_off[i];
+    op.fb.bias_eff = reinterpret_cast<int32_t*>(t);
+    op.fb.ycls = t + align_up(static_cast<size_t>(op.fb.ncls) * d.out_c * 4, 256);
+    op.fb.xcls = op.fb.ycls + align_up(d.out_h, 256);
+    if (op.fb.ncls > 1) {
+      st = cuda_status(cudaMemcpy(op.fb.ycls, classes[i].ycls, d.out_h, cudaMemcpyHostToDevice),
+                       "class tables");
+      if (!st)
+        st = cuda_status(
+            cudaMemcpy(op.fb.xcls, classes[i].xcls, d.out_w, cudaMemcpyHostToDevice),
+            "class tables");
+    }
+    if (!st)
+      st = cuda_status(launch_fold_bias(d, op.filter, op.bias, classes[i], op.fb.bias_eff,
+                                        ctx->stream),
+                       "fold bias");
+  }
+  if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "model preparation");
+
+  // Arena: op i's output lives from op i until the last op reading it
+  // (reshapes alias their input, extending its life).  Greedy first fit by
+  // descending size over the time-overlapping buffers.
+  if (!st) {
+    int last_real = n_ops - 1;
+    while (last_real > 0 && m->ops[last_real].d.kind == PSPML_OP_RESHAPE) --last_real;
+    struct Buf {
+      int op;
+      int64_t bytes;
+      int def, last;
+      int64_t off;
+    };
+    std::vector<Buf> bufs;
+    for (int i = 0; i < last_real; ++i) {
+      ModelOp& op = m->ops[i];
+      if (op.d.kind == PSPML_OP_RESHAPE) {
+        op.alias_input = true;
+        continue;
+      }
+      int last = i + 1;
+      while (last < n_ops && m->ops[last].d.kind == PSPML_OP_RESHAPE) ++last;
+      bufs.push_back(Buf{i, static_cast<int64_t>(align_up(
+                                static_cast<size_t>(max_micro_batch) * op.out_elems, 256)),
+                         i, last, 0});
+    }
+    std::vector<int> order(bufs.size());
+    for (size_t k = 0; k < order.size(); ++k) order[k] = static_cast<int>(k);
+    std::sort(order.begin(), order.end(),
+              [&](int a, int b) { return bufs[a].bytes > bufs[b].bytes; });
+    std::vector<int> placed;
+    int64_t arena = 0;
+    for (int k : order) {
+      Buf& b = bufs[k];
+      int64_t off = 0;
+      bool moved = true;
+      while (moved) {
+        moved = false;
+        for (int j : placed) {
+          const Buf& o = bufs[j];
+          const bool live_overlap = !(o.last < b.def || b.last < o.def);
+          const bool mem_overlap = !(o.off + o.bytes <= off || off + b.bytes <= o.off);
+          if (live_overlap && mem_overlap) {
+            off = o.off + o.bytes;
+            moved = true;
+          }
+        }
+      }
+      b.off = off;
+      placed.push_back(k);
+      arena = std::max(arena, off + b.bytes);
+      m->ops[b.op].out_off = off;
+    }
+    m->arena_bytes = static_cast<size_t>(arena);
+    if (arena > 0) st = cuda_status(cudaMalloc(&m->arena, m->arena_bytes), "cudaMalloc(arena)");
+  }
+  if (st) {
+    pspml_model_destroy(m);
+    return st;
+  }
+  *out = m;
+  return PSPML_OK;
+}
+
+int pspml_model_info(const pspml_model* m, size_t* in_bytes_per_sample,
+                     size_t* out_bytes_per_sample, size_t* arena_bytes) {
+  if (m == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null model");
+  if (in_bytes_per_sample) *in_bytes_per_sample = static_cast<size_t>(m->in_elems);
+  if (out_bytes_per_sample) *out_bytes_per_sample = static_cast<size_t>(m->out_elems);
+  if (arena_bytes) *arena_bytes = m->arena_bytes;
+  return PSPML_OK;
+}
+
+int pspml_forward_device(pspml_model* m, const int8_t* dev_in, int8_t* dev_out, int64_t batch,
+                         void* stream) {
+  clear_error();
+  if (m == nullptr || dev_in == nullptr || dev_out == nullptr || batch < 0)
+    return set_error(PSPML_ERR_INVALID_ARG, "bad forward arguments");
+  std::lock_guard<std::mutex> lock(m->mu);
+  cudaSetDevice(m->ctx->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  for (int64_t b0 = 0; b0 < batch; b0 += m->max_micro) {
+    const int64_t mb = std::min<int64_t>(m->max_micro, batch - b0);
+    const int st = forward_chunk(m, dev_in + b0 * m->in_elems, dev_out + b0 * m->out_elems, mb,
+                                 s, nullptr);
+    if (st) return st;
+  }
+  return PSPML_OK;
+}
+
+int pspml_forward_timed(pspml_model* m, const int8_t* dev_in, int8_t* dev_out, int64_t batch,
+                        float* ms_per_op, void* stream) {
+  clear_error();
+  if (m == nullptr || dev_in == nullptr || dev_out == nullptr || ms_per_op == nullptr ||
+      batch <= 0 || batch > m->max_micro)
+    return set_error(PSPML_ERR_INVALID_ARG, "bad timed-forward arguments");
+  std::lock_guard<std::mutex> lock(m->mu);
+  cudaSetDevice(m->ctx->device);
+  const size_t n = m->ops.size();
+  while (m->op_events.size() < n + 1) {
+    cudaEvent_t e;
+    int st = cuda_status(cudaEventCreate(&e), "cudaEventCreate");
+    if (st) return st;
+    m->op_events.push_back(e);
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  int st = forward_chunk(m, dev_in, dev_out, batch, s, &m->op_events);
+  if (st) return st;
+  st = wait_event(m->ctx, m->op_events[n]);
+  if (st) return st;
+  for (size_t i = 0; i < n; ++i) {
+    float ms = 0.f;
+    st = cuda_status(cudaEventElapsedTime(&ms, m->op_events[i], m->op_events[i + 1]),
+                     "cudaEventElapsedTime");
+    if (st) return st;
+    ms_per_op[i] = ms;
+  }
+  return PSPML_OK;
+}
+
+int pspml_forward(pspml_model* m, const int8_t* host_in, int8_t* host_out, int64_t batch,
+                  pspml_timing* timing) {
+  clear_error();
+  if (m == nullptr || host_in == nullptr || host_out == nullptr || batch < 0)
+    return set_error(PSPML_ERR_INVALID_ARG, "bad forward arguments");
+  const auto t0 = std::chrono::steady_clock::now();
+  std::lock_guard<std::mutex> lock(m->mu);
+  int st = cuda_status(cudaSetDevice(m->ctx->device), "cudaSetDevice");
+  if (st) return st;
+  if ((st = ensure_pipeline(m))) return st;
+  const int64_t chunks = (batch + m->max_micro - 1) / m->max_micro;
+  // Three streams: H2D of chunk c+1 and D2H of chunk c-1 run under the
+  // compute of chunk c; two staging slots per direction.
+  for (int64_t c = 0; c < chunks && !st; ++c) {
+    const int k = static_cast<int>(c & 1);
+    const int64_t b0 = c * m->max_micro;
+    const int64_t mb = std::min<int64_t>(m->max_micro, batch - b0);
+    const size_t in_b = static_cast<size_t>(mb * m->in_elems);
+    const size_t out_b = static_cast<size_t>(mb * m->out_elems);
+    if (c >= 2) cudaStreamWaitEvent(m->s_h2d, m->ev_in_free[k], 0);
+    st = cuda_status(cudaMemcpyAsync(m->stage_in[k], host_in + b0 * m->in_elems, in_b,
+                                     cudaMemcpyHostToDevice, m->s_h2d),
+                     "H2D copy");
+    if (st) break;
+    cudaEventRecord(m->ev_in_ready[k], m->s_h2d);
+    cudaStreamWaitEvent(m->s_comp, m->ev_in_ready[k], 0);
+    if (c >= 2) cudaStreamWaitEvent(m->s_comp, m->ev_out_free[k], 0);
+    st = forward_chunk(m, reinterpret_cast<int8_t*>(m->stage_in[k]),
+                       reinterpret_cast<int8_t*>(m->stage_out[k]), mb, m->s_comp, nullptr);
+    if (st) break;
+    cudaEventRecord(m->ev_in_free[k], m->s_comp);
+    cudaEventRecord(m->ev_out_ready[k], m->s_comp);
+    cudaStreamWaitEvent(m->s_d2h, m->ev_out_ready[k], 0);
+    st = cuda_status(cudaMemcpyAsync(host_out + b0 * m->out_elems, m->stage_out[k], out_b,
+                                     cudaMemcpyDeviceToHost, m->s_d2h),
+                     "D2H copy");
+    if (st) break;
+    cudaEventRecord(m->ev_out_free[k], m->s_d2h);
+  }
+  cudaEventRecord(m->ev_done, m->s_d2h);
+  const int wst = wait_event(m->ctx, m->ev_done);
+  if (!st) st = wst;
+  if (!st) st = cuda_status(cudaGetLastError(), "forward");
+  if (timing) {
+    timing->total_ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    timing->h2d_bytes = static_cast<double>(batch) * m->in_elems;
+    timing->d2h_bytes = static_cast<double>(batch) * m->out_elems;
+    timing->micro_batches = static_cast<int32_t>(chunks);
+    timing->devices = 1;
+  }
+  return st;
+}
+
+int pspml_forward_sharded(pspml_model* const* models, int32_t n_models, const int8_t* host_in,
+                          int8_t* host_out, int64_t batch, pspml_timing* timing) {
+  clear_error();
+  if (models == nullptr || n_models <= 0 || host_in == nullptr || host_out == nullptr ||
+      batch < 0)
+    return set_error(PSPML_ERR_INVALID_ARG, "bad sharded-forward arguments");
+  for (int i = 0; i < n_models; ++i) {
+    if (models[i] == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null model");
+    if (models[i]->in_elems != models[0]->in_elems ||
+        models[i]->out_elems != models[0]->out_elems)
+      return set_error(PSPML_ERR_INVALID_ARG, "models disagree on input/output size");
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  const int64_t per = (batch + n_models - 1) / n_models;
+  std::vector<int> status(n_models, PSPML_OK);
+  std::vector<std::string> msgs(n_models);
+  std::vector<std::thread> threads;
+  for (int i = 0; i < n_models; ++i) {
+    const int64_t b0 = std::min<int64_t>(batch, i * per);
+    const int64_t cnt = std::min<int64_t>(per, batch - b0);
+    threads.emplace_back([&, i, b0, cnt] {
+      if (cnt <= 0) return;
+      pspml_model* m = models[i];
+      status[i] = pspml_forward(m, host_in + b0 * m->in_elems, host_out + b0 * m->out_elems,
+                                cnt, nullptr);
+      if (status[i]) msgs[i] = pspml_last_error();
+    });
+  }
+  for (auto& t : threads) t.join();
+  int st = PSPML_OK;
+  for (int i = 0; i < n_models && !st; ++i)
+    if (status[i]) st = set_error(status[i], "device " + std::to_string(i) + ": " + msgs[i]);
+  if (timing) {
+    timing->total_ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    timing->h2d_bytes = static_cast<double>(batch) * models[0]->in_elems;
+    timing->d2h_bytes = static_cast<double>(batch) * models[0]->out_elems;
+    timing->micro_batches = 0;
+    timing->devices = n_models;
+  }
+  return st;
+}
+
+}  // extern "C"

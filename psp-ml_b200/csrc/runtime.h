@@ -1,0 +1,76 @@
+// runtime.h - context and model objects behind the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/pspml.h"
+#include "kernels.h"
+
+struct pspml_ctx {
+  int device = 0;
+  int num_sms = 148;
+  int64_t timeout_ms = 0;
+  unsigned* dev_err = nullptr;      // device error word written by kernels
+  uint8_t* workspace = nullptr;     // per-op folded biases / class tables
+  size_t workspace_bytes = 0;
+  cudaStream_t stream = nullptr;    // internal stream for synchronous work
+};
+
+namespace pspml {
+
+// Thread-local error message plumbing.
+int set_error(int status, const std::string& msg);
+int cuda_status(cudaError_t e, const char* what);
+void clear_error();
+
+// Validates an op descriptor; returns PSPML_OK or an error (message set).
+int validate_desc(const pspml_op_desc* d);
+
+// Waits for `ev` honouring the context's watchdog.
+int wait_event(pspml_ctx* ctx, cudaEvent_t ev);
+
+// Folds the bias into `ws` and runs the tensor-core GEMM for a conv / FC.
+int run_tc_with_workspace(pspml_ctx* ctx, const pspml_op_desc* d, GemmPath path, int64_t batch,
+                          const int8_t* in, const int8_t* filter, const int32_t* bias,
+                          const int32_t* mult, const int32_t* shift, int8_t* out,
+                          uint8_t* ws, size_t ws_bytes, cudaStream_t s);
+
+// One prepared op of a model.
+struct ModelOp {
+  pspml_op_desc d{};
+  GemmPath path = GemmPath::kDirect;
+  int8_t* filter = nullptr;   // device copies (into the model's weight buffer)
+  int32_t* bias = nullptr;
+  int32_t* mult = nullptr;
+  int32_t* shift = nullptr;
+  FoldedBias fb;              // tensor-core paths only
+  int64_t out_off = 0;        // arena offset of the output (bytes per micro-batch)
+  int64_t out_elems = 0;      // per sample
+  int64_t in_elems = 0;
+  bool alias_input = false;   // reshape: output is the input buffer
+};
+
+}  // namespace pspml
+
+struct pspml_model {
+  pspml_ctx* ctx = nullptr;
+  std::vector<pspml::ModelOp> ops;
+  uint8_t* weights = nullptr;        // device: blob + folded tables
+  uint8_t* arena = nullptr;          // device: intermediates for one micro-batch
+  size_t arena_bytes = 0;
+  int32_t max_micro = 0;
+  int64_t in_elems = 0, out_elems = 0;
+  // host-buffer pipeline state (lazily allocated)
+  uint8_t* stage_in[2] = {nullptr, nullptr};
+  uint8_t* stage_out[2] = {nullptr, nullptr};
+  cudaStream_t s_h2d = nullptr, s_comp = nullptr, s_d2h = nullptr;
+  cudaEvent_t ev_in_ready[2] = {}, ev_in_free[2] = {}, ev_out_ready[2] = {}, ev_out_free[2] = {};
+  cudaEvent_t ev_done = nullptr;
+  std::vector<cudaEvent_t> op_events;
+  std::mutex mu;
+};

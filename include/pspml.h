@@ -208,8 +208,10 @@ int pspml_forward_sharded(pspml_model* const* models, int32_t n_models,
                           int64_t batch, pspml_timing* timing);
 
 /* Timed variant, replacing generated::forward_timed (generated.rs:139-294):
- * runs one device-resident forward of `batch` (<= max_micro_batch) and
- * stores each op's device time in ms_per_op[n_ops]. */
+ * a device-resident forward of `batch` samples (micro-batched like
+ * pspml_forward_device) with CUDA events around every op; stores each op's
+ * device time, summed over the micro-batches, in ms_per_op[n_ops].  Returns
+ * when the work is done. */
 int pspml_forward_timed(pspml_model* m, const int8_t* dev_in, int8_t* dev_out,
                         int64_t batch, float* ms_per_op, void* stream);
 

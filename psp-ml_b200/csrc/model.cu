@@ -381,29 +381,43 @@ int pspml_forward_timed(pspml_model* m, const int8_t* dev_in, int8_t* dev_out, i
                         float* ms_per_op, void* stream) {
   clear_error();
   if (m == nullptr || dev_in == nullptr || dev_out == nullptr || ms_per_op == nullptr ||
-      batch <= 0 || batch > m->max_micro)
+      batch <= 0)
     return set_error(PSPML_ERR_INVALID_ARG, "bad timed-forward arguments");
   std::lock_guard<std::mutex> lock(m->mu);
   cudaSetDevice(m->ctx->device);
   const size_t n = m->ops.size();
-  while (m->op_events.size() < n + 1) {
+  const int64_t chunks = (batch + m->max_micro - 1) / m->max_micro;
+  const size_t need = static_cast<size_t>(chunks) * (n + 1);
+  while (m->op_events.size() < need) {
     cudaEvent_t e;
     int st = cuda_status(cudaEventCreate(&e), "cudaEventCreate");
     if (st) return st;
     m->op_events.push_back(e);
   }
   auto s = static_cast<cudaStream_t>(stream);
-  int st = forward_chunk(m, dev_in, dev_out, batch, s, &m->op_events);
-  if (st) return st;
-  st = wait_event(m->ctx, m->op_events[n]);
-  if (st) return st;
-  for (size_t i = 0; i < n; ++i) {
-    float ms = 0.f;
-    st = cuda_status(cudaEventElapsedTime(&ms, m->op_events[i], m->op_events[i + 1]),
-                     "cudaEventElapsedTime");
+  // Events bracket every op of every micro-batch; nothing waits on the host
+  // until the last one, so the timed work runs as in pspml_forward_device.
+  for (int64_t c = 0; c < chunks; ++c) {
+    const int64_t b0 = c * m->max_micro;
+    const int64_t mb = std::min<int64_t>(m->max_micro, batch - b0);
+    std::vector<cudaEvent_t> ev(m->op_events.begin() + c * (n + 1),
+                                m->op_events.begin() + (c + 1) * (n + 1));
+    const int st = forward_chunk(m, dev_in + b0 * m->in_elems, dev_out + b0 * m->out_elems, mb,
+                                 s, &ev);
     if (st) return st;
-    ms_per_op[i] = ms;
   }
+  int st = wait_event(m->ctx, m->op_events[need - 1]);
+  if (st) return st;
+  for (size_t i = 0; i < n; ++i) ms_per_op[i] = 0.f;
+  for (int64_t c = 0; c < chunks; ++c)
+    for (size_t i = 0; i < n; ++i) {
+      float ms = 0.f;
+      st = cuda_status(cudaEventElapsedTime(&ms, m->op_events[c * (n + 1) + i],
+                                            m->op_events[c * (n + 1) + i + 1]),
+                       "cudaEventElapsedTime");
+      if (st) return st;
+      ms_per_op[i] += ms;
+    }
   return PSPML_OK;
 }
 

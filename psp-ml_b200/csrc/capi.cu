@@ -17,8 +17,6 @@ namespace pspml {
 namespace {
 thread_local std::string g_last_error;
 
-size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
@@ -128,43 +126,26 @@ CUresult encode_tensor_map(CUtensorMap* map, const void* base, int rank, const u
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-// Runs a conv or FC through the tensor-core path using `ws` for the folded
-// bias and border-class tables.
-int run_tc_with_workspace(pspml_ctx* ctx, const pspml_op_desc* d, GemmPath path, int64_t batch,
-                          const int8_t* in, const int8_t* filter, const int32_t* bias,
-                          const int32_t* mult, const int32_t* shift, int8_t* out,
-                          uint8_t* ws, size_t ws_bytes, cudaStream_t s) {
-  static thread_local BorderClasses bc;
-  if (path == GemmPath::kTc4d) {
-    if (!build_border_classes(*d, &bc))
-      return set_error(PSPML_ERR_UNSUPPORTED, "too many border classes");
-  } else {
-    bc.n_ycls = bc.n_xcls = 1;
-    bc.ymask[0] = bc.xmask[0] = 0xFFFFFFFFu;
-    bc.ycls[0] = bc.xcls[0] = 0;
+// Stateless op call: prepares the op's derived tables in the context
+// workspace (ordered on `s` before the op itself) and launches it.
+int run_op_stateless(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch, const int8_t* in,
+                     const int8_t* filter, const int32_t* bias, const int32_t* mult,
+                     const int32_t* shift, int8_t* out, cudaStream_t s) {
+  const bool al = aligned16(in) && aligned16(out) && (filter == nullptr || aligned16(filter));
+  OpPath path = choose_path(*d, al);
+  size_t need = prepared_bytes(*d, path);
+  if (path == OpPath::kTc4d && need == 0) {  // too many border classes for the tables
+    path = OpPath::kDirect;
+    need = prepared_bytes(*d, path);
   }
-  FoldedBias fb;
-  fb.ncls = bc.n_ycls * bc.n_xcls;
-  fb.n_xcls = bc.n_xcls;
-  const size_t bias_bytes = align_up(static_cast<size_t>(fb.ncls) * d->out_c * 4, 256);
-  const size_t need = bias_bytes + align_up(d->out_h, 256) + align_up(d->out_w, 256);
-  if (need > ws_bytes) return set_error(PSPML_ERR_OOM, "workspace too small for folded bias");
-  fb.bias_eff = reinterpret_cast<int32_t*>(ws);
-  fb.ycls = ws + bias_bytes;
-  fb.xcls = fb.ycls + align_up(d->out_h, 256);
-  if (fb.ncls > 1) {
-    int st = cuda_status(cudaMemcpyAsync(fb.ycls, bc.ycls, d->out_h, cudaMemcpyHostToDevice, s),
-                         "class table upload");
-    if (st) return st;
-    st = cuda_status(cudaMemcpyAsync(fb.xcls, bc.xcls, d->out_w, cudaMemcpyHostToDevice, s),
-                     "class table upload");
-    if (st) return st;
-  }
-  int st = cuda_status(launch_fold_bias(*d, filter, bias, bc, fb.bias_eff, s), "fold bias");
+  if (need > ctx->workspace_bytes)
+    return set_error(PSPML_ERR_OOM, "context workspace too small for this op's tables");
+  PreparedOp p;
+  int st = cuda_status(prepare_op(*d, path, filter, bias, mult, shift, ctx->workspace, &p, s),
+                       "op preparation");
   if (st) return st;
-  return cuda_status(launch_tc_gemm(*d, path, batch, in, filter, fb, mult, shift, out,
-                                    ctx->dev_err, ctx->num_sms, s),
-                     "tensor-core gemm");
+  return cuda_status(launch_op(*d, p, batch, in, out, ctx->dev_err, ctx->num_sms, s),
+                     "op launch");
 }
 
 int check_op_ptrs(const pspml_ctx* ctx, const void* in, const void* out, int64_t batch) {
@@ -297,15 +278,8 @@ int pspml_conv2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch, const
     return st;
   if (batch == 0) return PSPML_OK;
   cudaSetDevice(ctx->device);
-  auto s = static_cast<cudaStream_t>(stream);
-  GemmPath path = choose_conv_path(*d);
-  if (path != GemmPath::kDirect && !(aligned16(in) && aligned16(out) && aligned16(filter)))
-    path = GemmPath::kDirect;
-  if (path == GemmPath::kDirect)
-    return cuda_status(launch_conv_direct(*d, batch, in, filter, bias, mult, shift, out, s),
-                       "direct conv");
-  return run_tc_with_workspace(ctx, d, path, batch, in, filter, bias, mult, shift, out,
-                               ctx->workspace, ctx->workspace_bytes, s);
+  return run_op_stateless(ctx, d, batch, in, filter, bias, mult, shift, out,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int pspml_depthwise_conv2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
@@ -321,9 +295,8 @@ int pspml_depthwise_conv2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t ba
     return st;
   if (batch == 0) return PSPML_OK;
   cudaSetDevice(ctx->device);
-  return cuda_status(launch_dwconv(*d, batch, in, filter, bias, mult, shift, out,
-                                   static_cast<cudaStream_t>(stream)),
-                     "depthwise conv");
+  return run_op_stateless(ctx, d, batch, in, filter, bias, mult, shift, out,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int pspml_fully_connected_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
@@ -339,14 +312,8 @@ int pspml_fully_connected_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t bat
     return st;
   if (batch == 0) return PSPML_OK;
   cudaSetDevice(ctx->device);
-  auto s = static_cast<cudaStream_t>(stream);
-  GemmPath path = choose_fc_path(*d);
-  if (path == GemmPath::kTc2d && !(aligned16(in) && aligned16(filter))) path = GemmPath::kFcWarp;
-  if (path == GemmPath::kFcWarp)
-    return cuda_status(launch_fc_warp(*d, batch, in, filter, bias, mult, shift, out, s),
-                       "fully connected");
-  return run_tc_with_workspace(ctx, d, path, batch, in, filter, bias, mult, shift, out,
-                               ctx->workspace, ctx->workspace_bytes, s);
+  return run_op_stateless(ctx, d, batch, in, filter, bias, mult, shift, out,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int pspml_max_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch, const int8_t* in,

@@ -1,7 +1,15 @@
-// cuda_core.cu - int8 kernels that run on the CUDA cores: depthwise conv,
-// direct conv for channel counts the tensor-core path does not take, a
-// warp-per-output FC, and max / average pooling.  All are NHWC with the
-// TFLite requantisation fused in.
+// cuda_core.cu - int8 kernels on the CUDA cores, NHWC, with the TFLite
+// requantisation fused in:
+//   k_dw3x3_s8       depthwise 3x3 (stride 1/2), dp4a with byte-masked weights
+//   k_small_conv_s8  conv with few input channels (K <= 128) over packed patches
+//   k_conv_direct_s8 any conv (fallback)
+//   k_dw_generic_s8  any depthwise conv (fallback)
+//   k_fc_warp_s8     FC with K % 16 != 0 (one warp per output)
+//   k_maxpool_s8 / k_avgpool_s8
+//
+// The dp4a kernels accumulate sum(x * w) with out-of-image taps filled with
+// the input zero point; the folded bias (bias - zp_in * sum(w)) makes that
+// exactly TFLite's sum((x - zp_in) * w) + bias.
 #include <algorithm>
 
 #include "kernels.h"
@@ -12,11 +20,13 @@ namespace pspml {
 namespace {
 
 constexpr int kBlock = 256;
+constexpr int kMaxGridZ = 65535;
 
 struct Geom {
   int32_t H, W, C, Ho, Wo, Co, KH, KW, sh, sw, pt, pl;
   int32_t zp_in;
-  ActParams ap;
+  uint32_t lo4, hi4;
+  int32_t clamp;
 };
 
 Geom geom_of(const pspml_op_desc& d) {
@@ -34,7 +44,9 @@ Geom geom_of(const pspml_op_desc& d) {
   g.pt = d.pad_top;
   g.pl = d.pad_left;
   g.zp_in = d.zp_in;
-  g.ap = ActParams{d.zp_out, d.act_min, d.act_max};
+  g.lo4 = splat4(d.act_min);
+  g.hi4 = splat4(d.act_max);
+  g.clamp = (d.act_min > -128 || d.act_max < 127) ? 1 : 0;
   return g;
 }
 
@@ -42,80 +54,199 @@ unsigned grid_for(int64_t n) {
   return static_cast<unsigned>(std::max<int64_t>(1, (n + kBlock - 1) / kBlock));
 }
 
-// ----------------------------------------------------------- depthwise conv
-// One thread per (sample, oy, ox, VEC channels).  Out-of-image taps are
-// skipped (TFLite: padding is the real value zero).  filter [KH][KW][C].
-template <int VEC>
-__global__ void k_dwconv_s8(const int8_t* __restrict__ in, const int8_t* __restrict__ f,
-                            const int32_t* __restrict__ bias, const int32_t* __restrict__ mult,
-                            const int32_t* __restrict__ shift, int8_t* __restrict__ out,
-                            const Geom g, int64_t total) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= total) return;
-  const int cv = g.C / VEC;
-  const int c0 = static_cast<int>(idx % cv) * VEC;
-  const int64_t pix = idx / cv;
-  const int ox = static_cast<int>(pix % g.Wo);
-  const int oy = static_cast<int>((pix / g.Wo) % g.Ho);
-  const int64_t n = pix / (static_cast<int64_t>(g.Wo) * g.Ho);
-  int32_t acc[VEC];
+__device__ __forceinline__ uint32_t finish4(int32_t a0, int32_t a1, int32_t a2, int32_t a3,
+                                            const int4& b, const RqChannel& q0,
+                                            const RqChannel& q1, const RqChannel& q2,
+                                            const RqChannel& q3, const Geom& g) {
+  uint32_t w = pack_sat4(rq_apply(a0 + b.x, q0), rq_apply(a1 + b.y, q1), rq_apply(a2 + b.z, q2),
+                         rq_apply(a3 + b.w, q3));
+  if (g.clamp) w = clamp4(w, g.lo4, g.hi4);
+  return w;
+}
+
+__device__ __forceinline__ int8_t finish1(int32_t a, const RqChannel& q, const Geom& g) {
+  int32_t r = rq_apply(a, q);
+  r = max(r, -128);
+  r = min(r, 127);
+  uint32_t w = static_cast<uint32_t>(r) & 0xFFu;
+  if (g.clamp) w = clamp4(w * 0x01010101u, g.lo4, g.hi4) & 0xFFu;
+  return static_cast<int8_t>(w);
+}
+
+// ------------------------------------------------------ depthwise 3x3 (dp4a)
+// Thread: 4 channels (one word) x PX consecutive output pixels of one row.
+// Block: 128 threads over (pixel group, channel word) pairs of one output
+// row (blockIdx.y) of one image (blockIdx.z + n_base).  Weights [9][C].
+template <int S, int PX>
+__global__ void __launch_bounds__(128)
+    k_dw3x3_s8(const uint32_t* __restrict__ in, const uint32_t* __restrict__ f,
+               const int32_t* __restrict__ bias_eff, const RqChannel* __restrict__ rq,
+               uint32_t* __restrict__ out, const Geom g, int64_t n_base) {
+  constexpr int NIN = (PX - 1) * S + 3;
+  const int cwn = g.C >> 2;
+  const int pair = blockIdx.x * 128 + threadIdx.x;
+  const int groups = (g.Wo + PX - 1) / PX;
+  if (pair >= groups * cwn) return;
+  const int cw = pair % cwn;
+  const int pg = pair / cwn;
+  const int oy = blockIdx.y;
+  const int64_t n = n_base + blockIdx.z;
+  const int ox0 = pg * PX;
+
+  uint32_t wm[9][4];
 #pragma unroll
-  for (int j = 0; j < VEC; ++j) acc[j] = bias != nullptr ? __ldg(bias + c0 + j) : 0;
-  const int iy0 = oy * g.sh - g.pt, ix0 = ox * g.sw - g.pl;
-  const int8_t* img = in + n * g.H * g.W * static_cast<int64_t>(g.C);
-  for (int ky = 0; ky < g.KH; ++ky) {
-    const int iy = iy0 + ky;
-    if (iy < 0 || iy >= g.H) continue;
-    for (int kx = 0; kx < g.KW; ++kx) {
-      const int ix = ix0 + kx;
-      if (ix < 0 || ix >= g.W) continue;
-      const int8_t* xp = img + (static_cast<int64_t>(iy) * g.W + ix) * g.C + c0;
-      const int8_t* wp = f + (ky * g.KW + kx) * g.C + c0;
-      if constexpr (VEC == 16) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xp));
-        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wp));
-        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
-        const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  for (int t = 0; t < 9; ++t) {
+    const uint32_t w = __ldg(f + t * cwn + cw);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+    for (int j = 0; j < 4; ++j) wm[t][j] = w & (0xFFu << (8 * j));
+  }
+  int32_t acc[PX][4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            acc[4 * q + j] += (sbyte(xs[q], j) - g.zp_in) * sbyte(ws[q], j);
-      } else if constexpr (VEC == 4) {
-        const uint32_t xv = __ldg(reinterpret_cast<const uint32_t*>(xp));
-        const uint32_t wv = __ldg(reinterpret_cast<const uint32_t*>(wp));
+  for (int p = 0; p < PX; ++p)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] += (sbyte(xv, j) - g.zp_in) * sbyte(wv, j);
+    for (int j = 0; j < 4; ++j) acc[p][j] = 0;
+
+  const uint32_t zpw = splat4(g.zp_in);
+  const int ix0 = ox0 * S - g.pl;
+  const uint32_t* img = in + n * static_cast<int64_t>(g.H) * g.W * cwn + cw;
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky) {
+    const int iy = oy * S - g.pt + ky;
+    const bool row_ok = iy >= 0 && iy < g.H;
+    const uint32_t* rowp = img + static_cast<int64_t>(row_ok ? iy : 0) * g.W * cwn;
+    uint32_t x[NIN];
+#pragma unroll
+    for (int c = 0; c < NIN; ++c) {
+      const int ix = ix0 + c;
+      x[c] = (row_ok && ix >= 0 && ix < g.W) ? __ldg(rowp + ix * cwn) : zpw;
+    }
+#pragma unroll
+    for (int p = 0; p < PX; ++p)
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          acc[p][j] = __dp4a(static_cast<int>(x[p * S + kx]), static_cast<int>(wm[ky * 3 + kx][j]),
+                             acc[p][j]);
+  }
+
+  const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff) + cw);
+  const RqChannel q0 = load_rq(rq + 4 * cw), q1 = load_rq(rq + 4 * cw + 1),
+                  q2 = load_rq(rq + 4 * cw + 2), q3 = load_rq(rq + 4 * cw + 3);
+  uint32_t* orow = out + ((n * g.Ho + oy) * static_cast<int64_t>(g.Wo)) * cwn + cw;
+#pragma unroll
+  for (int p = 0; p < PX; ++p)
+    if (ox0 + p < g.Wo)
+      orow[static_cast<int64_t>(ox0 + p) * cwn] =
+          finish4(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
+}
+
+// --------------------------------------------------- small-channel conv (dp4a)
+// Thread: one output pixel x COB output channels (blockIdx.y picks the chunk).
+// The KHxKWxCI patch is packed into NW words in TFLite filter order
+// (ky, kx, ci); out-of-image taps hold the input zero point.  Weights of the
+// chunk sit in shared memory as [COB][NW] words (16-byte rows).
+template <int KH, int KW, int CI, int COB>
+__global__ void __launch_bounds__(128)
+    k_small_conv_s8(const int8_t* __restrict__ in, const uint32_t* __restrict__ wpack,
+                    int32_t nw_stride, const int32_t* __restrict__ bias_eff,
+                    const RqChannel* __restrict__ rq, int8_t* __restrict__ out, const Geom g,
+                    int64_t n_base) {
+  constexpr int K = KH * KW * CI;
+  constexpr int NW = (K + 3) / 4;
+  constexpr int NW4 = (NW + 3) / 4;
+  __shared__ uint4 sw[COB][NW4];
+  const int co0 = blockIdx.y * COB;
+  for (int i = threadIdx.x; i < COB * NW4; i += blockDim.x) {
+    const int co = i / NW4, w4 = i - (i / NW4) * NW4;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (co0 + co < g.Co)
+      v = __ldg(reinterpret_cast<const uint4*>(wpack + static_cast<int64_t>(co0 + co) * nw_stride) +
+                w4);
+    sw[co][w4] = v;
+  }
+  __syncthreads();
+  const int pix = blockIdx.x * 128 + threadIdx.x;
+  if (pix >= g.Ho * g.Wo) return;
+  const int oy = pix / g.Wo, ox = pix - (pix / g.Wo) * g.Wo;
+  const int64_t n = n_base + blockIdx.z;
+  const int8_t* img = in + n * static_cast<int64_t>(g.H) * g.W * CI;
+
+  uint32_t x[NW4 * 4];
+#pragma unroll
+  for (int i = 0; i < NW4 * 4; ++i) x[i] = 0;
+  const uint32_t zpb = static_cast<uint32_t>(g.zp_in) & 0xFFu;
+#pragma unroll
+  for (int ky = 0; ky < KH; ++ky) {
+    const int iy = oy * g.sh - g.pt + ky;
+#pragma unroll
+    for (int kx = 0; kx < KW; ++kx) {
+      const int ix = ox * g.sw - g.pl + kx;
+      const bool ok = iy >= 0 && iy < g.H && ix >= 0 && ix < g.W;
+      const int8_t* px = img + (static_cast<int64_t>(ok ? iy : 0) * g.W + (ok ? ix : 0)) * CI;
+      if constexpr (CI % 4 == 0) {
+#pragma unroll
+        for (int c4 = 0; c4 < CI / 4; ++c4) {
+          const uint32_t v = ok ? __ldg(reinterpret_cast<const uint32_t*>(px) + c4)
+                                : zpb * 0x01010101u;
+          x[((ky * KW + kx) * CI) / 4 + c4] = v;
+        }
       } else {
-        acc[0] += (static_cast<int32_t>(xp[0]) - g.zp_in) * static_cast<int32_t>(wp[0]);
+#pragma unroll
+        for (int ci = 0; ci < CI; ++ci) {
+          const int k = (ky * KW + kx) * CI + ci;
+          const uint32_t b = ok ? static_cast<uint32_t>(static_cast<uint8_t>(__ldg(px + ci))) : zpb;
+          x[k >> 2] |= b << (8 * (k & 3));
+        }
       }
     }
   }
-  int8_t* op = out + pix * g.C + c0;
-  int32_t r[VEC];
+
+  const int cnt = min(COB, g.Co - co0);
+  int8_t* op = out + ((n * g.Ho + oy) * static_cast<int64_t>(g.Wo) + ox) * g.Co + co0;
+  const bool vec = (g.Co % 4 == 0) && cnt == COB &&
+                   (reinterpret_cast<uintptr_t>(op) & 3u) == 0;
 #pragma unroll
-  for (int j = 0; j < VEC; ++j)
-    r[j] = finish_dev(acc[j], __ldg(mult + c0 + j), __ldg(shift + c0 + j), g.ap);
-  if constexpr (VEC == 16) {
-    *reinterpret_cast<uint4*>(op) =
-        make_uint4(pack4_s8(r[0], r[1], r[2], r[3]), pack4_s8(r[4], r[5], r[6], r[7]),
-                   pack4_s8(r[8], r[9], r[10], r[11]), pack4_s8(r[12], r[13], r[14], r[15]));
-  } else if constexpr (VEC == 4) {
-    *reinterpret_cast<uint32_t*>(op) = pack4_s8(r[0], r[1], r[2], r[3]);
-  } else {
-    op[0] = static_cast<int8_t>(r[0]);
+  for (int c4 = 0; c4 < COB / 4; ++c4) {
+    int32_t a[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int co = c4 * 4 + j;
+      int32_t s = 0;
+#pragma unroll
+      for (int w4 = 0; w4 < NW4; ++w4) {
+        const uint4 wv = sw[co][w4];
+        s = __dp4a(static_cast<int>(x[4 * w4 + 0]), static_cast<int>(wv.x), s);
+        s = __dp4a(static_cast<int>(x[4 * w4 + 1]), static_cast<int>(wv.y), s);
+        s = __dp4a(static_cast<int>(x[4 * w4 + 2]), static_cast<int>(wv.z), s);
+        s = __dp4a(static_cast<int>(x[4 * w4 + 3]), static_cast<int>(wv.w), s);
+      }
+      a[j] = s;
+    }
+    if (vec) {
+      const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff + co0) + c4);
+      const int cb = co0 + 4 * c4;
+      reinterpret_cast<uint32_t*>(op)[c4] =
+          finish4(a[0], a[1], a[2], a[3], b, load_rq(rq + cb), load_rq(rq + cb + 1),
+                  load_rq(rq + cb + 2), load_rq(rq + cb + 3), g);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int co = c4 * 4 + j;
+        if (co < cnt)
+          op[co] = finish1(a[j] + __ldg(bias_eff + co0 + co), load_rq(rq + co0 + co), g);
+      }
+    }
   }
 }
 
 // ------------------------------------------------------------- direct conv
-// One thread per (sample, oy, ox) and COB output channels (blockIdx.y picks
-// the channel chunk).  The chunk's weights sit in shared memory as int32
-// [K][COB] so the inner loop is a broadcast load and COB multiply-adds.
+// Fallback for any conv: one thread per (sample, oy, ox) and COB output
+// channels; weights of the chunk in shared memory as int32 [K][COB].
 template <int COB>
 __global__ void k_conv_direct_s8(const int8_t* __restrict__ in, const int8_t* __restrict__ f,
                                  const int32_t* __restrict__ bias,
-                                 const int32_t* __restrict__ mult,
-                                 const int32_t* __restrict__ shift, int8_t* __restrict__ out,
+                                 const RqChannel* __restrict__ rq, int8_t* __restrict__ out,
                                  const Geom g, int64_t pixels) {
   extern __shared__ int32_t sw[];
   const int K = g.KH * g.KW * g.C;
@@ -155,17 +286,43 @@ __global__ void k_conv_direct_s8(const int8_t* __restrict__ in, const int8_t* __
   int8_t* op = out + pix * g.Co + co0;
 #pragma unroll
   for (int j = 0; j < COB; ++j)
-    if (co0 + j < g.Co)
-      op[j] = static_cast<int8_t>(
-          finish_dev(acc[j], __ldg(mult + co0 + j), __ldg(shift + co0 + j), g.ap));
+    if (co0 + j < g.Co) op[j] = finish1(acc[j], load_rq(rq + co0 + j), g);
+}
+
+// --------------------------------------------------- depthwise (fallback)
+__global__ void k_dw_generic_s8(const int8_t* __restrict__ in, const int8_t* __restrict__ f,
+                                const int32_t* __restrict__ bias,
+                                const RqChannel* __restrict__ rq, int8_t* __restrict__ out,
+                                const Geom g, int64_t total) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int c = static_cast<int>(idx % g.C);
+  const int64_t pix = idx / g.C;
+  const int ox = static_cast<int>(pix % g.Wo);
+  const int oy = static_cast<int>((pix / g.Wo) % g.Ho);
+  const int64_t n = pix / (static_cast<int64_t>(g.Wo) * g.Ho);
+  int32_t acc = bias != nullptr ? __ldg(bias + c) : 0;
+  const int iy0 = oy * g.sh - g.pt, ix0 = ox * g.sw - g.pl;
+  const int8_t* img = in + n * g.H * g.W * static_cast<int64_t>(g.C);
+  for (int ky = 0; ky < g.KH; ++ky) {
+    const int iy = iy0 + ky;
+    if (iy < 0 || iy >= g.H) continue;
+    for (int kx = 0; kx < g.KW; ++kx) {
+      const int ix = ix0 + kx;
+      if (ix < 0 || ix >= g.W) continue;
+      acc += (static_cast<int32_t>(img[(static_cast<int64_t>(iy) * g.W + ix) * g.C + c]) -
+              g.zp_in) *
+             static_cast<int32_t>(f[(ky * g.KW + kx) * g.C + c]);
+    }
+  }
+  out[pix * g.C + c] = finish1(acc, load_rq(rq + c), g);
 }
 
 // --------------------------------------------------------------- FC (warp)
-// One warp per (sample, output): strided dot product and a shuffle reduce.
 __global__ void k_fc_warp_s8(const int8_t* __restrict__ in, const int8_t* __restrict__ f,
-                             const int32_t* __restrict__ bias, const int32_t* __restrict__ mult,
-                             const int32_t* __restrict__ shift, int8_t* __restrict__ out,
-                             int64_t K, int32_t N, int64_t total, int32_t zp_in, ActParams ap) {
+                             const int32_t* __restrict__ bias, const RqChannel* __restrict__ rq,
+                             int8_t* __restrict__ out, int64_t K, int32_t N, int64_t total,
+                             const Geom g) {
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= total) return;
@@ -175,13 +332,10 @@ __global__ void k_fc_warp_s8(const int8_t* __restrict__ in, const int8_t* __rest
   const int8_t* wr = f + static_cast<int64_t>(o) * K;
   int32_t s = 0;
   for (int64_t k = lane; k < K; k += 32)
-    s += (static_cast<int32_t>(x[k]) - zp_in) * static_cast<int32_t>(wr[k]);
+    s += (static_cast<int32_t>(x[k]) - g.zp_in) * static_cast<int32_t>(wr[k]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
-  if (lane == 0) {
-    const int32_t acc = s + (bias != nullptr ? bias[o] : 0);
-    out[b * N + o] = static_cast<int8_t>(finish_dev(acc, mult[o], shift[o], ap));
-  }
+  if (lane == 0) out[b * N + o] = finish1(s + (bias != nullptr ? bias[o] : 0), load_rq(rq + o), g);
 }
 
 // ----------------------------------------------------------------- pooling
@@ -227,27 +381,22 @@ __global__ void k_maxpool_s8(const int8_t* __restrict__ in, int8_t* __restrict__
   }
   int8_t* op = out + pix * g.C + c0;
   if constexpr (VEC >= 4) {
-    const uint32_t lo = (static_cast<uint32_t>(g.ap.act_min) & 0xFFu) * 0x01010101u;
-    const uint32_t hi = (static_cast<uint32_t>(g.ap.act_max) & 0xFFu) * 0x01010101u;
 #pragma unroll
-    for (int q = 0; q < kWords; ++q) m[q] = __vmins4(__vmaxs4(m[q], lo), hi);
+    for (int q = 0; q < kWords; ++q) m[q] = clamp4(m[q], g.lo4, g.hi4);
     if constexpr (VEC == 16)
       *reinterpret_cast<uint4*>(op) = make_uint4(m[0], m[1], m[2], m[3]);
     else
       *reinterpret_cast<uint32_t*>(op) = m[0];
   } else {
-    m1 = max(m1, g.ap.act_min);
-    m1 = min(m1, g.ap.act_max);
-    op[0] = static_cast<int8_t>(m1);
+    op[0] = static_cast<int8_t>(clamp4(static_cast<uint32_t>(m1) & 0xFFu, g.lo4, g.hi4) & 0xFFu);
   }
 }
 
 // Average pool: int32 sum of the in-image window, divided by the count with
-// round-half-away-from-zero (TFLite), clamped.  One thread per (sample,
-// oy, ox, 4 channels) or per channel when C % 4 != 0.
+// round-half-away-from-zero (TFLite), clamped.
 template <int VEC>
 __global__ void k_avgpool_s8(const int8_t* __restrict__ in, int8_t* __restrict__ out,
-                             const Geom g, int64_t total) {
+                             const Geom g, int32_t act_min, int32_t act_max, int64_t total) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   const int cv = g.C / VEC;
@@ -285,8 +434,8 @@ __global__ void k_avgpool_s8(const int8_t* __restrict__ in, int8_t* __restrict__
   for (int j = 0; j < VEC; ++j) {
     int32_t a = acc[j];
     a = a > 0 ? (a + cnt / 2) / cnt : (a - cnt / 2) / cnt;
-    a = max(a, g.ap.act_min);
-    a = min(a, g.ap.act_max);
+    a = max(a, act_min);
+    a = min(a, act_max);
     r[j] = a;
   }
   if constexpr (VEC == 4)
@@ -297,29 +446,77 @@ __global__ void k_avgpool_s8(const int8_t* __restrict__ in, int8_t* __restrict__
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-}  // namespace
-
-cudaError_t launch_dwconv(const pspml_op_desc& d, int64_t batch, const int8_t* in,
-                          const int8_t* filter, const int32_t* bias, const int32_t* mult,
-                          const int32_t* shift, int8_t* out, cudaStream_t s) {
-  const Geom g = geom_of(d);
-  const int64_t pix = batch * g.Ho * g.Wo;
-  if (g.C % 16 == 0 && aligned(in, 16) && aligned(out, 16) && aligned(filter, 16)) {
-    const int64_t total = pix * (g.C / 16);
-    k_dwconv_s8<16><<<grid_for(total), kBlock, 0, s>>>(in, filter, bias, mult, shift, out, g, total);
-  } else if (g.C % 4 == 0 && aligned(in, 4) && aligned(out, 4) && aligned(filter, 4)) {
-    const int64_t total = pix * (g.C / 4);
-    k_dwconv_s8<4><<<grid_for(total), kBlock, 0, s>>>(in, filter, bias, mult, shift, out, g, total);
-  } else {
-    const int64_t total = pix * g.C;
-    k_dwconv_s8<1><<<grid_for(total), kBlock, 0, s>>>(in, filter, bias, mult, shift, out, g, total);
+template <int KH, int KW, int CI>
+cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
+                           int8_t* out, cudaStream_t s) {
+  const int cob = g.Co <= 8 ? 8 : g.Co <= 16 ? 16 : 32;
+  const int pix = g.Ho * g.Wo;
+  for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
+    const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
+    const dim3 grid((pix + 127) / 128, (g.Co + cob - 1) / cob, nz);
+    if (cob == 8)
+      k_small_conv_s8<KH, KW, CI, 8><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff, p.rq,
+                                                          out, g, n0);
+    else if (cob == 16)
+      k_small_conv_s8<KH, KW, CI, 16><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff, p.rq,
+                                                           out, g, n0);
+    else
+      k_small_conv_s8<KH, KW, CI, 32><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff, p.rq,
+                                                           out, g, n0);
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_conv_direct(const pspml_op_desc& d, int64_t batch, const int8_t* in,
-                               const int8_t* filter, const int32_t* bias, const int32_t* mult,
-                               const int32_t* shift, int8_t* out, cudaStream_t s) {
+}  // namespace
+
+bool small_conv_supported(const pspml_op_desc& d) {
+  if (d.kernel_h != 3 || d.kernel_w != 3) return false;
+  return d.in_c == 1 || d.in_c == 2 || d.in_c == 3 || d.in_c == 4 || d.in_c == 8;
+}
+
+cudaError_t launch_small_conv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                              const int8_t* in, int8_t* out, cudaStream_t s) {
+  const Geom g = geom_of(d);
+  switch (d.in_c) {
+    case 1: return small_conv_cob<3, 3, 1>(g, p, batch, in, out, s);
+    case 2: return small_conv_cob<3, 3, 2>(g, p, batch, in, out, s);
+    case 3: return small_conv_cob<3, 3, 3>(g, p, batch, in, out, s);
+    case 4: return small_conv_cob<3, 3, 4>(g, p, batch, in, out, s);
+    case 8: return small_conv_cob<3, 3, 8>(g, p, batch, in, out, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_dw3x3(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                         const int8_t* in, int8_t* out, cudaStream_t s) {
+  const Geom g = geom_of(d);
+  constexpr int PX = 8;
+  const int groups = (g.Wo + PX - 1) / PX;
+  const int pairs = groups * (g.C / 4);
+  for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
+    const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
+    const dim3 grid((pairs + 127) / 128, g.Ho, nz);
+    const auto* i32 = reinterpret_cast<const uint32_t*>(in);
+    const auto* f32 = reinterpret_cast<const uint32_t*>(p.filter);
+    auto* o32 = reinterpret_cast<uint32_t*>(out);
+    if (g.sh == 1)
+      k_dw3x3_s8<1, PX><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+    else
+      k_dw3x3_s8<2, PX><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dw_generic(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                              const int8_t* in, int8_t* out, cudaStream_t s) {
+  const Geom g = geom_of(d);
+  const int64_t total = batch * g.Ho * g.Wo * g.C;
+  k_dw_generic_s8<<<grid_for(total), kBlock, 0, s>>>(in, p.filter, p.bias, p.rq, out, g, total);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_conv_direct(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                               const int8_t* in, int8_t* out, cudaStream_t s) {
   const Geom g = geom_of(d);
   const int64_t pixels = batch * g.Ho * g.Wo;
   const int K = g.KH * g.KW * g.C;
@@ -331,25 +528,23 @@ cudaError_t launch_conv_direct(const pspml_op_desc& d, int64_t batch, const int8
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(k_conv_direct_s8<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
-    k_conv_direct_s8<16><<<grid, kBlock, smem, s>>>(in, filter, bias, mult, shift, out, g, pixels);
+    k_conv_direct_s8<16><<<grid, kBlock, smem, s>>>(in, p.filter, p.bias, p.rq, out, g, pixels);
   } else {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(k_conv_direct_s8<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
-    k_conv_direct_s8<8><<<grid, kBlock, smem, s>>>(in, filter, bias, mult, shift, out, g, pixels);
+    k_conv_direct_s8<8><<<grid, kBlock, smem, s>>>(in, p.filter, p.bias, p.rq, out, g, pixels);
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_fc_warp(const pspml_op_desc& d, int64_t batch, const int8_t* in,
-                           const int8_t* filter, const int32_t* bias, const int32_t* mult,
-                           const int32_t* shift, int8_t* out, cudaStream_t s) {
+cudaError_t launch_fc_warp(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                           const int8_t* in, int8_t* out, cudaStream_t s) {
+  const Geom g = geom_of(d);
   const int64_t K = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
   const int64_t total = batch * d.out_c;
-  const int64_t threads = total * 32;
-  k_fc_warp_s8<<<grid_for(threads), kBlock, 0, s>>>(in, filter, bias, mult, shift, out, K,
-                                                   d.out_c, total, d.zp_in,
-                                                   ActParams{d.zp_out, d.act_min, d.act_max});
+  k_fc_warp_s8<<<grid_for(total * 32), kBlock, 0, s>>>(in, p.filter, p.bias, p.rq, out, K,
+                                                       d.out_c, total, g);
   return cudaGetLastError();
 }
 
@@ -376,10 +571,10 @@ cudaError_t launch_avgpool(const pspml_op_desc& d, int64_t batch, const int8_t* 
   const int64_t pix = batch * g.Ho * g.Wo;
   if (g.C % 4 == 0 && aligned(in, 4) && aligned(out, 4)) {
     const int64_t total = pix * (g.C / 4);
-    k_avgpool_s8<4><<<grid_for(total), kBlock, 0, s>>>(in, out, g, total);
+    k_avgpool_s8<4><<<grid_for(total), kBlock, 0, s>>>(in, out, g, d.act_min, d.act_max, total);
   } else {
     const int64_t total = pix * g.C;
-    k_avgpool_s8<1><<<grid_for(total), kBlock, 0, s>>>(in, out, g, total);
+    k_avgpool_s8<1><<<grid_for(total), kBlock, 0, s>>>(in, out, g, d.act_min, d.act_max, total);
   }
   return cudaGetLastError();
 }

@@ -15,15 +15,17 @@
 //                    corrects for the input zero point there.
 //   B  weights [N][taps*Kc] exactly as TFLite stores them ([Co][KH][KW][Ci]).
 //
-// Persistent kernel, one CTA per SM, 6 warps:
-//   warp 0      TMA producer (one thread), STAGES-deep smem ring
-//   warp 1      tensor-memory allocator + MMA issuer (one thread)
-//   warps 2..5  epilogue: tcgen05.ld -> requant -> int8 stores
-// Two accumulator buffers in tensor memory let the epilogue of one tile run
-// under the MMAs of the next.
+// Persistent kernel, one CTA per SM:
+//   warp 0           TMA producer (one thread), STAGES-deep smem ring
+//   warp 1           tensor-memory allocator + MMA issuer (one thread)
+//   warps 2..2+4G-1  G epilogue groups of 4 warps (one per tensor-memory
+//                    lane quarter).  Group g takes every G-th tile of the
+//                    CTA; NB >= G accumulator buffers in tensor memory let
+//                    the MMAs run ahead of the epilogues.
+// The epilogue is the critical path for the small-K layers of these
+// networks (K = 32..512), so it gets up to 16 warps.
 #include <algorithm>
 #include <atomic>
-#include <cstdio>
 
 #include "kernels.h"
 #include "ptx.cuh"
@@ -34,7 +36,6 @@ namespace pspml {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
 
@@ -54,13 +55,13 @@ struct TcGemmArgs {
   int32_t Kc;          // channels per tap (column stride of a tap in B)
   int8_t* out;
   int64_t ldo;
-  const int32_t* bias;
+  const int32_t* bias;  // [ncls][N] folded bias
   const uint8_t* ycls;
   const uint8_t* xcls;
   int32_t n_xcls;
-  const int32_t* mult;
-  const int32_t* shift;
-  int32_t zp_out, act_min, act_max;
+  const RqChannel* rq;
+  uint32_t lo4, hi4;    // activation clamp, bytes replicated
+  int32_t clamp;        // act range narrower than int8
   unsigned* err;
   int32_t stages;
 };
@@ -80,13 +81,21 @@ struct SwizzleFor<32> {
   static constexpr uint32_t kLayout = 6;  // 32B swizzle
 };
 
+// Tensor-memory accumulator buffers and epilogue groups per tile width.
+template <int BN>
+struct EpiShape {
+  static constexpr int kBufs = (512 / BN) >= 8 ? 8 : (512 / BN);
+  static constexpr int kGroups = kBufs >= 4 ? 4 : kBufs;
+  static constexpr int kThreads = 64 + 128 * kGroups;
+  static constexpr uint32_t kTmemCols = kBufs * BN;
+};
+
 __device__ __forceinline__ void record_error(unsigned* err, volatile int* abort_flag,
                                              unsigned code) {
   *abort_flag = 1;
   if (err != nullptr) atomicCAS(err, 0u, code);
 }
 
-// Output-pixel coordinates of tile tm (4D path).
 struct TileOrigin {
   int32_t x0, y0;
   int64_t n0;
@@ -106,23 +115,30 @@ __device__ __forceinline__ TileOrigin tile_origin(const TcGemmArgs& p, int64_t t
 
 // Requantises 32 accumulators of one output row and stores them.
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int8_t* dst,
-                                               const int32_t* bias, const int32_t* mult,
-                                               const int32_t* shift, int cnt,
-                                               const ActParams& ap) {
-  // mult/shift chunks start 128 B apart from a 256 B-aligned base; the
-  // folded bias row of a border class is 16 B aligned only when N % 4 == 0.
-  if (cnt == 32 && (reinterpret_cast<uintptr_t>(bias) & 15u) == 0) {
+                                               const int32_t* bias, const RqChannel* rq, int cnt,
+                                               const TcGemmArgs& p) {
+  if (cnt == 32) {
+    const bool bvec = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
     uint32_t packed[8];
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
-      const int4 b4 = __ldg(reinterpret_cast<const int4*>(bias) + g);
-      const int4 m4 = __ldg(reinterpret_cast<const int4*>(mult) + g);
-      const int4 s4 = __ldg(reinterpret_cast<const int4*>(shift) + g);
-      const int32_t r0 = finish_dev(static_cast<int32_t>(v[4 * g + 0]) + b4.x, m4.x, s4.x, ap);
-      const int32_t r1 = finish_dev(static_cast<int32_t>(v[4 * g + 1]) + b4.y, m4.y, s4.y, ap);
-      const int32_t r2 = finish_dev(static_cast<int32_t>(v[4 * g + 2]) + b4.z, m4.z, s4.z, ap);
-      const int32_t r3 = finish_dev(static_cast<int32_t>(v[4 * g + 3]) + b4.w, m4.w, s4.w, ap);
-      packed[g] = pack4_s8(r0, r1, r2, r3);
+      int4 b4;
+      if (bvec) {
+        b4 = __ldg(reinterpret_cast<const int4*>(bias) + g);
+      } else {
+        b4 = make_int4(__ldg(bias + 4 * g), __ldg(bias + 4 * g + 1), __ldg(bias + 4 * g + 2),
+                       __ldg(bias + 4 * g + 3));
+      }
+      const int32_t r0 = rq_apply(static_cast<int32_t>(v[4 * g + 0]) + b4.x, load_rq(rq + 4 * g));
+      const int32_t r1 =
+          rq_apply(static_cast<int32_t>(v[4 * g + 1]) + b4.y, load_rq(rq + 4 * g + 1));
+      const int32_t r2 =
+          rq_apply(static_cast<int32_t>(v[4 * g + 2]) + b4.z, load_rq(rq + 4 * g + 2));
+      const int32_t r3 =
+          rq_apply(static_cast<int32_t>(v[4 * g + 3]) + b4.w, load_rq(rq + 4 * g + 3));
+      uint32_t w = pack_sat4(r0, r1, r2, r3);
+      if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
+      packed[g] = w;
     }
     if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
       uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -142,24 +158,28 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int8_t* 
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (j < cnt) {
-        const int32_t r =
-            finish_dev(static_cast<int32_t>(v[j]) + __ldg(bias + j), __ldg(mult + j),
-                       __ldg(shift + j), ap);
-        dst[j] = static_cast<int8_t>(r);
+        int32_t r = rq_apply(static_cast<int32_t>(v[j]) + __ldg(bias + j), load_rq(rq + j));
+        r = max(r, -128);
+        r = min(r, 127);
+        uint32_t w = static_cast<uint32_t>(r) & 0xFFu;
+        if (p.clamp) w = clamp4(w * 0x01010101u, p.lo4, p.hi4) & 0xFFu;
+        dst[j] = static_cast<int8_t>(w);
       }
     }
   }
 }
 
 template <int BN, int BK>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
     k_gemm_s8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const TcGemmArgs p) {
   constexpr int A_BYTES = kBM * BK;
   constexpr int B_BYTES = BN * BK;
   constexpr uint32_t kLayout = SwizzleFor<BK>::kLayout;
   constexpr uint32_t kSbo = 8 * BK;  // bytes between 8-row groups
-  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr int NB = EpiShape<BN>::kBufs;
+  constexpr int G = EpiShape<BN>::kGroups;
+  constexpr uint32_t kTmemCols = EpiShape<BN>::kTmemCols;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -170,8 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * B_BYTES);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
+  uint64_t* tempty = tfull + NB;
+  uint64_t* mma_done = tempty + NB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -183,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NB; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
     }
@@ -255,16 +275,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = make_idesc_s8(kBM, BN);
       int s = 0;
       uint32_t ph = 0;
-      int acc = 0;
-      uint32_t aph = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag)) {
+      int64_t i = 0;  // local tile index
+      for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x, ++i) {
+        const int b = static_cast<int>(i % NB);
+        const uint32_t use = static_cast<uint32_t>(i / NB);
+        if (!mbar_wait(&tempty[b], (use & 1u) ^ 1u, abort_flag)) {
           record_error(p.err, abort_flag, kDevErrMmaWait);
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
         for (int it = 0; it < kiters; ++it) {
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             record_error(p.err, abort_flag, kDevErrMmaWait);
@@ -287,9 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
-        acc ^= 1;
-        if (acc == 0) aph ^= 1u;
+        umma_commit(&tfull[b]);
       }
       // All MMAs issued by this thread complete before tensor memory is freed.
       umma_commit(mma_done);
@@ -297,15 +316,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // --------------------------------------------------------- epilogue
+    const int grp = (warp - 2) >> 2;
     const int q = warp & 3;  // tensor-memory lane quarter this warp may read
     const int row = q * 32 + lane;
-    const ActParams ap{p.zp_out, p.act_min, p.act_max};
-    int acc = 0;
-    uint32_t aph = 0;
-    for (int64_t t = blockIdx.x; t < p.tiles_total; t += gridDim.x) {
+    int64_t i = grp;
+    for (int64_t t = blockIdx.x + static_cast<int64_t>(grp) * gridDim.x; t < p.tiles_total;
+         t += static_cast<int64_t>(G) * gridDim.x, i += G) {
+      const int b = static_cast<int>(i % NB);
+      const uint32_t use = static_cast<uint32_t>(i / NB);
       int ready = 0;
       if (lane == 0) {
-        ready = mbar_wait(&tfull[acc], aph, abort_flag) ? 1 : 0;
+        ready = mbar_wait(&tfull[b], use & 1u, abort_flag) ? 1 : 0;
         if (!ready) record_error(p.err, abort_flag, kDevErrEpiWait);
       }
       ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
@@ -336,19 +357,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN; c += 32) {
         uint32_t v[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(acc * BN + c),
+                      static_cast<uint32_t>(b * BN + c),
                   v);
         const int32_t nc = n0 + c;
-        if (valid && nc < p.N) {
-          const int cnt = min(32, p.N - nc);
-          epilogue_chunk(v, orow + nc, brow + nc, p.mult + nc, p.shift + nc, cnt, ap);
-        }
+        if (valid && nc < p.N)
+          epilogue_chunk(v, orow + nc, brow + nc, p.rq + nc, min(32, p.N - nc), p);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      acc ^= 1;
-      if (acc == 0) aph ^= 1u;
+      if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
 
@@ -356,49 +373,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
-  }
-}
-
-// ----------------------------------------------------------- bias folding
-struct FoldArgs {
-  int32_t N, taps, kw, Kc;
-  int32_t n_ycls, n_xcls;
-  int32_t zp_in;
-  uint32_t ymask[64];
-  uint32_t xmask[64];
-};
-
-// One warp per output channel: per-tap weight sums, then one folded bias
-// per border class.
-__global__ void k_fold_bias(const int8_t* __restrict__ filter, const int32_t* __restrict__ bias,
-                            int32_t* __restrict__ bias_eff, const FoldArgs a) {
-  __shared__ int32_t wsum_s[8][64];
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + w;
-  if (n >= a.N) return;
-  int32_t* wsum = wsum_s[w];
-  const int8_t* fr = filter + static_cast<int64_t>(n) * a.taps * a.Kc;
-  for (int tap = 0; tap < a.taps; ++tap) {
-    int32_t s = 0;
-    for (int c = lane; c < a.Kc; c += 32) s += fr[static_cast<int64_t>(tap) * a.Kc + c];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-    if (lane == 0) wsum[tap] = s;
-  }
-  __syncwarp();
-  const int32_t b = bias != nullptr ? bias[n] : 0;
-  const int ncls = a.n_ycls * a.n_xcls;
-  for (int cls = lane; cls < ncls; cls += 32) {
-    const uint32_t ym = a.ymask[cls / a.n_xcls];
-    const uint32_t xm = a.xmask[cls % a.n_xcls];
-    int32_t s = 0;
-    for (int tap = 0; tap < a.taps; ++tap) {
-      const int ky = tap / a.kw, kx = tap - (tap / a.kw) * a.kw;
-      if (((ym >> ky) & 1u) && ((xm >> kx) & 1u)) s += wsum[tap];
-    }
-    bias_eff[static_cast<int64_t>(cls) * a.N + n] =
-        static_cast<int32_t>(static_cast<uint32_t>(b) -
-                             static_cast<uint32_t>(a.zp_in) * static_cast<uint32_t>(s));
   }
 }
 
@@ -437,7 +411,8 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   }
   const int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
   if (grid <= 0) return cudaSuccess;
-  k_gemm_s8<BN, BK><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(ma, mb, args);
+  k_gemm_s8<BN, BK><<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb,
+                                                                                      args);
   return cudaGetLastError();
 }
 
@@ -454,87 +429,9 @@ cudaError_t run_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
 
 }  // namespace
 
-bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc) {
-  const int kh = d.kernel_h, kw = d.kernel_w;
-  if (d.out_h > 4096 || d.out_w > 4096 || kh > 32 || kw > 32) return false;
-  auto classify = [](int out, int in, int k, int stride, int pad, uint32_t* masks, int* nmask,
-                     uint8_t* cls) {
-    *nmask = 0;
-    for (int o = 0; o < out; ++o) {
-      uint32_t m = 0;
-      for (int t = 0; t < k; ++t) {
-        const int i = o * stride + t - pad;
-        if (i >= 0 && i < in) m |= 1u << t;
-      }
-      int found = -1;
-      for (int j = 0; j < *nmask; ++j)
-        if (masks[j] == m) found = j;
-      if (found < 0) {
-        if (*nmask >= 64) return false;
-        masks[*nmask] = m;
-        found = (*nmask)++;
-      }
-      cls[o] = static_cast<uint8_t>(found);
-    }
-    return true;
-  };
-  if (!classify(d.out_h, d.in_h, kh, d.stride_h, d.pad_top, bc->ymask, &bc->n_ycls, bc->ycls))
-    return false;
-  if (!classify(d.out_w, d.in_w, kw, d.stride_w, d.pad_left, bc->xmask, &bc->n_xcls, bc->xcls))
-    return false;
-  return true;
-}
-
-cudaError_t launch_fold_bias(const pspml_op_desc& d, const int8_t* filter, const int32_t* bias,
-                             const BorderClasses& bc, int32_t* bias_eff, cudaStream_t s) {
-  FoldArgs a{};
-  a.N = d.out_c;
-  if (d.kind == PSPML_OP_FULLY_CONNECTED) {
-    a.taps = 1;
-    a.kw = 1;
-    a.Kc = d.in_h * d.in_w * d.in_c;
-    a.n_ycls = 1;
-    a.n_xcls = 1;
-    a.ymask[0] = 1;
-    a.xmask[0] = 1;
-  } else {
-    a.taps = d.kernel_h * d.kernel_w;
-    a.kw = d.kernel_w;
-    a.Kc = d.in_c;
-    a.n_ycls = bc.n_ycls;
-    a.n_xcls = bc.n_xcls;
-    for (int i = 0; i < 64; ++i) {
-      a.ymask[i] = bc.ymask[i];
-      a.xmask[i] = bc.xmask[i];
-    }
-  }
-  if (a.taps > 64) return cudaErrorInvalidValue;
-  a.zp_in = d.zp_in;
-  const int blocks = (a.N + 7) / 8;
-  k_fold_bias<<<blocks, 256, 0, s>>>(filter, bias, bias_eff, a);
-  return cudaGetLastError();
-}
-
-GemmPath choose_fc_path(const pspml_op_desc& d) {
-  const int64_t K = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
-  return (K % 16 == 0) ? GemmPath::kTc2d : GemmPath::kFcWarp;
-}
-
-GemmPath choose_conv_path(const pspml_op_desc& d) {
-  if (d.in_c % 16 != 0) return GemmPath::kDirect;
-  if (d.kernel_h == 1 && d.kernel_w == 1 && d.stride_h == 1 && d.stride_w == 1 &&
-      d.pad_top == 0 && d.pad_left == 0 && d.out_h == d.in_h && d.out_w == d.in_w)
-    return GemmPath::kTc2d;
-  if (d.stride_h == 1 && d.stride_w == 1 && d.kernel_h * d.kernel_w <= 64 &&
-      d.kernel_h <= 32 && d.kernel_w <= 32 && d.out_w <= 4096 && d.out_h <= 4096)
-    return GemmPath::kTc4d;
-  return GemmPath::kDirect;
-}
-
-cudaError_t launch_tc_gemm(const pspml_op_desc& d, GemmPath path, int64_t batch,
-                           const int8_t* in, const int8_t* filter, const FoldedBias& fb,
-                           const int32_t* mult, const int32_t* shift, int8_t* out,
-                           unsigned* dev_err, int num_sms, cudaStream_t s) {
+cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
+                           const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                           cudaStream_t s) {
   const int N = d.out_c;
   const bool is_fc = d.kind == PSPML_OP_FULLY_CONNECTED;
   const int Kc = is_fc ? d.in_h * d.in_w * d.in_c : d.in_c;
@@ -552,15 +449,14 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, GemmPath path, int64_t batch,
   a.N = N;
   a.Kc = Kc;
   a.out = out;
-  a.bias = fb.bias_eff;
-  a.ycls = fb.ncls > 1 ? fb.ycls : nullptr;
-  a.xcls = fb.ncls > 1 ? fb.xcls : nullptr;
-  a.n_xcls = fb.n_xcls;
-  a.mult = mult;
-  a.shift = shift;
-  a.zp_out = d.zp_out;
-  a.act_min = d.act_min;
-  a.act_max = d.act_max;
+  a.bias = pp.bias_eff;
+  a.ycls = pp.ncls > 1 ? pp.ycls : nullptr;
+  a.xcls = pp.ncls > 1 ? pp.xcls : nullptr;
+  a.n_xcls = pp.n_xcls;
+  a.rq = pp.rq;
+  a.lo4 = splat4(d.act_min);
+  a.hi4 = splat4(d.act_max);
+  a.clamp = (d.act_min > -128 || d.act_max < 127) ? 1 : 0;
   a.err = dev_err;
 
   const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
@@ -568,7 +464,7 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, GemmPath path, int64_t batch,
                                             : CU_TENSOR_MAP_SWIZZLE_32B;
   CUtensorMap ma, mb;
   const uint32_t estr[4] = {1, 1, 1, 1};
-  if (path == GemmPath::kTc4d) {
+  if (pp.path == OpPath::kTc4d) {
     const int bw = std::min(pow2_ceil(d.out_w), 128);
     const int bh = std::min(pow2_ceil(d.out_h), 128 / bw);
     const int bi = 128 / (bw * bh);
@@ -610,7 +506,7 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, GemmPath path, int64_t batch,
     const uint64_t dims[2] = {static_cast<uint64_t>(taps) * Kc, static_cast<uint64_t>(N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(taps) * Kc};
     const uint32_t box[2] = {static_cast<uint32_t>(bk), static_cast<uint32_t>(bn)};
-    if (encode_tensor_map(&mb, filter, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
+    if (encode_tensor_map(&mb, pp.filter, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
   switch (bk) {

@@ -1,80 +1,111 @@
-// kernels.h - launchers for the device kernels (host side, C++).
+// kernels.h - device-side preparation and launch of the int8 ops (host C++).
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/pspml.h"
+#include "requant.cuh"
 
 namespace pspml {
 
-// Folded epilogue tables for a conv / FC layer on the device:
-//   bias_eff[cls][n] = bias[n] - zp_in * sum of w[n][tap][ci] over the taps
-//   that lie inside the image for border class cls.
-// Class cls = ycls[y] * n_xcls + xcls[x] for an output pixel (x, y); a FC or
-// unpadded layer has one class.
-struct FoldedBias {
-  int32_t* bias_eff = nullptr;  // [ncls][N]
-  uint8_t* ycls = nullptr;      // [Ho] (null when ncls == 1)
-  uint8_t* xcls = nullptr;      // [Wo]
-  int32_t ncls = 1;
-  int32_t n_xcls = 1;
+// Which kernel runs an op.
+enum class OpPath {
+  kTc2d,       // tcgen05 GEMM, A = [rows][K] (FC, 1x1 stride-1 conv)
+  kTc4d,       // tcgen05 implicit GEMM over NHWC (stride-1 conv, in_c % 16 == 0)
+  kSmallConv,  // CUDA-core dp4a conv over packed patches (small in_c)
+  kDirect,     // CUDA-core conv, any shape (fallback)
+  kFcWarp,     // CUDA-core FC, one warp per output (K % 16 != 0)
+  kDw3x3,      // CUDA-core dp4a depthwise 3x3, C % 4 == 0
+  kDwGeneric,  // CUDA-core depthwise, any shape (fallback)
+  kMaxPool,
+  kAvgPool,
+  kReshape
 };
 
-// Host-side description of the border classes of a stride-1 conv.
+// Border classes of a conv with padding: output row y has class ycls[y],
+// column x has class xcls[x]; ymask/xmask give the in-image filter taps of
+// each class.
 struct BorderClasses {
   int32_t n_ycls = 1, n_xcls = 1;
-  uint32_t ymask[64] = {0};  // valid-ky bit mask per row class
-  uint32_t xmask[64] = {0};  // valid-kx bit mask per column class
-  uint8_t ycls[4096];        // class of each output row
-  uint8_t xcls[4096];        // class of each output column
+  uint32_t ymask[64] = {0};
+  uint32_t xmask[64] = {0};
+  uint8_t ycls[4096];
+  uint8_t xcls[4096];
 };
-
-// Fills `bc` for op `d` (stride must be 1 when more than one class is
-// possible).  Returns false if the geometry has too many classes.
 bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc);
 
-// Device prep: bias_eff[cls][n] from raw weights/bias (filter in
-// [N][KH][KW][Ci] layout, or [N][K] for FC which is one tap).
-cudaError_t launch_fold_bias(const pspml_op_desc& d, const int8_t* filter, const int32_t* bias,
-                             const BorderClasses& bc, int32_t* bias_eff, cudaStream_t s);
+// Everything a kernel needs beyond the activations, on the device.
+struct PreparedOp {
+  OpPath path = OpPath::kDirect;
+  const int8_t* filter = nullptr;   // TFLite-layout filter
+  const int32_t* bias = nullptr;    // raw bias (fallback kernels)
+  const int32_t* mult = nullptr;
+  const int32_t* shift = nullptr;
+  const uint32_t* wpack = nullptr;  // kSmallConv: [N][nw] patch-order words
+  int32_t nw = 0;
+  int32_t* bias_eff = nullptr;      // [ncls][N]: bias - zp_in * (in-image weight sum)
+  RqChannel* rq = nullptr;          // [N]
+  uint8_t* ycls = nullptr;          // [out_h] (tensor-core conv with ncls > 1)
+  uint8_t* xcls = nullptr;          // [out_w]
+  int32_t ncls = 1, n_xcls = 1;
+};
 
-// Which implementation runs a conv / FC.
-enum class GemmPath { kTc2d, kTc4d, kDirect, kFcWarp };
-GemmPath choose_conv_path(const pspml_op_desc& d);
-GemmPath choose_fc_path(const pspml_op_desc& d);
+// Input-channel / kernel shapes k_small_conv_s8 is instantiated for.
+bool small_conv_supported(const pspml_op_desc& d);
 
-// tcgen05 GEMM (2D: rows x K times N x K; 4D: implicit stride-1 conv).
-// `rows` is batch*Ho*Wo for a conv, batch for FC.
-cudaError_t launch_tc_gemm(const pspml_op_desc& d, GemmPath path, int64_t batch,
-                           const int8_t* in, const int8_t* filter, const FoldedBias& fb,
-                           const int32_t* mult, const int32_t* shift, int8_t* out,
-                           unsigned* dev_err, int num_sms, cudaStream_t s);
+// Path for op `d` given operand alignment (16-byte aligned pointers allow the
+// TMA / vector paths).
+OpPath choose_path(const pspml_op_desc& d, bool aligned16);
 
-// CUDA-core direct conv (any stride / padding / channel count).
-cudaError_t launch_conv_direct(const pspml_op_desc& d, int64_t batch, const int8_t* in,
-                               const int8_t* filter, const int32_t* bias, const int32_t* mult,
-                               const int32_t* shift, int8_t* out, cudaStream_t s);
+// Device bytes prepare_op needs for `d` on `path`.
+size_t prepared_bytes(const pspml_op_desc& d, OpPath path);
 
-// CUDA-core FC (one warp per output), for K not a multiple of 16.
-cudaError_t launch_fc_warp(const pspml_op_desc& d, int64_t batch, const int8_t* in,
-                           const int8_t* filter, const int32_t* bias, const int32_t* mult,
-                           const int32_t* shift, int8_t* out, cudaStream_t s);
+// Fills `out` using `mem` (device, prepared_bytes(d, path) bytes, 256-byte
+// aligned) for derived tables; kernels on `s`.  Returns a cudaError_t.
+cudaError_t prepare_op(const pspml_op_desc& d, OpPath path, const int8_t* filter,
+                       const int32_t* bias, const int32_t* mult, const int32_t* shift,
+                       uint8_t* mem, PreparedOp* out, cudaStream_t s);
 
-cudaError_t launch_dwconv(const pspml_op_desc& d, int64_t batch, const int8_t* in,
-                          const int8_t* filter, const int32_t* bias, const int32_t* mult,
-                          const int32_t* shift, int8_t* out, cudaStream_t s);
+// Launches op `d` over `batch` samples.
+cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                      const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                      cudaStream_t s);
 
+// ---- individual launchers (gemm_tc.cu, cuda_core.cu)
+cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                           const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                           cudaStream_t s);
+cudaError_t launch_small_conv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                              const int8_t* in, int8_t* out, cudaStream_t s);
+cudaError_t launch_conv_direct(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                               const int8_t* in, int8_t* out, cudaStream_t s);
+cudaError_t launch_fc_warp(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                           const int8_t* in, int8_t* out, cudaStream_t s);
+cudaError_t launch_dw3x3(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                         const int8_t* in, int8_t* out, cudaStream_t s);
+cudaError_t launch_dw_generic(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                              const int8_t* in, int8_t* out, cudaStream_t s);
 cudaError_t launch_maxpool(const pspml_op_desc& d, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s);
-
 cudaError_t launch_avgpool(const pspml_op_desc& d, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s);
+
+// ---- preparation kernels (prep.cu)
+cudaError_t launch_fold_bias(const pspml_op_desc& d, const int8_t* filter, const int32_t* bias,
+                             const BorderClasses& bc, int32_t* bias_eff, cudaStream_t s);
+cudaError_t launch_build_rq(const int32_t* mult, const int32_t* shift, int32_t zp_out, int32_t n,
+                            RqChannel* rq, cudaStream_t s);
+cudaError_t launch_pack_patch_weights(const int8_t* filter, int32_t n, int32_t k, int32_t nw,
+                                      uint32_t* out, cudaStream_t s);
 
 // Encodes a tiled TMA descriptor through the driver entry point.
 CUresult encode_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                            const uint64_t* strides_bytes, const uint32_t* box,
                            const uint32_t* elem_strides, CUtensorMapSwizzle swizzle);
+
+inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 }  // namespace pspml

@@ -50,42 +50,8 @@ int64_t filter_bytes_of(const pspml_op_desc& d) {
 
 int run_op(pspml_model* m, const ModelOp& op, int64_t mb, const int8_t* src, int8_t* dst,
            cudaStream_t s) {
-  const pspml_op_desc& d = op.d;
-  pspml_ctx* ctx = m->ctx;
-  cudaError_t e = cudaSuccess;
-  switch (d.kind) {
-    case PSPML_OP_CONV2D:
-      if (op.path == GemmPath::kDirect)
-        e = launch_conv_direct(d, mb, src, op.filter, op.bias, op.mult, op.shift, dst, s);
-      else
-        e = launch_tc_gemm(d, op.path, mb, src, op.filter, op.fb, op.mult, op.shift, dst,
-                           ctx->dev_err, ctx->num_sms, s);
-      break;
-    case PSPML_OP_FULLY_CONNECTED:
-      if (op.path == GemmPath::kFcWarp)
-        e = launch_fc_warp(d, mb, src, op.filter, op.bias, op.mult, op.shift, dst, s);
-      else
-        e = launch_tc_gemm(d, op.path, mb, src, op.filter, op.fb, op.mult, op.shift, dst,
-                           ctx->dev_err, ctx->num_sms, s);
-      break;
-    case PSPML_OP_DEPTHWISE_CONV2D:
-      e = launch_dwconv(d, mb, src, op.filter, op.bias, op.mult, op.shift, dst, s);
-      break;
-    case PSPML_OP_MAX_POOL2D:
-      e = launch_maxpool(d, mb, src, dst, s);
-      break;
-    case PSPML_OP_AVERAGE_POOL2D:
-      e = launch_avgpool(d, mb, src, dst, s);
-      break;
-    case PSPML_OP_RESHAPE:
-      if (dst != src)
-        e = cudaMemcpyAsync(dst, src, static_cast<size_t>(mb * op.out_elems),
-                            cudaMemcpyDeviceToDevice, s);
-      break;
-    default:
-      return set_error(PSPML_ERR_INVALID_ARG, "unknown op kind");
-  }
-  return cuda_status(e, "op launch");
+  return cuda_status(
+      launch_op(op.d, op.prep, mb, src, dst, m->ctx->dev_err, m->ctx->num_sms, s), "op launch");
 }
 
 // Output pointer of every op for one micro-batch.
@@ -225,8 +191,8 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
   m->out_elems = out_elems_of(ops[n_ops - 1]);
   m->ops.resize(n_ops);
 
-  // Tables for the tensor-core ops go after the blob.
-  std::vector<BorderClasses> classes(n_ops);
+  // Prepared tables (folded biases, requantisation constants, packed
+  // weights) go after the blob.
   std::vector<size_t> table_off(n_ops, 0);
   size_t wbytes = align_up(blob_bytes, 256);
   for (int i = 0; i < n_ops; ++i) {
@@ -234,26 +200,15 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     op.d = ops[i];
     op.in_elems = in_elems_of(ops[i]);
     op.out_elems = out_elems_of(ops[i]);
-    if (op.d.kind == PSPML_OP_CONV2D) op.path = choose_conv_path(op.d);
-    if (op.d.kind == PSPML_OP_FULLY_CONNECTED) op.path = choose_fc_path(op.d);
-    const bool tc = (op.d.kind == PSPML_OP_CONV2D || op.d.kind == PSPML_OP_FULLY_CONNECTED) &&
-                    (op.path == GemmPath::kTc2d || op.path == GemmPath::kTc4d);
-    if (!tc) continue;
-    BorderClasses& bc = classes[i];
-    if (op.path == GemmPath::kTc4d) {
-      if (!build_border_classes(op.d, &bc)) {
-        op.path = GemmPath::kDirect;
-        continue;
-      }
-    } else {
-      bc.n_ycls = bc.n_xcls = 1;
-      bc.ymask[0] = bc.xmask[0] = 0xFFFFFFFFu;
+    OpPath path = choose_path(op.d, true);
+    size_t need = prepared_bytes(op.d, path);
+    if (path == OpPath::kTc4d && need == 0) {  // too many border classes for the tables
+      path = OpPath::kDirect;
+      need = prepared_bytes(op.d, path);
     }
-    op.fb.ncls = bc.n_ycls * bc.n_xcls;
-    op.fb.n_xcls = bc.n_xcls;
+    op.prep.path = path;
     table_off[i] = wbytes;
-    wbytes += align_up(static_cast<size_t>(op.fb.ncls) * op.d.out_c * 4, 256) +
-              align_up(op.d.out_h, 256) + align_up(op.d.out_w, 256);
+    wbytes += need;
   }
   st = cuda_status(cudaMalloc(&m->weights, wbytes), "cudaMalloc(weights)");
   if (!st && blob_bytes > 0)
@@ -262,29 +217,17 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
   for (int i = 0; i < n_ops && !st; ++i) {
     ModelOp& op = m->ops[i];
     const pspml_op_desc& d = op.d;
+    const int8_t* filter = nullptr;
+    const int32_t *bias = nullptr, *mult = nullptr, *shift = nullptr;
     if (has_weights(d)) {
-      op.filter = reinterpret_cast<int8_t*>(m->weights + d.filter_off);
-      op.bias = d.bias_off >= 0 ? reinterpret_cast<int32_t*>(m->weights + d.bias_off) : nullptr;
-      op.mult = reinterpret_cast<int32_t*>(m->weights + d.mult_off);
-      op.shift = reinterpret_cast<int32_t*>(m->weights + d.shift_off);
+      filter = reinterpret_cast<int8_t*>(m->weights + d.filter_off);
+      bias = d.bias_off >= 0 ? reinterpret_cast<int32_t*>(m->weights + d.bias_off) : nullptr;
+      mult = reinterpret_cast<int32_t*>(m->weights + d.mult_off);
+      shift = reinterpret_cast<int32_t*>(m->weights + d.shift_off);
     }
-    if (table_off[i] == 0) continue;
-    uint8_t* t = m->weights + table_off[i];
-    op.fb.bias_eff = reinterpret_cast<int32_t*>(t);
-    op.fb.ycls = t + align_up(static_cast<size_t>(op.fb.ncls) * d.out_c * 4, 256);
-    op.fb.xcls = op.fb.ycls + align_up(d.out_h, 256);
-    if (op.fb.ncls > 1) {
-      st = cuda_status(cudaMemcpy(op.fb.ycls, classes[i].ycls, d.out_h, cudaMemcpyHostToDevice),
-                       "class tables");
-      if (!st)
-        st = cuda_status(
-            cudaMemcpy(op.fb.xcls, classes[i].xcls, d.out_w, cudaMemcpyHostToDevice),
-            "class tables");
-    }
-    if (!st)
-      st = cuda_status(launch_fold_bias(d, op.filter, op.bias, classes[i], op.fb.bias_eff,
-                                        ctx->stream),
-                       "fold bias");
+    st = cuda_status(prepare_op(d, op.prep.path, filter, bias, mult, shift,
+                                m->weights + table_off[i], &op.prep, ctx->stream),
+                     "op preparation");
   }
   if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "model preparation");
 

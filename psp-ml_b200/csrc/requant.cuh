@@ -31,6 +31,90 @@ __device__ __forceinline__ int32_t mbqm_dev(int32_t x, int32_t m, int32_t shift)
   return (h >> right) + (rem > thr ? 1 : 0);
 }
 
+// Per-channel requantisation constants (16 bytes, one vector load).
+//
+// Fast form, for a right shift r = -shift in [1, 23] (every calibrated TFLite
+// layer): with a = acc + bias, p = a * M and C = 2^30 + 2^(30+r) + zp * 2^(31+r),
+//   out + zp_out = floor((p + C - [a < 0] * 2^31) / 2^(31 + r))
+// which equals RoundingDivideByPOT(SaturatingRoundingDoublingHighMul(a, M), r)
+// + zp_out exactly: the high-mul rounding is floor((p + 2^30) / 2^31); the
+// POT division adds 2^(r-1) minus one for a negative high-mul result and
+// floors; floor((floor(x / A) + k) / B) = floor((x + k*A) / (A*B)) merges the
+// two floors; and replacing [high-mul < 0] by [a < 0] only differs when the
+// high-mul is 0, where both give 0 for r >= 1.  With t = p + C split into
+// 32-bit halves (lo, hi), the [a < 0] * 2^31 correction lowers hi by one
+// exactly when a < 0 and lo < 2^31, so
+//   out + zp_out = (hi + ((a & ~lo) >> 31)) >> (r - 1).
+// |p| < 2^62 and |C| < 2^62 for r <= 23, so t never overflows.
+// Other shifts (left shifts, r == 0, r > 23) take the general path: sr < 0,
+// c_lo holds the TFLite shift and c_hi the output zero point.
+struct RqChannel {
+  int32_t m;
+  uint32_t c_lo;
+  int32_t c_hi;
+  int32_t sr;
+};
+
+__host__ __device__ inline RqChannel make_rq(int32_t m, int32_t shift, int32_t zp_out) {
+  RqChannel q;
+  const int32_t r = -shift;
+  if (m > 0 && r >= 1 && r <= 23) {
+    const int64_t c = (int64_t{1} << 30) + (int64_t{1} << (30 + r)) +
+                      static_cast<int64_t>(zp_out) * (int64_t{1} << (31 + r));
+    q.m = m;
+    q.c_lo = static_cast<uint32_t>(static_cast<uint64_t>(c));
+    q.c_hi = static_cast<int32_t>(c >> 32);
+    q.sr = r - 1;
+  } else {
+    q.m = m;
+    q.c_lo = static_cast<uint32_t>(shift);
+    q.c_hi = zp_out;
+    q.sr = -1;
+  }
+  return q;
+}
+
+// requantised value + zp_out, before clamping.
+__device__ __forceinline__ int32_t rq_apply(int32_t a, const RqChannel& q) {
+  if (q.sr >= 0) {
+    const int64_t c = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi))
+                                            << 32) | q.c_lo);
+    const int64_t t = static_cast<int64_t>(a) * q.m + c;
+    const int32_t lo = static_cast<int32_t>(t);
+    const int32_t hi = static_cast<int32_t>(t >> 32);
+    return (hi + ((a & ~lo) >> 31)) >> q.sr;
+  }
+  return mbqm_dev(a, q.m, static_cast<int32_t>(q.c_lo)) + q.c_hi;
+}
+
+__device__ __forceinline__ RqChannel load_rq(const RqChannel* p) {
+  const int4 v = __ldg(reinterpret_cast<const int4*>(p));
+  RqChannel q;
+  q.m = v.x;
+  q.c_lo = static_cast<uint32_t>(v.y);
+  q.c_hi = v.z;
+  q.sr = v.w;
+  return q;
+}
+
+// Four int32 -> four int8 with saturation to [-128, 127], x0 in byte 0.
+// cvt.pack.sat.s8.s32.b32 d, a, b, c gives d = (c << 16) | sat(a) << 8 | sat(b).
+__device__ __forceinline__ uint32_t pack_sat4(int32_t x0, int32_t x1, int32_t x2, int32_t x3) {
+  uint32_t hi, d;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(x3), "r"(x2));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x1), "r"(x0), "r"(hi));
+  return d;
+}
+
+// Clamp of four packed int8 lanes to [lo, hi] (bytes replicated).
+__device__ __forceinline__ uint32_t clamp4(uint32_t v, uint32_t lo4, uint32_t hi4) {
+  return __vmins4(__vmaxs4(v, lo4), hi4);
+}
+
+__host__ __device__ inline uint32_t splat4(int32_t v) {
+  return (static_cast<uint32_t>(v) & 0xFFu) * 0x01010101u;
+}
+
 struct ActParams {
   int32_t zp_out, act_min, act_max;
 };

@@ -16,7 +16,7 @@ struct pspml_ctx {
   int num_sms = 148;
   int64_t timeout_ms = 0;
   unsigned* dev_err = nullptr;      // device error word written by kernels
-  uint8_t* workspace = nullptr;     // per-op folded biases / class tables
+  uint8_t* workspace = nullptr;     // per-op prepared tables (folded bias, requant)
   size_t workspace_bytes = 0;
   cudaStream_t stream = nullptr;    // internal stream for synchronous work
 };
@@ -34,21 +34,10 @@ int validate_desc(const pspml_op_desc* d);
 // Waits for `ev` honouring the context's watchdog.
 int wait_event(pspml_ctx* ctx, cudaEvent_t ev);
 
-// Folds the bias into `ws` and runs the tensor-core GEMM for a conv / FC.
-int run_tc_with_workspace(pspml_ctx* ctx, const pspml_op_desc* d, GemmPath path, int64_t batch,
-                          const int8_t* in, const int8_t* filter, const int32_t* bias,
-                          const int32_t* mult, const int32_t* shift, int8_t* out,
-                          uint8_t* ws, size_t ws_bytes, cudaStream_t s);
-
 // One prepared op of a model.
 struct ModelOp {
   pspml_op_desc d{};
-  GemmPath path = GemmPath::kDirect;
-  int8_t* filter = nullptr;   // device copies (into the model's weight buffer)
-  int32_t* bias = nullptr;
-  int32_t* mult = nullptr;
-  int32_t* shift = nullptr;
-  FoldedBias fb;              // tensor-core paths only
+  PreparedOp prep;
   int64_t out_off = 0;        // arena offset of the output (bytes per micro-batch)
   int64_t out_elems = 0;      // per sample
   int64_t in_elems = 0;
@@ -60,7 +49,7 @@ struct ModelOp {
 struct pspml_model {
   pspml_ctx* ctx = nullptr;
   std::vector<pspml::ModelOp> ops;
-  uint8_t* weights = nullptr;        // device: blob + folded tables
+  uint8_t* weights = nullptr;        // device: blob + prepared tables
   uint8_t* arena = nullptr;          // device: intermediates for one micro-batch
   size_t arena_bytes = 0;
   int32_t max_micro = 0;

@@ -1,0 +1,46 @@
+"""The device requantisation uses a closed form of TFLite's
+MultiplyByQuantizedMultiplier (see psp-ml_b200/csrc/requant.cuh).  This
+restates that closed form in Python integers and checks it against the
+oracle's literal gemmlowp arithmetic over edge and random inputs."""
+import random
+
+from oracle import oracle as orc
+
+U64 = (1 << 64) - 1
+
+
+def closed_form(a: int, m: int, r: int, zp: int) -> int:
+    """(hi + ((a & ~lo) >> 31)) >> (r - 1) with t = a*m + C split in halves."""
+    c = (1 << 30) + (1 << (30 + r)) + zp * (1 << (31 + r))
+    t = (a * m + c) & U64                      # 64-bit wrap (never needed for r <= 23)
+    lo = t & 0xFFFFFFFF
+    hi = t >> 32
+    if hi >= 1 << 31:
+        hi -= 1 << 32
+    adj = -1 if ((a & 0xFFFFFFFF) & (~lo & 0xFFFFFFFF)) >> 31 else 0
+    return (hi + adj) >> (r - 1)
+
+
+def test_closed_form_matches_tflite_definition():
+    rng = random.Random(1)
+    edges = [0, 1, -1, 2, -2, (1 << 31) - 1, -(1 << 31), 1 << 30, -(1 << 30), 12345, -12345]
+    for it in range(60000):
+        m = rng.choice([1 << 30, (1 << 31) - 1, rng.randint(1 << 30, (1 << 31) - 1)])
+        r = rng.randint(1, 23)
+        zp = rng.randint(-128, 127)
+        if it % 5 == 0:
+            a = rng.choice(edges)
+        elif it % 3 == 0:
+            a = rng.randint(-(1 << 31), (1 << 31) - 1)
+        else:
+            a = rng.randint(-(1 << 26), 1 << 26)
+        assert closed_form(a, m, r, zp) == orc.mbqm(a, m, -r) + zp, (a, m, r, zp)
+
+
+def test_closed_form_exact_halves():
+    # values whose first rounding lands exactly on a tie of the second
+    for r in range(1, 24):
+        for a in (-(3 << r), -(1 << r), -1, 0, 1, 1 << r, 3 << r):
+            for m in (1 << 30, (1 << 30) + 1, (1 << 31) - 1):
+                for zp in (-128, 0, 127):
+                    assert closed_form(a, m, r, zp) == orc.mbqm(a, m, -r) + zp

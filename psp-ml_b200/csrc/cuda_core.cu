@@ -54,12 +54,13 @@ unsigned grid_for(int64_t n) {
   return static_cast<unsigned>(std::max<int64_t>(1, (n + kBlock - 1) / kBlock));
 }
 
+template <bool FAST = false>
 __device__ __forceinline__ uint32_t finish4(int32_t a0, int32_t a1, int32_t a2, int32_t a3,
                                             const int4& b, const RqChannel& q0,
                                             const RqChannel& q1, const RqChannel& q2,
                                             const RqChannel& q3, const Geom& g) {
-  uint32_t w = pack_sat4(rq_apply(a0 + b.x, q0), rq_apply(a1 + b.y, q1), rq_apply(a2 + b.z, q2),
-                         rq_apply(a3 + b.w, q3));
+  uint32_t w = pack_sat4(rq_sel<FAST>(a0 + b.x, q0), rq_sel<FAST>(a1 + b.y, q1),
+                         rq_sel<FAST>(a2 + b.z, q2), rq_sel<FAST>(a3 + b.w, q3));
   if (g.clamp) w = clamp4(w, g.lo4, g.hi4);
   return w;
 }
@@ -77,7 +78,7 @@ __device__ __forceinline__ int8_t finish1(int32_t a, const RqChannel& q, const G
 // Thread: 4 channels (one word) x PX consecutive output pixels of one row.
 // Block: 128 threads over (pixel group, channel word) pairs of one output
 // row (blockIdx.y) of one image (blockIdx.z + n_base).  Weights [9][C].
-template <int S, int PX>
+template <int S, int PX, bool FAST>
 __global__ void __launch_bounds__(128)
     k_dw3x3_s8(const uint32_t* __restrict__ in, const uint32_t* __restrict__ f,
                const int32_t* __restrict__ bias_eff, const RqChannel* __restrict__ rq,
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(128)
   for (int p = 0; p < PX; ++p)
     if (ox0 + p < g.Wo)
       orow[static_cast<int64_t>(ox0 + p) * cwn] =
-          finish4(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
+          finish4<FAST>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
 }
 
 // --------------------------------------------------- small-channel conv (dp4a)
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(128)
 // The KHxKWxCI patch is packed into NW words in TFLite filter order
 // (ky, kx, ci); out-of-image taps hold the input zero point.  Weights of the
 // chunk sit in shared memory as [COB][NW] words (16-byte rows).
-template <int KH, int KW, int CI, int COB>
+template <int KH, int KW, int CI, int COB, bool FAST>
 __global__ void __launch_bounds__(128)
     k_small_conv_s8(const int8_t* __restrict__ in, const uint32_t* __restrict__ wpack,
                     int32_t nw_stride, const int32_t* __restrict__ bias_eff,
@@ -227,7 +228,7 @@ __global__ void __launch_bounds__(128)
       const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff + co0) + c4);
       const int cb = co0 + 4 * c4;
       reinterpret_cast<uint32_t*>(op)[c4] =
-          finish4(a[0], a[1], a[2], a[3], b, load_rq(rq + cb), load_rq(rq + cb + 1),
+          finish4<FAST>(a[0], a[1], a[2], a[3], b, load_rq(rq + cb), load_rq(rq + cb + 1),
                   load_rq(rq + cb + 2), load_rq(rq + cb + 3), g);
     } else {
 #pragma unroll
@@ -446,7 +447,7 @@ __global__ void k_avgpool_s8(const int8_t* __restrict__ in, int8_t* __restrict__
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-template <int KH, int KW, int CI>
+template <int KH, int KW, int CI, bool FAST>
 cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s) {
   const int cob = g.Co <= 8 ? 8 : g.Co <= 16 ? 16 : 32;
@@ -455,16 +456,23 @@ cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, co
     const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
     const dim3 grid((pix + 127) / 128, (g.Co + cob - 1) / cob, nz);
     if (cob == 8)
-      k_small_conv_s8<KH, KW, CI, 8><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff, p.rq,
-                                                          out, g, n0);
+      k_small_conv_s8<KH, KW, CI, 8, FAST><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
+                                                                p.rq, out, g, n0);
     else if (cob == 16)
-      k_small_conv_s8<KH, KW, CI, 16><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff, p.rq,
-                                                           out, g, n0);
+      k_small_conv_s8<KH, KW, CI, 16, FAST><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
+                                                                 p.rq, out, g, n0);
     else
-      k_small_conv_s8<KH, KW, CI, 32><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff, p.rq,
-                                                           out, g, n0);
+      k_small_conv_s8<KH, KW, CI, 32, FAST><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
+                                                                 p.rq, out, g, n0);
   }
   return cudaGetLastError();
+}
+
+template <int KH, int KW, int CI>
+cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
+                           int8_t* out, cudaStream_t s) {
+  if (p.all_fast_known) return small_conv_cob<KH, KW, CI, true>(g, p, batch, in, out, s);
+  return small_conv_cob<KH, KW, CI, false>(g, p, batch, in, out, s);
 }
 
 }  // namespace
@@ -499,10 +507,17 @@ cudaError_t launch_dw3x3(const pspml_op_desc& d, const PreparedOp& p, int64_t ba
     const auto* i32 = reinterpret_cast<const uint32_t*>(in);
     const auto* f32 = reinterpret_cast<const uint32_t*>(p.filter);
     auto* o32 = reinterpret_cast<uint32_t*>(out);
-    if (g.sh == 1)
-      k_dw3x3_s8<1, PX><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
-    else
-      k_dw3x3_s8<2, PX><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+    if (p.all_fast_known) {
+      if (g.sh == 1)
+        k_dw3x3_s8<1, PX, true><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+      else
+        k_dw3x3_s8<2, PX, true><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+    } else {
+      if (g.sh == 1)
+        k_dw3x3_s8<1, PX, false><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+      else
+        k_dw3x3_s8<2, PX, false><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+    }
   }
   return cudaGetLastError();
 }

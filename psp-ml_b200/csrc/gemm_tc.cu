@@ -60,11 +60,22 @@ struct TcGemmArgs {
   const uint8_t* xcls;
   int32_t n_xcls;
   const RqChannel* rq;
+  const int32_t* all_fast;  // -1: every channel has a fast-form requant entry
+  int32_t ncls;             // rows of the folded-bias table
+  int32_t param_smem;       // bytes of requant + bias tables staged in smem (0: read global)
   uint32_t lo4, hi4;    // activation clamp, bytes replicated
   int32_t clamp;        // act range narrower than int8
   unsigned* err;
   int32_t stages;
 };
+
+constexpr int kParamSmemMax = 32 * 1024;
+
+size_t param_smem_bytes(int n, int ncls) {
+  const size_t b = static_cast<size_t>(n) * sizeof(RqChannel) +
+                   (static_cast<size_t>(ncls) * n * 4 + 15) / 16 * 16;
+  return b <= static_cast<size_t>(kParamSmemMax) ? b : 0;
+}
 
 template <int BK>
 struct SwizzleFor;
@@ -113,52 +124,49 @@ __device__ __forceinline__ TileOrigin tile_origin(const TcGemmArgs& p, int64_t t
   return o;
 }
 
-// Requantises 32 accumulators of one output row and stores them.
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int8_t* dst,
+// Requantises 32 accumulators of one output row and stores them.  bias / rq
+// point into shared memory when the tables are staged there, else global.
+template <bool FAST>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int8_t* dst,
                                                const int32_t* bias, const RqChannel* rq, int cnt,
                                                const TcGemmArgs& p) {
-  if (cnt == 32) {
+  if (cnt == 16) {
     const bool bvec = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
-    uint32_t packed[8];
+    uint32_t packed[4];
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
+    for (int g = 0; g < 4; ++g) {
       int4 b4;
       if (bvec) {
-        b4 = __ldg(reinterpret_cast<const int4*>(bias) + g);
+        b4 = reinterpret_cast<const int4*>(bias)[g];
       } else {
-        b4 = make_int4(__ldg(bias + 4 * g), __ldg(bias + 4 * g + 1), __ldg(bias + 4 * g + 2),
-                       __ldg(bias + 4 * g + 3));
+        b4 = make_int4(bias[4 * g], bias[4 * g + 1], bias[4 * g + 2], bias[4 * g + 3]);
       }
-      const int32_t r0 = rq_apply(static_cast<int32_t>(v[4 * g + 0]) + b4.x, load_rq(rq + 4 * g));
-      const int32_t r1 =
-          rq_apply(static_cast<int32_t>(v[4 * g + 1]) + b4.y, load_rq(rq + 4 * g + 1));
-      const int32_t r2 =
-          rq_apply(static_cast<int32_t>(v[4 * g + 2]) + b4.z, load_rq(rq + 4 * g + 2));
-      const int32_t r3 =
-          rq_apply(static_cast<int32_t>(v[4 * g + 3]) + b4.w, load_rq(rq + 4 * g + 3));
+      const RqChannel q0 = rq[4 * g], q1 = rq[4 * g + 1], q2 = rq[4 * g + 2], q3 = rq[4 * g + 3];
+      const int32_t r0 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 0]) + b4.x, q0);
+      const int32_t r1 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 1]) + b4.y, q1);
+      const int32_t r2 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 2]) + b4.z, q2);
+      const int32_t r3 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 3]) + b4.w, q3);
       uint32_t w = pack_sat4(r0, r1, r2, r3);
       if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
       packed[g] = w;
     }
     if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
-      d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     } else if ((reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
       uint32_t* d1 = reinterpret_cast<uint32_t*>(dst);
 #pragma unroll
-      for (int g = 0; g < 8; ++g) d1[g] = packed[g];
+      for (int g = 0; g < 4; ++g) d1[g] = packed[g];
     } else {
 #pragma unroll
-      for (int g = 0; g < 8; ++g)
+      for (int g = 0; g < 4; ++g)
 #pragma unroll
         for (int j = 0; j < 4; ++j) dst[4 * g + j] = static_cast<int8_t>(packed[g] >> (8 * j));
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
       if (j < cnt) {
-        int32_t r = rq_apply(static_cast<int32_t>(v[j]) + __ldg(bias + j), load_rq(rq + j));
+        int32_t r = rq_sel<FAST>(static_cast<int32_t>(v[j]) + bias[j], rq[j]);
         r = max(r, -128);
         r = min(r, 127);
         uint32_t w = static_cast<uint32_t>(r) & 0xFFu;
@@ -169,7 +177,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int8_t* 
   }
 }
 
-template <int BN, int BK>
+template <int BN, int BK, bool FAST_ONLY>
 __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
     k_gemm_s8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const TcGemmArgs p) {
@@ -187,7 +195,10 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
   const int stages = p.stages;
   uint8_t* sA = smem;
   uint8_t* sB = smem + stages * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * B_BYTES);
+  uint8_t* sP = sB + stages * B_BYTES;  // staged requant + bias tables
+  RqChannel* srq = reinterpret_cast<RqChannel*>(sP);
+  int32_t* sbias = reinterpret_cast<int32_t*>(sP + static_cast<size_t>(p.N) * sizeof(RqChannel));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sP + p.param_smem);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + NB;
@@ -218,6 +229,10 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
+  }
+  if (p.param_smem) {
+    for (int i = threadIdx.x; i < p.N; i += blockDim.x) srq[i] = p.rq[i];
+    for (int i = threadIdx.x; i < p.ncls * p.N; i += blockDim.x) sbias[i] = p.bias[i];
   }
   tc_fence_before();
   __syncthreads();
@@ -319,6 +334,9 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
     const int grp = (warp - 2) >> 2;
     const int q = warp & 3;  // tensor-memory lane quarter this warp may read
     const int row = q * 32 + lane;
+    const bool fast = FAST_ONLY || *p.all_fast != 0;
+    const RqChannel* rqb = p.param_smem ? srq : p.rq;
+    const int32_t* bb = p.param_smem ? sbias : p.bias;
     int64_t i = grp;
     for (int64_t t = blockIdx.x + static_cast<int64_t>(grp) * gridDim.x; t < p.tiles_total;
          t += static_cast<int64_t>(G) * gridDim.x, i += G) {
@@ -337,7 +355,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       const int64_t tm = t / p.tiles_n;
       bool valid;
       int8_t* orow;
-      const int32_t* brow = p.bias;
+      const int32_t* brow = bb;
       if (p.conv4d) {
         const TileOrigin o = tile_origin(p, tm);
         const int32_t x = o.x0 + (row & ((1 << p.bw_log2) - 1));
@@ -346,7 +364,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
         valid = x < p.Wo && y < p.Ho && n < p.nimg;
         orow = p.out + ((n * p.Ho + y) * p.Wo + x) * static_cast<int64_t>(p.N);
         if (valid && p.ycls != nullptr)
-          brow = p.bias + static_cast<int64_t>(p.ycls[y] * p.n_xcls + p.xcls[x]) * p.N;
+          brow = bb + static_cast<int64_t>(p.ycls[y] * p.n_xcls + p.xcls[x]) * p.N;
       } else {
         const int64_t r = tm * kBM + row;
         valid = r < p.rows;
@@ -354,14 +372,23 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       }
       const int32_t n0 = tn * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                       static_cast<uint32_t>(b * BN + c),
                   v);
         const int32_t nc = n0 + c;
-        if (valid && nc < p.N)
-          epilogue_chunk(v, orow + nc, brow + nc, p.rq + nc, min(32, p.N - nc), p);
+        if (valid && nc < p.N) {
+          const int cnt = min(16, p.N - nc);
+          if constexpr (FAST_ONLY) {
+            epilogue_chunk<true>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
+          } else {
+            if (fast)
+              epilogue_chunk<true>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
+            else
+              epilogue_chunk<false>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -388,11 +415,11 @@ int pow2_ceil(int v) {
   return p;
 }
 
-template <int BN, int BK>
+template <int BN, int BK, bool FAST_ONLY>
 cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args, int num_sms,
                    cudaStream_t s) {
   constexpr int stage_bytes = kBM * BK + BN * BK;
-  constexpr int overhead = 1024 + 64 * 8 + 64;
+  const int overhead = 1024 + 64 * 8 + 64 + args.param_smem;
   int stages = (kSmemLimit - overhead) / stage_bytes;
   stages = std::min(stages, kMaxStages);
   // At least 120 KB so that a second CTA never shares the SM: the grid is
@@ -404,26 +431,26 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   cudaGetDevice(&dev);
   const uint32_t bit = 1u << (dev & 31);
   if ((attr_set.load() & bit) == 0) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<BN, BK>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<BN, BK, FAST_ONLY>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
   const int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
   if (grid <= 0) return cudaSuccess;
-  k_gemm_s8<BN, BK><<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb,
+  k_gemm_s8<BN, BK, FAST_ONLY><<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb,
                                                                                       args);
   return cudaGetLastError();
 }
 
-template <int BK>
+template <int BK, bool FAST_ONLY>
 cudaError_t run_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
                       const TcGemmArgs& args, int num_sms, cudaStream_t s) {
   switch (bn) {
-    case 32: return run_tc<32, BK>(ma, mb, args, num_sms, s);
-    case 64: return run_tc<64, BK>(ma, mb, args, num_sms, s);
-    case 128: return run_tc<128, BK>(ma, mb, args, num_sms, s);
-    default: return run_tc<256, BK>(ma, mb, args, num_sms, s);
+    case 32: return run_tc<32, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
+    case 64: return run_tc<64, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
+    case 128: return run_tc<128, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
+    default: return run_tc<256, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
   }
 }
 
@@ -454,6 +481,9 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t
   a.xcls = pp.ncls > 1 ? pp.xcls : nullptr;
   a.n_xcls = pp.n_xcls;
   a.rq = pp.rq;
+  a.all_fast = pp.rq_all_fast;
+  a.ncls = pp.ncls;
+  a.param_smem = static_cast<int32_t>(param_smem_bytes(N, pp.ncls));
   a.lo4 = splat4(d.act_min);
   a.hi4 = splat4(d.act_max);
   a.clamp = (d.act_min > -128 || d.act_max < 127) ? 1 : 0;
@@ -509,10 +539,17 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t
     if (encode_tensor_map(&mb, pp.filter, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  if (pp.all_fast_known) {
+    switch (bk) {
+      case 128: return run_tc_bn<128, true>(bn, ma, mb, a, num_sms, s);
+      case 64: return run_tc_bn<64, true>(bn, ma, mb, a, num_sms, s);
+      default: return run_tc_bn<32, true>(bn, ma, mb, a, num_sms, s);
+    }
+  }
   switch (bk) {
-    case 128: return run_tc_bn<128>(bn, ma, mb, a, num_sms, s);
-    case 64: return run_tc_bn<64>(bn, ma, mb, a, num_sms, s);
-    default: return run_tc_bn<32>(bn, ma, mb, a, num_sms, s);
+    case 128: return run_tc_bn<128, false>(bn, ma, mb, a, num_sms, s);
+    case 64: return run_tc_bn<64, false>(bn, ma, mb, a, num_sms, s);
+    default: return run_tc_bn<32, false>(bn, ma, mb, a, num_sms, s);
   }
 }
 

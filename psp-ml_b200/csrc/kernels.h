@@ -48,6 +48,8 @@ struct PreparedOp {
   int32_t nw = 0;
   int32_t* bias_eff = nullptr;      // [ncls][N]: bias - zp_in * (in-image weight sum)
   RqChannel* rq = nullptr;          // [N]
+  int32_t* rq_all_fast = nullptr;   // -1 when every channel has a fast-form entry, else 0
+  bool all_fast_known = false;      // host knows every channel takes the fast form
   uint8_t* ycls = nullptr;          // [out_h] (tensor-core conv with ncls > 1)
   uint8_t* xcls = nullptr;          // [out_w]
   int32_t ncls = 1, n_xcls = 1;
@@ -68,6 +70,10 @@ size_t prepared_bytes(const pspml_op_desc& d, OpPath path);
 cudaError_t prepare_op(const pspml_op_desc& d, OpPath path, const int8_t* filter,
                        const int32_t* bias, const int32_t* mult, const int32_t* shift,
                        uint8_t* mem, PreparedOp* out, cudaStream_t s);
+
+// True when every channel's (multiplier, shift) takes the fast requant form
+// (host copies of the arrays).
+bool host_all_fast(const int32_t* mult, const int32_t* shift, int32_t n);
 
 // Launches op `d` over `batch` samples.
 cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
@@ -97,7 +103,7 @@ cudaError_t launch_avgpool(const pspml_op_desc& d, int64_t batch, const int8_t* 
 cudaError_t launch_fold_bias(const pspml_op_desc& d, const int8_t* filter, const int32_t* bias,
                              const BorderClasses& bc, int32_t* bias_eff, cudaStream_t s);
 cudaError_t launch_build_rq(const int32_t* mult, const int32_t* shift, int32_t zp_out, int32_t n,
-                            RqChannel* rq, cudaStream_t s);
+                            RqChannel* rq, int32_t* all_fast, cudaStream_t s);
 cudaError_t launch_pack_patch_weights(const int8_t* filter, int32_t n, int32_t k, int32_t nw,
                                       uint32_t* out, cudaStream_t s);
 

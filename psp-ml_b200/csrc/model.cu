@@ -228,6 +228,12 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     st = cuda_status(prepare_op(d, op.prep.path, filter, bias, mult, shift,
                                 m->weights + table_off[i], &op.prep, ctx->stream),
                      "op preparation");
+    if (has_weights(d)) {
+      const auto* hb = static_cast<const uint8_t*>(blob);
+      op.prep.all_fast_known =
+          host_all_fast(reinterpret_cast<const int32_t*>(hb + d.mult_off),
+                        reinterpret_cast<const int32_t*>(hb + d.shift_off), d.out_c);
+    }
   }
   if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "model preparation");
 

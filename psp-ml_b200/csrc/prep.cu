@@ -73,9 +73,14 @@ __global__ void k_fold_dw(const int8_t* __restrict__ filter, const int32_t* __re
 }
 
 __global__ void k_build_rq(const int32_t* __restrict__ mult, const int32_t* __restrict__ shift,
-                           int32_t zp_out, int32_t n, RqChannel* __restrict__ rq) {
+                           int32_t zp_out, int32_t n, RqChannel* __restrict__ rq,
+                           int32_t* __restrict__ all_fast) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) rq[i] = make_rq(mult[i], shift[i], zp_out);
+  if (i < n) {
+    const RqChannel q = make_rq(mult[i], shift[i], zp_out);
+    rq[i] = q;
+    if (q.sr < 0) atomicAnd(all_fast, 0);
+  }
 }
 
 // [N][K] int8 -> [N][nw] words, zero padded past K.
@@ -184,30 +189,30 @@ size_t prepared_bytes(const pspml_op_desc& d, OpPath path) {
   switch (path) {
     case OpPath::kTc2d:
       c.take<int32_t>(n * 4);
-      c.take<RqChannel>(n * sizeof(RqChannel));
+      c.take<RqChannel>((n + 1) * sizeof(RqChannel));
       break;
     case OpPath::kTc4d: {
       BorderClasses bc;
       if (!build_border_classes(d, &bc)) return 0;
       c.take<int32_t>(static_cast<size_t>(bc.n_ycls) * bc.n_xcls * n * 4);
-      c.take<RqChannel>(n * sizeof(RqChannel));
+      c.take<RqChannel>((n + 1) * sizeof(RqChannel));
       c.take<uint8_t>(d.out_h);
       c.take<uint8_t>(d.out_w);
       break;
     }
     case OpPath::kSmallConv:
       c.take<int32_t>(n * 4);
-      c.take<RqChannel>(n * sizeof(RqChannel));
+      c.take<RqChannel>((n + 1) * sizeof(RqChannel));
       c.take<uint32_t>(n * small_conv_words(d) * 4);
       break;
     case OpPath::kDw3x3:
       c.take<int32_t>(n * 4);
-      c.take<RqChannel>(n * sizeof(RqChannel));
+      c.take<RqChannel>((n + 1) * sizeof(RqChannel));
       break;
     case OpPath::kDirect:
     case OpPath::kFcWarp:
     case OpPath::kDwGeneric:
-      c.take<RqChannel>(n * sizeof(RqChannel));
+      c.take<RqChannel>((n + 1) * sizeof(RqChannel));
       break;
     default:
       break;
@@ -230,8 +235,9 @@ cudaError_t prepare_op(const pspml_op_desc& d, OpPath path, const int8_t* filter
   BorderClasses* bc = nullptr;
   static thread_local BorderClasses bc_store;
   auto rq_and = [&]() {
-    p.rq = c.take<RqChannel>(static_cast<size_t>(n) * sizeof(RqChannel));
-    return launch_build_rq(mult, shift, d.zp_out, n, p.rq, s);
+    p.rq = c.take<RqChannel>((static_cast<size_t>(n) + 1) * sizeof(RqChannel));
+    p.rq_all_fast = reinterpret_cast<int32_t*>(p.rq + n);
+    return launch_build_rq(mult, shift, d.zp_out, n, p.rq, p.rq_all_fast, s);
   };
   switch (path) {
     case OpPath::kTc2d:
@@ -291,6 +297,12 @@ cudaError_t prepare_op(const pspml_op_desc& d, OpPath path, const int8_t* filter
   return e;
 }
 
+bool host_all_fast(const int32_t* mult, const int32_t* shift, int32_t n) {
+  for (int32_t i = 0; i < n; ++i)
+    if (make_rq(mult[i], shift[i], 0).sr < 0) return false;
+  return true;
+}
+
 cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                       const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                       cudaStream_t s) {
@@ -348,8 +360,10 @@ cudaError_t launch_fold_bias(const pspml_op_desc& d, const int8_t* filter, const
 }
 
 cudaError_t launch_build_rq(const int32_t* mult, const int32_t* shift, int32_t zp_out, int32_t n,
-                            RqChannel* rq, cudaStream_t s) {
-  k_build_rq<<<(n + 127) / 128, 128, 0, s>>>(mult, shift, zp_out, n, rq);
+                            RqChannel* rq, int32_t* all_fast, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(all_fast, 0xFF, sizeof(int32_t), s);
+  if (e != cudaSuccess) return e;
+  k_build_rq<<<(n + 127) / 128, 128, 0, s>>>(mult, shift, zp_out, n, rq, all_fast);
   return cudaGetLastError();
 }
 

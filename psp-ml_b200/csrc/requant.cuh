@@ -48,7 +48,7 @@ __device__ __forceinline__ int32_t mbqm_dev(int32_t x, int32_t m, int32_t shift)
 // |p| < 2^62 and |C| < 2^62 for r <= 23, so t never overflows.
 // Other shifts (left shifts, r == 0, r > 23) take the general path: sr < 0,
 // c_lo holds the TFLite shift and c_hi the output zero point.
-struct RqChannel {
+struct __align__(16) RqChannel {
   int32_t m;
   uint32_t c_lo;
   int32_t c_hi;
@@ -74,17 +74,28 @@ __host__ __device__ inline RqChannel make_rq(int32_t m, int32_t shift, int32_t z
   return q;
 }
 
-// requantised value + zp_out, before clamping.
+// requantised value + zp_out, before clamping: fast form only (q.sr >= 0).
+__device__ __forceinline__ int32_t rq_fast(int32_t a, const RqChannel& q) {
+  const int64_t c =
+      static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi)) << 32) | q.c_lo);
+  const int64_t t = static_cast<int64_t>(a) * q.m + c;
+  const int32_t lo = static_cast<int32_t>(t);
+  const int32_t hi = static_cast<int32_t>(t >> 32);
+  return (hi + ((a & ~lo) >> 31)) >> q.sr;
+}
+
+// requantised value + zp_out, before clamping; any channel.
 __device__ __forceinline__ int32_t rq_apply(int32_t a, const RqChannel& q) {
-  if (q.sr >= 0) {
-    const int64_t c = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi))
-                                            << 32) | q.c_lo);
-    const int64_t t = static_cast<int64_t>(a) * q.m + c;
-    const int32_t lo = static_cast<int32_t>(t);
-    const int32_t hi = static_cast<int32_t>(t >> 32);
-    return (hi + ((a & ~lo) >> 31)) >> q.sr;
-  }
+  if (q.sr >= 0) return rq_fast(a, q);
   return mbqm_dev(a, q.m, static_cast<int32_t>(q.c_lo)) + q.c_hi;
+}
+
+// Requantisation selected at compile time: FAST when every channel of the
+// op has a fast-form table entry (the op's all-fast flag).
+template <bool FAST>
+__device__ __forceinline__ int32_t rq_sel(int32_t a, const RqChannel& q) {
+  if constexpr (FAST) return rq_fast(a, q);
+  return rq_apply(a, q);
 }
 
 __device__ __forceinline__ RqChannel load_rq(const RqChannel* p) {

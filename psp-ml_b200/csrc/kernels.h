@@ -18,6 +18,7 @@ enum class OpPath {
   kSmallConv,  // CUDA-core dp4a conv over packed patches (small in_c)
   kDirect,     // CUDA-core conv, any shape (fallback)
   kFcWarp,     // CUDA-core FC, one warp per output (K % 16 != 0)
+  kDwTc,       // tcgen05 depthwise 3x3 stride 1 (block-diagonal), C % 32 == 0
   kDw3x3,      // CUDA-core dp4a depthwise 3x3, C % 4 == 0
   kDwGeneric,  // CUDA-core depthwise, any shape (fallback)
   kMaxPool,
@@ -57,6 +58,17 @@ struct PreparedOp {
 
 // Input-channel / kernel shapes k_small_conv_s8 is instantiated for.
 bool small_conv_supported(const pspml_op_desc& d);
+
+// Depthwise shapes the tensor-core depthwise kernel takes (dw_tc.cu).
+bool dw_tc_supported(const pspml_op_desc& d);
+// Packs the block-diagonal weights ([C/32][9][2][32][16] bytes, 9216 per
+// group) and folds the per-class bias; masks_dev holds 128 words.
+cudaError_t prepare_dw_tc(const pspml_op_desc& d, const int8_t* filter, const int32_t* bias,
+                          const BorderClasses& bc, uint8_t* wpack, int32_t* bias_eff,
+                          uint32_t* masks_dev, cudaStream_t s);
+cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                         const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                         cudaStream_t s);
 
 // Path for op `d` given operand alignment (16-byte aligned pointers allow the
 // TMA / vector paths).

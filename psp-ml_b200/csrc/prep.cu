@@ -166,6 +166,7 @@ OpPath choose_path(const pspml_op_desc& d, bool aligned16) {
       return OpPath::kDirect;
     }
     case PSPML_OP_DEPTHWISE_CONV2D:
+      if (aligned16 && dw_tc_supported(d)) return OpPath::kDwTc;
       if (d.in_c % 4 == 0 && d.kernel_h == 3 && d.kernel_w == 3 &&
           (d.stride_h == 1 || d.stride_h == 2) && d.stride_w == d.stride_h && aligned16)
         return OpPath::kDw3x3;
@@ -209,6 +210,17 @@ size_t prepared_bytes(const pspml_op_desc& d, OpPath path) {
       c.take<int32_t>(n * 4);
       c.take<RqChannel>((n + 1) * sizeof(RqChannel));
       break;
+    case OpPath::kDwTc: {
+      BorderClasses bc;
+      if (!build_border_classes(d, &bc)) return 0;
+      c.take<int32_t>(static_cast<size_t>(bc.n_ycls) * bc.n_xcls * n * 4);
+      c.take<RqChannel>((n + 1) * sizeof(RqChannel));
+      c.take<uint8_t>(d.out_h);
+      c.take<uint8_t>(d.out_w);
+      c.take<uint8_t>(n / 32 * 9216);
+      c.take<uint32_t>(128 * 4);
+      break;
+    }
     case OpPath::kDirect:
     case OpPath::kFcWarp:
     case OpPath::kDwGeneric:
@@ -277,6 +289,27 @@ cudaError_t prepare_op(const pspml_op_desc& d, OpPath path, const int8_t* filter
       e = launch_fold_bias(d, filter, bias, *bc, p.bias_eff, s);
       break;
     }
+    case OpPath::kDwTc: {
+      if (!build_border_classes(d, &bc_store)) return cudaErrorInvalidValue;
+      bc = &bc_store;
+      p.ncls = bc->n_ycls * bc->n_xcls;
+      p.n_xcls = bc->n_xcls;
+      p.bias_eff = c.take<int32_t>(static_cast<size_t>(p.ncls) * n * 4);
+      if ((e = rq_and()) != cudaSuccess) break;
+      p.ycls = c.take<uint8_t>(d.out_h);
+      p.xcls = c.take<uint8_t>(d.out_w);
+      if ((e = cudaMemcpyAsync(p.ycls, bc->ycls, d.out_h, cudaMemcpyHostToDevice, s)) !=
+          cudaSuccess)
+        break;
+      if ((e = cudaMemcpyAsync(p.xcls, bc->xcls, d.out_w, cudaMemcpyHostToDevice, s)) !=
+          cudaSuccess)
+        break;
+      uint8_t* wp = c.take<uint8_t>(static_cast<size_t>(n) / 32 * 9216);
+      p.wpack = reinterpret_cast<const uint32_t*>(wp);
+      uint32_t* masks = c.take<uint32_t>(128 * 4);
+      e = prepare_dw_tc(d, filter, bias, *bc, wp, p.bias_eff, masks, s);
+      break;
+    }
     case OpPath::kDw3x3: {
       p.bias_eff = c.take<int32_t>(static_cast<size_t>(n) * 4);
       if ((e = rq_and()) != cudaSuccess) break;
@@ -317,6 +350,8 @@ cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch
       return launch_conv_direct(d, p, batch, in, out, s);
     case OpPath::kFcWarp:
       return launch_fc_warp(d, p, batch, in, out, s);
+    case OpPath::kDwTc:
+      return launch_dw_tc(d, p, batch, in, out, dev_err, num_sms, s);
     case OpPath::kDw3x3:
       return launch_dw3x3(d, p, batch, in, out, s);
     case OpPath::kDwGeneric:

@@ -102,6 +102,17 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// Contiguous global -> shared copy completed on `bar` (bytes: multiple of
+// 16, both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // -------------------------------------------------------------- tcgen05
 // Tensor-memory allocation is warp-wide (.sync.aligned).
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

@@ -329,19 +329,22 @@ def run_ours(args, wl, rank, world, local_rank):
                            "bf16_tflops (no int8 measurement)")
 
     # ---- end to end: pinned host buffers through pspml_forward
-    hin = torch.empty(n_local * in_e, dtype=torch.int8).pin_memory()
-    hout = torch.empty(max(1, n_local) * out_e, dtype=torch.int8).pin_memory()
-    hin.copy_(x_dev)
-    torch.cuda.synchronize()
-    e2e_steps = max(1, min(args.steps, 3))
-    model.forward(hin.data_ptr(), hout.data_ptr(), n_local)  # warm the pipeline
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        model.forward(hin.data_ptr(), hout.data_ptr(), n_local)
-    e2e_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
-    e2e = {"value": round(global_batch / e2e_s, 1), "unit": UNIT,
-           "h2d_bytes_per_step": int(n_local * in_e), "d2h_bytes_per_step": int(n_local * out_e)}
+    e2e = None
+    if not args.no_e2e:
+        hin = torch.empty(n_local * in_e, dtype=torch.int8).pin_memory()
+        hout = torch.empty(max(1, n_local) * out_e, dtype=torch.int8).pin_memory()
+        hin.copy_(x_dev)
+        torch.cuda.synchronize()
+        e2e_steps = max(1, min(args.steps, 3))
+        model.forward(hin.data_ptr(), hout.data_ptr(), n_local)  # warm the pipeline
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            model.forward(hin.data_ptr(), hout.data_ptr(), n_local)
+        e2e_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
+        e2e = {"value": round(global_batch / e2e_s, 1), "unit": UNIT,
+               "h2d_bytes_per_step": int(n_local * in_e),
+               "d2h_bytes_per_step": int(n_local * out_e)}
 
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
@@ -386,6 +389,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--micro", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the host-buffer pass (short profiling runs)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -309,7 +309,7 @@ __global__ void k_fold_dw_classes(const int8_t* __restrict__ f, const int32_t* _
 bool dw_tc_supported(const pspml_op_desc& d) {
   return d.kind == PSPML_OP_DEPTHWISE_CONV2D && d.in_c % 32 == 0 && d.kernel_h == 3 &&
          d.kernel_w == 3 && d.stride_h == 1 && d.stride_w == 1 && d.pad_left <= 1 &&
-         d.out_w <= 65535 && d.out_h <= 4096;
+         d.out_w >= 128 && d.out_w <= 65535 && d.out_h <= 4096;
 }
 
 size_t dw_tc_param_smem(int ncls) {

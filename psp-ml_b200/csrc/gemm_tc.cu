@@ -177,10 +177,58 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int8_t* 
   }
 }
 
-template <int BN, int BK, bool FAST_ONLY>
+struct NoTable {
+  int32_t unused;
+};
+
+// Constant-table version of epilogue_chunk (fast requant only): every
+// per-channel read indexes the kernel-parameter table directly.
+__device__ __forceinline__ void epilogue_chunk_tab(const uint32_t (&v)[16], int8_t* dst,
+                                                   const EpiTable& tab, int bias_off, int nc,
+                                                   int cnt, const TcGemmArgs& p) {
+  if (cnt == 16) {
+    uint32_t packed[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      int32_t r[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int ch = nc + 4 * g + k;
+        r[k] = rq_fast(static_cast<int32_t>(v[4 * g + k]) + tab.bias[bias_off + ch], tab.rq[ch]);
+      }
+      uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
+      if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
+      packed[g] = w;
+    }
+    if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    } else {
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[4 * g + j] = static_cast<int8_t>(packed[g] >> (8 * j));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j < cnt) {
+        int32_t r = rq_fast(static_cast<int32_t>(v[j]) + tab.bias[bias_off + nc + j],
+                            tab.rq[nc + j]);
+        r = max(r, -128);
+        r = min(r, 127);
+        uint32_t w = static_cast<uint32_t>(r) & 0xFFu;
+        if (p.clamp) w = clamp4(w * 0x01010101u, p.lo4, p.hi4) & 0xFFu;
+        dst[j] = static_cast<int8_t>(w);
+      }
+    }
+  }
+}
+
+template <int BN, int BK, bool FAST_ONLY, class Tab>
 __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
     k_gemm_s8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const TcGemmArgs p) {
+              const TcGemmArgs p, const __grid_constant__ Tab tab) {
+  constexpr bool kTab = sizeof(Tab) == sizeof(EpiTable);
   constexpr int A_BYTES = kBM * BK;
   constexpr int B_BYTES = BN * BK;
   constexpr uint32_t kLayout = SwizzleFor<BK>::kLayout;
@@ -356,6 +404,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       bool valid;
       int8_t* orow;
       const int32_t* brow = bb;
+      int cls_off = 0;
       if (p.conv4d) {
         const TileOrigin o = tile_origin(p, tm);
         const int32_t x = o.x0 + (row & ((1 << p.bw_log2) - 1));
@@ -363,8 +412,10 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
         const int64_t n = o.n0 + (row >> (p.bw_log2 + p.bh_log2));
         valid = x < p.Wo && y < p.Ho && n < p.nimg;
         orow = p.out + ((n * p.Ho + y) * p.Wo + x) * static_cast<int64_t>(p.N);
-        if (valid && p.ycls != nullptr)
-          brow = bb + static_cast<int64_t>(p.ycls[y] * p.n_xcls + p.xcls[x]) * p.N;
+        if (valid && p.ycls != nullptr) {
+          cls_off = (p.ycls[y] * p.n_xcls + p.xcls[x]) * p.N;
+          brow = bb + cls_off;
+        }
       } else {
         const int64_t r = tm * kBM + row;
         valid = r < p.rows;
@@ -380,7 +431,9 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
         const int32_t nc = n0 + c;
         if (valid && nc < p.N) {
           const int cnt = min(16, p.N - nc);
-          if constexpr (FAST_ONLY) {
+          if constexpr (kTab) {
+            epilogue_chunk_tab(v, orow + nc, tab, cls_off, nc, cnt, p);
+          } else if constexpr (FAST_ONLY) {
             epilogue_chunk<true>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
           } else {
             if (fast)
@@ -415,10 +468,14 @@ int pow2_ceil(int v) {
   return p;
 }
 
-template <int BN, int BK, bool FAST_ONLY>
-cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args, int num_sms,
-                   cudaStream_t s) {
+// Two variants per tile shape: the constant-table epilogue (fast requant,
+// tables as a kernel parameter) when the host holds a table for the op, and
+// the general one (tables in smem or global, runtime fast/slow flag).
+template <int BN, int BK>
+cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args,
+                   const EpiTable* table, int num_sms, cudaStream_t s) {
   constexpr int stage_bytes = kBM * BK + BN * BK;
+  if (table != nullptr) args.param_smem = 0;
   const int overhead = 1024 + 64 * 8 + 64 + args.param_smem;
   int stages = (kSmemLimit - overhead) / stage_bytes;
   stages = std::min(stages, kMaxStages);
@@ -429,28 +486,38 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   static std::atomic<uint32_t> attr_set{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint32_t bit = 1u << (dev & 31);
+  const uint32_t bit = (table != nullptr ? 2u : 1u) << (2 * (dev & 15));
   if ((attr_set.load() & bit) == 0) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<BN, BK, FAST_ONLY>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    cudaError_t e =
+        table != nullptr
+            ? cudaFuncSetAttribute(k_gemm_s8<BN, BK, true, EpiTable>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit)
+            : cudaFuncSetAttribute(k_gemm_s8<BN, BK, false, NoTable>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
   const int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
   if (grid <= 0) return cudaSuccess;
-  k_gemm_s8<BN, BK, FAST_ONLY><<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb,
-                                                                                      args);
+  if (table != nullptr)
+    k_gemm_s8<BN, BK, true, EpiTable>
+        <<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb, args, *table);
+  else
+    k_gemm_s8<BN, BK, false, NoTable>
+        <<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb, args,
+                                                                         NoTable{0});
   return cudaGetLastError();
 }
 
-template <int BK, bool FAST_ONLY>
+template <int BK>
 cudaError_t run_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
-                      const TcGemmArgs& args, int num_sms, cudaStream_t s) {
+                      const TcGemmArgs& args, const EpiTable* table, int num_sms,
+                      cudaStream_t s) {
   switch (bn) {
-    case 32: return run_tc<32, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
-    case 64: return run_tc<64, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
-    case 128: return run_tc<128, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
-    default: return run_tc<256, BK, FAST_ONLY>(ma, mb, args, num_sms, s);
+    case 32: return run_tc<32, BK>(ma, mb, args, table, num_sms, s);
+    case 64: return run_tc<64, BK>(ma, mb, args, table, num_sms, s);
+    case 128: return run_tc<128, BK>(ma, mb, args, table, num_sms, s);
+    default: return run_tc<256, BK>(ma, mb, args, table, num_sms, s);
   }
 }
 
@@ -539,17 +606,11 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t
     if (encode_tensor_map(&mb, pp.filter, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  if (pp.all_fast_known) {
-    switch (bk) {
-      case 128: return run_tc_bn<128, true>(bn, ma, mb, a, num_sms, s);
-      case 64: return run_tc_bn<64, true>(bn, ma, mb, a, num_sms, s);
-      default: return run_tc_bn<32, true>(bn, ma, mb, a, num_sms, s);
-    }
-  }
+  const EpiTable* table = pp.all_fast_known ? pp.table : nullptr;
   switch (bk) {
-    case 128: return run_tc_bn<128, false>(bn, ma, mb, a, num_sms, s);
-    case 64: return run_tc_bn<64, false>(bn, ma, mb, a, num_sms, s);
-    default: return run_tc_bn<32, false>(bn, ma, mb, a, num_sms, s);
+    case 128: return run_tc_bn<128>(bn, ma, mb, a, table, num_sms, s);
+    case 64: return run_tc_bn<64>(bn, ma, mb, a, table, num_sms, s);
+    default: return run_tc_bn<32>(bn, ma, mb, a, table, num_sms, s);
   }
 }
 

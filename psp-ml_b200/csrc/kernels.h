@@ -38,8 +38,21 @@ struct BorderClasses {
 };
 bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc);
 
+// Requantisation constants and folded biases of one op passed to the GEMM
+// kernel as a __grid_constant__ parameter: the epilogue's per-channel
+// reads are warp-uniform, and the constant bank serves them without
+// occupying the L1 data pipe (staging them in shared memory made that pipe
+// the bottleneck: every lane reloads the same 20 bytes per output).
+constexpr int kTabRq = 512;
+constexpr int kTabBias = 2560;
+struct EpiTable {
+  RqChannel rq[kTabRq];
+  int32_t bias[kTabBias];  // [ncls][N]
+};
+
 // Everything a kernel needs beyond the activations, on the device.
 struct PreparedOp {
+  const EpiTable* table = nullptr;  // host copy for the constant-table epilogue (or null)
   OpPath path = OpPath::kDirect;
   const int8_t* filter = nullptr;   // TFLite-layout filter
   const int32_t* bias = nullptr;    // raw bias (fallback kernels)

@@ -236,6 +236,25 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     }
   }
   if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "model preparation");
+  // Host copies of the requant / folded-bias tables for the tensor-core ops
+  // whose tables fit a kernel parameter.
+  for (int i = 0; i < n_ops && !st; ++i) {
+    PreparedOp& p = m->ops[i].prep;
+    const int n = m->ops[i].d.out_c;
+    const bool tc = p.path == OpPath::kTc2d || p.path == OpPath::kTc4d;
+    if (!tc || !p.all_fast_known || n > kTabRq || p.ncls * n > kTabBias) continue;
+    auto t = std::make_unique<EpiTable>();
+    std::memset(t.get(), 0, sizeof(EpiTable));
+    st = cuda_status(cudaMemcpy(t->rq, p.rq, static_cast<size_t>(n) * sizeof(RqChannel),
+                                cudaMemcpyDeviceToHost),
+                     "table copy");
+    if (!st)
+      st = cuda_status(cudaMemcpy(t->bias, p.bias_eff, static_cast<size_t>(p.ncls) * n * 4,
+                                  cudaMemcpyDeviceToHost),
+                       "table copy");
+    p.table = t.get();
+    m->tables.push_back(std::move(t));
+  }
 
   // Arena: op i's output lives from op i until the last op reading it
   // (reshapes alias their input, extending its life).  Greedy first fit by

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -61,5 +62,6 @@ struct pspml_model {
   cudaEvent_t ev_in_ready[2] = {}, ev_in_free[2] = {}, ev_out_ready[2] = {}, ev_out_free[2] = {};
   cudaEvent_t ev_done = nullptr;
   std::vector<cudaEvent_t> op_events;
+  std::vector<std::unique_ptr<pspml::EpiTable>> tables;  // constant-table epilogues
   std::mutex mu;
 };

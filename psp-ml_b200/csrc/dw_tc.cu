@@ -80,9 +80,36 @@ __device__ __forceinline__ void dw_epilogue16(const uint32_t (&v)[16], int8_t* d
   *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
 
-template <bool FAST_ONLY>
+struct NoTab {
+  int32_t unused;
+};
+
+// Constant-table epilogue: the CTA's channel group is fixed, so the
+// per-channel reads are warp-uniform constant-bank loads.
+__device__ __forceinline__ void dw_epilogue16_tab(const uint32_t (&v)[16], int8_t* dst,
+                                                  const EpiTable& tab, int bias_off, int ch0,
+                                                  const DwTcArgs& p) {
+  uint32_t packed[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    int32_t r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int ch = ch0 + 4 * g + k;
+      r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]), tab.mh[ch], tab.bs[bias_off + ch]);
+    }
+    uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
+    if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
+    packed[g] = w;
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
+template <bool FAST_ONLY, class Tab>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_dw_tc_s8(const __grid_constant__ CUtensorMap tmIn, const DwTcArgs p) {
+    k_dw_tc_s8(const __grid_constant__ CUtensorMap tmIn, const DwTcArgs p,
+               const __grid_constant__ Tab tab) {
+  constexpr bool kTab = sizeof(Tab) == sizeof(EpiTable);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -249,10 +276,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                       static_cast<uint32_t>(b * 32 + c),
                   v);
         if (valid) {
-          if (fast)
-            dw_epilogue16<true>(v, orow + c, brow + c, srq + c, p);
-          else
-            dw_epilogue16<false>(v, orow + c, brow + c, srq + c, p);
+          if constexpr (kTab) {
+            dw_epilogue16_tab(v, orow + c, tab, cls * p.C, c0 + c, p);
+          } else {
+            if (fast)
+              dw_epilogue16<true>(v, orow + c, brow + c, srq + c, p);
+            else
+              dw_epilogue16<false>(v, orow + c, brow + c, srq + c, p);
+          }
         }
       }
       tc_fence_before();
@@ -382,24 +413,33 @@ cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t b
 
   const int per = std::max(1, num_sms / a.n_groups);
   const int grid = a.n_groups * per;
+  // Variants: constant-table epilogue (fast requant, tables as a kernel
+  // parameter), fast requant from smem tables, general requant.
+  const int variant = (pp.all_fast_known && pp.table != nullptr) ? 2 : pp.all_fast_known ? 1 : 0;
   static std::atomic<uint32_t> attr_set{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint32_t bit = (pp.all_fast_known ? 2u : 1u) << (2 * (dev & 15));
+  const uint32_t bit = (1u << variant) << (3 * (dev & 7));
   if ((attr_set.load() & bit) == 0) {
-    cudaError_t e =
-        pp.all_fast_known
-            ? cudaFuncSetAttribute(k_dw_tc_s8<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   kSmemLimit)
-            : cudaFuncSetAttribute(k_dw_tc_s8<false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    cudaError_t e = cudaSuccess;
+    if (variant == 2)
+      e = cudaFuncSetAttribute(k_dw_tc_s8<true, EpiTable>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    else if (variant == 1)
+      e = cudaFuncSetAttribute(k_dw_tc_s8<true, NoTab>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    else
+      e = cudaFuncSetAttribute(k_dw_tc_s8<false, NoTab>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
-  if (pp.all_fast_known)
-    k_dw_tc_s8<true><<<grid, kThreads, smem, s>>>(m, a);
+  if (variant == 2)
+    k_dw_tc_s8<true, EpiTable><<<grid, kThreads, smem, s>>>(m, a, *pp.table);
+  else if (variant == 1)
+    k_dw_tc_s8<true, NoTab><<<grid, kThreads, smem, s>>>(m, a, NoTab{0});
   else
-    k_dw_tc_s8<false><<<grid, kThreads, smem, s>>>(m, a);
+    k_dw_tc_s8<false, NoTab><<<grid, kThreads, smem, s>>>(m, a, NoTab{0});
   return cudaGetLastError();
 }
 

@@ -194,7 +194,7 @@ __device__ __forceinline__ void epilogue_chunk_tab(const uint32_t (&v)[16], int8
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int ch = nc + 4 * g + k;
-        r[k] = rq_fast(static_cast<int32_t>(v[4 * g + k]) + tab.bias[bias_off + ch], tab.rq[ch]);
+        r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]), tab.mh[ch], tab.bs[bias_off + ch]);
       }
       uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
       if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
@@ -212,8 +212,7 @@ __device__ __forceinline__ void epilogue_chunk_tab(const uint32_t (&v)[16], int8
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       if (j < cnt) {
-        int32_t r = rq_fast(static_cast<int32_t>(v[j]) + tab.bias[bias_off + nc + j],
-                            tab.rq[nc + j]);
+        int32_t r = rq_tab(static_cast<int32_t>(v[j]), tab.mh[nc + j], tab.bs[bias_off + nc + j]);
         r = max(r, -128);
         r = min(r, 127);
         uint32_t w = static_cast<uint32_t>(r) & 0xFFu;

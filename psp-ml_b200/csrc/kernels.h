@@ -43,12 +43,28 @@ bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc);
 // reads are warp-uniform, and the constant bank serves them without
 // occupying the L1 data pipe (staging them in shared memory made that pipe
 // the bottleneck: every lane reloads the same 20 bytes per output).
+// Two 64-bit constant loads per output: {M, C_hi} per channel and
+// {bias, shift} per (border class, channel).  The low word of C is 2^30 for
+// every channel whose right shift is >= 2, which the host checks before it
+// builds a table.
 constexpr int kTabRq = 512;
 constexpr int kTabBias = 2560;
 struct EpiTable {
-  RqChannel rq[kTabRq];
-  int32_t bias[kTabBias];  // [ncls][N]
+  int2 mh[kTabRq];    // {M, high word of C - 2^32}
+  int2 bs[kTabBias];  // [ncls][N] {folded bias, right shift - 1}
 };
+
+// Fast requant with the table's split constants (C low word = 2^30).
+__device__ __forceinline__ int32_t rq_tab(int32_t acc, const int2 mh, const int2 bs) {
+  const int32_t a = acc + bs.x;
+  const int64_t c =
+      static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(mh.y)) << 32) |
+                           0x40000000u);
+  const int64_t t = static_cast<int64_t>(a) * mh.x + c;
+  const uint32_t lo = static_cast<uint32_t>(t);
+  const int32_t hi = static_cast<int32_t>(t >> 32);
+  return (hi + static_cast<int32_t>((~static_cast<uint32_t>(a) | lo) >> 31)) >> bs.y;
+}
 
 // Everything a kernel needs beyond the activations, on the device.
 struct PreparedOp {

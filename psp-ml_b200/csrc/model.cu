@@ -241,17 +241,28 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
   for (int i = 0; i < n_ops && !st; ++i) {
     PreparedOp& p = m->ops[i].prep;
     const int n = m->ops[i].d.out_c;
-    const bool tc = p.path == OpPath::kTc2d || p.path == OpPath::kTc4d;
+    const bool tc =
+        p.path == OpPath::kTc2d || p.path == OpPath::kTc4d || p.path == OpPath::kDwTc;
     if (!tc || !p.all_fast_known || n > kTabRq || p.ncls * n > kTabBias) continue;
-    auto t = std::make_unique<EpiTable>();
-    std::memset(t.get(), 0, sizeof(EpiTable));
-    st = cuda_status(cudaMemcpy(t->rq, p.rq, static_cast<size_t>(n) * sizeof(RqChannel),
+    std::vector<RqChannel> rq(n);
+    std::vector<int32_t> bias(static_cast<size_t>(p.ncls) * n);
+    st = cuda_status(cudaMemcpy(rq.data(), p.rq, static_cast<size_t>(n) * sizeof(RqChannel),
                                 cudaMemcpyDeviceToHost),
                      "table copy");
     if (!st)
-      st = cuda_status(cudaMemcpy(t->bias, p.bias_eff, static_cast<size_t>(p.ncls) * n * 4,
+      st = cuda_status(cudaMemcpy(bias.data(), p.bias_eff, bias.size() * 4,
                                   cudaMemcpyDeviceToHost),
                        "table copy");
+    if (st) break;
+    bool low_word_fixed = true;  // every channel's C low word is 2^30 (right shift >= 2)
+    for (const RqChannel& q : rq) low_word_fixed = low_word_fixed && q.c_lo == 0x40000000u;
+    if (!low_word_fixed) continue;
+    auto t = std::make_unique<EpiTable>();
+    std::memset(t.get(), 0, sizeof(EpiTable));
+    for (int c = 0; c < n; ++c) t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
+    for (int k = 0; k < p.ncls; ++k)
+      for (int c = 0; c < n; ++c)
+        t->bs[k * n + c] = make_int2(bias[static_cast<size_t>(k) * n + c], rq[c].sr);
     p.table = t.get();
     m->tables.push_back(std::move(t));
   }

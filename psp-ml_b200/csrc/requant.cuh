@@ -46,6 +46,9 @@ __device__ __forceinline__ int32_t mbqm_dev(int32_t x, int32_t m, int32_t shift)
 // exactly when a < 0 and lo < 2^31, so
 //   out + zp_out = (hi + ((a & ~lo) >> 31)) >> (r - 1).
 // |p| < 2^62 and |C| < 2^62 for r <= 23, so t never overflows.
+// The table stores C - 2^32 (one less in the high word); with t' = p + C - 2^32
+// the same result is (hi' + ((~a | lo) >>> 31)) >> (r - 1), because
+// 1 - ([a < 0] & ~lo[31]) = (~a | lo)[31]: one LOP3 and one shifted add.
 // Other shifts (left shifts, r == 0, r > 23) take the general path: sr < 0,
 // c_lo holds the TFLite shift and c_hi the output zero point.
 struct __align__(16) RqChannel {
@@ -60,7 +63,8 @@ __host__ __device__ inline RqChannel make_rq(int32_t m, int32_t shift, int32_t z
   const int32_t r = -shift;
   if (m > 0 && r >= 1 && r <= 23) {
     const int64_t c = (int64_t{1} << 30) + (int64_t{1} << (30 + r)) +
-                      static_cast<int64_t>(zp_out) * (int64_t{1} << (31 + r));
+                      static_cast<int64_t>(zp_out) * (int64_t{1} << (31 + r)) -
+                      (int64_t{1} << 32);
     q.m = m;
     q.c_lo = static_cast<uint32_t>(static_cast<uint64_t>(c));
     q.c_hi = static_cast<int32_t>(c >> 32);
@@ -79,9 +83,9 @@ __device__ __forceinline__ int32_t rq_fast(int32_t a, const RqChannel& q) {
   const int64_t c =
       static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi)) << 32) | q.c_lo);
   const int64_t t = static_cast<int64_t>(a) * q.m + c;
-  const int32_t lo = static_cast<int32_t>(t);
+  const uint32_t lo = static_cast<uint32_t>(t);
   const int32_t hi = static_cast<int32_t>(t >> 32);
-  return (hi + ((a & ~lo) >> 31)) >> q.sr;
+  return (hi + static_cast<int32_t>((~static_cast<uint32_t>(a) | lo) >> 31)) >> q.sr;
 }
 
 // requantised value + zp_out, before clamping; any channel.

@@ -44,3 +44,27 @@ def test_closed_form_exact_halves():
             for m in (1 << 30, (1 << 30) + 1, (1 << 31) - 1):
                 for zp in (-128, 0, 127):
                     assert closed_form(a, m, r, zp) == orc.mbqm(a, m, -r) + zp
+
+
+def closed_form_predecremented(a: int, m: int, r: int, zp: int) -> int:
+    """The form the device evaluates: C - 2^32 in the table and
+    hi' + ((~a | lo) >>> 31)."""
+    c = (1 << 30) + (1 << (30 + r)) + zp * (1 << (31 + r)) - (1 << 32)
+    t = (a * m + c) & U64
+    lo = t & 0xFFFFFFFF
+    hi = t >> 32
+    if hi >= 1 << 31:
+        hi -= 1 << 32
+    bit = ((~a & 0xFFFFFFFF) | lo) >> 31
+    return (hi + bit) >> (r - 1)
+
+
+def test_predecremented_form_matches_tflite_definition():
+    rng = random.Random(5)
+    edges = [0, 1, -1, 2, -2, (1 << 31) - 1, -(1 << 31), 1 << 30, -(1 << 30)]
+    for it in range(60000):
+        m = rng.choice([1 << 30, (1 << 31) - 1, rng.randint(1 << 30, (1 << 31) - 1)])
+        r = rng.randint(1, 23)
+        zp = rng.randint(-128, 127)
+        a = rng.choice(edges) if it % 4 == 0 else rng.randint(-(1 << 31), (1 << 31) - 1)
+        assert closed_form_predecremented(a, m, r, zp) == orc.mbqm(a, m, -r) + zp, (a, m, r, zp)

@@ -160,6 +160,29 @@ int pspml_fully_connected_s8(pspml_ctx* ctx, const pspml_op_desc* d,
                              const int32_t* mult, const int32_t* shift,
                              int8_t* out, void* stream);
 
+/* pspml_fully_connected_s8 for callers that cannot allocate device memory
+ * (no counterpart in the reference): code running under CUDA graph capture,
+ * where cudaMalloc is not allowed; hosts whose device memory budget is fixed
+ * at start-up; callers that pass only buffers they already own.  It takes no
+ * context and allocates nothing: its scratch (folded biases, requantisation
+ * table, error word) is a fixed 256 KiB array inside the library, held on
+ * every device that loads the library until the process exits.
+ *  - Ops needing more scratch than that (more than about 13000 output
+ *    channels) are rejected with PSPML_ERR_INVALID_ARG and a message.
+ *  - The first call on a device looks up the array's device address and
+ *    clears the error word (a synchronous memset); make that first call
+ *    before any stream capture begins.
+ *  - All calls on a device share the one array: calls whose GPU work
+ *    overlaps (different streams, or host threads without ordering) race
+ *    and may produce wrong results.  Order them on one stream.
+ * Arguments and results are those of pspml_fully_connected_s8 (device
+ * pointers, asynchronous on `stream`). */
+int pspml_fully_connected_s8_noalloc(const pspml_op_desc* d, int64_t batch,
+                                     const int8_t* in, const int8_t* filter,
+                                     const int32_t* bias, const int32_t* mult,
+                                     const int32_t* shift, int8_t* out,
+                                     void* stream);
+
 /* Replaces naive::max_pool2d (naive.rs:98-132); any window and stride. */
 int pspml_max_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
                         const int8_t* in, int8_t* out, void* stream);

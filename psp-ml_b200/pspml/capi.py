@@ -91,6 +91,8 @@ _PROTOS = {
                                   [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "pspml_fully_connected_s8": (ctypes.c_int,
                                  [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "pspml_fully_connected_s8_noalloc": (ctypes.c_int,
+                                         [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "pspml_max_pool2d_s8": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
     "pspml_average_pool2d_s8": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
     "pspml_model_create": (ctypes.c_int, [_vp, _vp, _i32, _vp, _sz, _i32, ctypes.POINTER(_vp)]),

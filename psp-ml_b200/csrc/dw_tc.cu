@@ -39,7 +39,8 @@ constexpr int kSmemLimit = 232448;
 
 struct DwTcArgs {
   int32_t n_groups;
-  int64_t tiles_per_group;
+  int64_t tiles_per_group;  // below 2^31 (the host splits larger batches)
+  FastDiv fd_tiles_x, fd_ho;
   int32_t tiles_x, Ho, Wo, C;
   int32_t pad_t, pad_l;
   const uint8_t* wpack;    // [groups][9][2][32][16]
@@ -47,7 +48,7 @@ struct DwTcArgs {
   const int32_t* bias;     // [ncls][C]
   const uint8_t* ycls;
   const uint8_t* xcls;
-  int32_t n_xcls, ncls;
+  int32_t n_xcls, ncls, base_cls;
   const RqChannel* rq;
   uint32_t lo4, hi4;
   int32_t clamp;
@@ -84,32 +85,63 @@ struct NoTab {
   int32_t unused;
 };
 
-// Constant-table epilogue: the CTA's channel group is fixed, so the
-// per-channel reads are warp-uniform constant-bank loads.
-__device__ __forceinline__ void dw_epilogue16_tab(const uint32_t (&v)[16], int8_t* dst,
-                                                  const EpiTable& tab, int bias_off, int ch0,
-                                                  const DwTcArgs& p) {
-  uint32_t packed[4];
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    int32_t r[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int ch = ch0 + 4 * g + k;
-      r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]), tab.mh[ch], tab.bs[bias_off + ch]);
-    }
-    uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
-    if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
-    packed[g] = w;
+// Epilogue variants of k_dw_tc_s8.
+enum : int {
+  kDwGeneral = 0,  // general requant, tables staged in smem
+  kDwFast = 1,     // fast requant, tables staged in smem
+  kDwStatic = 2    // fast requant, tables a kernel parameter read at
+                   // compile-time offsets (one code path per channel group)
+};
+template <int MODE>
+struct DwTabOf {
+  using type = NoTab;
+};
+template <>
+struct DwTabOf<kDwStatic> {
+  using type = EpiTable;
+};
+constexpr int kDwStaticGroups = 4;  // channel groups with a compile-time path
+
+// One tile row of channel group GRP: 32 accumulators from tensor memory,
+// border-class bias difference if any, requant, one 32-byte store.
+template <int GRP, bool CLAMP>
+__device__ __forceinline__ void dw_row_static(const EpiTable& tab, uint32_t taddr, int8_t* dst,
+                                              bool valid, bool border, int cls_off,
+                                              const DwTcArgs& p) {
+  constexpr int c0 = GRP * 32;
+  uint32_t v0[16], v1[16];
+  tmem_ld16_nowait(taddr, v0);
+  tmem_ld16_nowait(taddr + 16, v1);
+  tmem_wait_ld(v0);
+  tmem_wait_ld(v1);
+  if (border) {
+    add_class_delta(v0, tab, cls_off + c0, 16);
+    add_class_delta(v1, tab, cls_off + c0 + 16, 16);
   }
-  *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  const uint4 w0 = requant16_tab<CLAMP>(v0, tab, c0, p.lo4, p.hi4);
+  const uint4 w1 = requant16_tab<CLAMP>(v1, tab, c0 + 16, p.lo4, p.hi4);
+  if (valid) {
+    reinterpret_cast<uint4*>(dst)[0] = w0;
+    reinterpret_cast<uint4*>(dst)[1] = w1;
+  }
 }
 
-template <bool FAST_ONLY, class Tab>
+template <bool CLAMP>
+__device__ __forceinline__ void dw_row_static_any(int grp_ch, const EpiTable& tab,
+                                                  uint32_t taddr, int8_t* dst, bool valid,
+                                                  bool border, int cls_off, const DwTcArgs& p) {
+  switch (grp_ch) {
+    case 0: dw_row_static<0, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
+    case 1: dw_row_static<1, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
+    case 2: dw_row_static<2, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
+    default: dw_row_static<3, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
+  }
+}
+
+template <int MODE, bool CLAMP>
 __global__ void __launch_bounds__(kThreads, 1)
     k_dw_tc_s8(const __grid_constant__ CUtensorMap tmIn, const DwTcArgs p,
-               const __grid_constant__ Tab tab) {
-  constexpr bool kTab = sizeof(Tab) == sizeof(EpiTable);
+               const __grid_constant__ typename DwTabOf<MODE>::type tab) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -173,10 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int64_t t = slot; t < p.tiles_per_group; t += nslots) {
-        const int tx = static_cast<int>(t % p.tiles_x);
-        const int64_t rest = t / p.tiles_x;
-        const int y = static_cast<int>(rest % p.Ho);
-        const int n = static_cast<int>(rest / p.Ho);
+        const uint32_t rest = p.fd_tiles_x.div(static_cast<uint32_t>(t));
+        const int tx = static_cast<int>(static_cast<uint32_t>(t) - rest * p.tiles_x);
+        const uint32_t n = p.fd_ho.div(rest);
+        const int y = static_cast<int>(rest - n * p.Ho);
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
           dw_record_error(p.err, abort_flag, kDevErrTmaWait);
           ok = false;
@@ -189,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int h = 0; h < 2; ++h)
             tma_load_4d(a + (ky * 2 + h) * kRegion, &tmIn, &full[s], c0 + h * 16,
-                        tx * 128 - p.pad_l, y - p.pad_t + ky, n);
+                        tx * 128 - p.pad_l, y - p.pad_t + ky, static_cast<int>(n));
         ++issued;
         if (++s == stages) {
           s = 0;
@@ -246,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int grp = (warp - 2) >> 2;
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const bool fast = FAST_ONLY;
+    const uint32_t tlane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     int64_t i = grp;
     for (int64_t t = slot + static_cast<int64_t>(grp) * nslots; t < p.tiles_per_group;
          t += static_cast<int64_t>(kG) * nslots, i += kG) {
@@ -260,26 +292,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
       if (!ready) break;
       tc_fence_after();
-      const int tx = static_cast<int>(t % p.tiles_x);
-      const int64_t rest = t / p.tiles_x;
-      const int y = static_cast<int>(rest % p.Ho);
-      const int64_t n = rest / p.Ho;
+      const uint32_t rest = p.fd_tiles_x.div(static_cast<uint32_t>(t));
+      const int tx = static_cast<int>(static_cast<uint32_t>(t) - rest * p.tiles_x);
+      const uint32_t n = p.fd_ho.div(rest);
+      const int y = static_cast<int>(rest - n * p.Ho);
       const int x = tx * 128 + row;
       const bool valid = x < p.Wo;
-      int8_t* orow = p.out + ((n * p.Ho + y) * static_cast<int64_t>(p.Wo) + x) * p.C + c0;
+      int8_t* orow = p.out + (static_cast<int64_t>(rest) * p.Wo + x) * p.C + c0;
       const int cls = valid ? p.ycls[y] * p.n_xcls + p.xcls[x] : 0;
-      const int32_t* brow = sbias + cls * 32;
+      const uint32_t tb = tlane + static_cast<uint32_t>(b * 32);
+      if constexpr (MODE == kDwStatic) {
+        dw_row_static_any<CLAMP>(grp_ch, tab, tb, orow, valid, cls != p.base_cls, cls * p.C, p);
+      } else {
+        const int32_t* brow = sbias + cls * 32;
 #pragma unroll
-      for (int c = 0; c < 32; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(b * 32 + c),
-                  v);
-        if (valid) {
-          if constexpr (kTab) {
-            dw_epilogue16_tab(v, orow + c, tab, cls * p.C, c0 + c, p);
-          } else {
-            if (fast)
+        for (int c = 0; c < 32; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(tb + static_cast<uint32_t>(c), v);
+          if (valid) {
+            if constexpr (MODE == kDwFast)
               dw_epilogue16<true>(v, orow + c, brow + c, srq + c, p);
             else
               dw_epilogue16<false>(v, orow + c, brow + c, srq + c, p);
@@ -368,9 +399,29 @@ cudaError_t prepare_dw_tc(const pspml_op_desc& d, const int8_t* filter, const in
   return cudaGetLastError();
 }
 
-cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
-                         const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
-                         cudaStream_t s) {
+namespace {
+
+template <int MODE, bool CLAMP>
+cudaError_t launch_dw_variant(const CUtensorMap& m, const DwTcArgs& a,
+                              const typename DwTabOf<MODE>::type& tab, int grid, int smem,
+                              cudaStream_t s) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((done.load() & bit) == 0) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        k_dw_tc_s8<MODE, CLAMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return e;
+    done.fetch_or(bit);
+  }
+  k_dw_tc_s8<MODE, CLAMP><<<grid, kThreads, smem, s>>>(m, a, tab);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dw_tc_once(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
+                              const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                              cudaStream_t s) {
   const int C = d.in_c;
   DwTcArgs a{};
   a.n_groups = C / 32;
@@ -381,6 +432,9 @@ cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t b
   a.pad_t = d.pad_top;
   a.pad_l = d.pad_left;
   a.tiles_per_group = batch * d.out_h * a.tiles_x;
+  if (a.tiles_per_group >= (1ll << 31)) return cudaErrorInvalidValue;
+  a.fd_tiles_x = FastDiv(static_cast<uint32_t>(a.tiles_x));
+  a.fd_ho = FastDiv(static_cast<uint32_t>(a.Ho));
   a.wpack = reinterpret_cast<const uint8_t*>(pp.wpack);
   a.out = out;
   a.bias = pp.bias_eff;
@@ -388,6 +442,7 @@ cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t b
   a.xcls = pp.xcls;
   a.n_xcls = pp.n_xcls;
   a.ncls = pp.ncls;
+  a.base_cls = pp.base_cls;
   a.rq = pp.rq;
   a.lo4 = splat4(d.act_min);
   a.hi4 = splat4(d.act_max);
@@ -413,34 +468,35 @@ cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t b
 
   const int per = std::max(1, num_sms / a.n_groups);
   const int grid = a.n_groups * per;
-  // Variants: constant-table epilogue (fast requant, tables as a kernel
-  // parameter), fast requant from smem tables, general requant.
-  const int variant = (pp.all_fast_known && pp.table != nullptr) ? 2 : pp.all_fast_known ? 1 : 0;
-  static std::atomic<uint32_t> attr_set{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint32_t bit = (1u << variant) << (3 * (dev & 7));
-  if ((attr_set.load() & bit) == 0) {
-    cudaError_t e = cudaSuccess;
-    if (variant == 2)
-      e = cudaFuncSetAttribute(k_dw_tc_s8<true, EpiTable>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    else if (variant == 1)
-      e = cudaFuncSetAttribute(k_dw_tc_s8<true, NoTab>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    else
-      e = cudaFuncSetAttribute(k_dw_tc_s8<false, NoTab>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return e;
-    attr_set.fetch_or(bit);
+  // Constant-table epilogue when the host holds a table and every channel
+  // group has its compile-time path; else fast or general requant from the
+  // smem-staged tables.
+  if (pp.all_fast_known && pp.table != nullptr && a.n_groups <= kDwStaticGroups &&
+      (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    return a.clamp ? launch_dw_variant<kDwStatic, true>(m, a, *pp.table, grid, smem, s)
+                   : launch_dw_variant<kDwStatic, false>(m, a, *pp.table, grid, smem, s);
   }
-  if (variant == 2)
-    k_dw_tc_s8<true, EpiTable><<<grid, kThreads, smem, s>>>(m, a, *pp.table);
-  else if (variant == 1)
-    k_dw_tc_s8<true, NoTab><<<grid, kThreads, smem, s>>>(m, a, NoTab{0});
-  else
-    k_dw_tc_s8<false, NoTab><<<grid, kThreads, smem, s>>>(m, a, NoTab{0});
-  return cudaGetLastError();
+  if (pp.all_fast_known) return launch_dw_variant<kDwFast, false>(m, a, NoTab{0}, grid, smem, s);
+  return launch_dw_variant<kDwGeneral, false>(m, a, NoTab{0}, grid, smem, s);
+}
+
+}  // namespace
+
+// Tile indices are 32-bit in the kernel: larger batches run as several
+// launches over batch slices.
+cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
+                         const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                         cudaStream_t s) {
+  const int64_t tiles_per = static_cast<int64_t>(d.out_h) * ((d.out_w + 127) / 128);
+  const int64_t chunk = std::max<int64_t>(1, ((1ll << 31) - 1) / tiles_per);
+  const int64_t in_per = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
+  const int64_t out_per = static_cast<int64_t>(d.out_h) * d.out_w * d.out_c;
+  for (int64_t b0 = 0; b0 < batch; b0 += chunk) {
+    const cudaError_t e = launch_dw_tc_once(d, pp, std::min(chunk, batch - b0), in + b0 * in_per,
+                                            out + b0 * out_per, dev_err, num_sms, s);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace pspml

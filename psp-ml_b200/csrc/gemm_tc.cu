@@ -62,6 +62,8 @@ struct TcGemmArgs {
   const RqChannel* rq;
   const int32_t* all_fast;  // -1: every channel has a fast-form requant entry
   int32_t ncls;             // rows of the folded-bias table
+  int32_t base_cls;         // border class whose bias the constant table holds
+  FastDiv fd_tiles_n, fd_per_img, fd_tiles_x;  // tile index -> (n tile, m tile), origin
   int32_t param_smem;       // bytes of requant + bias tables staged in smem (0: read global)
   uint32_t lo4, hi4;    // activation clamp, bytes replicated
   int32_t clamp;        // act range narrower than int8
@@ -111,16 +113,16 @@ struct TileOrigin {
   int32_t x0, y0;
   int64_t n0;
 };
-__device__ __forceinline__ TileOrigin tile_origin(const TcGemmArgs& p, int64_t tm) {
-  const int64_t per_img = static_cast<int64_t>(p.tiles_x) * p.tiles_y;
-  const int64_t ti = tm / per_img;
-  const int32_t rem = static_cast<int32_t>(tm - ti * per_img);
-  const int32_t ty = rem / p.tiles_x;
+// Tile indices stay below 2^31 (the host splits larger batches).
+__device__ __forceinline__ TileOrigin tile_origin(const TcGemmArgs& p, uint32_t tm) {
+  const uint32_t ti = p.fd_per_img.div(tm);
+  const int32_t rem = static_cast<int32_t>(tm - ti * p.fd_per_img.d);
+  const int32_t ty = static_cast<int32_t>(p.fd_tiles_x.div(static_cast<uint32_t>(rem)));
   const int32_t tx = rem - ty * p.tiles_x;
   TileOrigin o;
   o.x0 = tx << p.bw_log2;
   o.y0 = ty << p.bh_log2;
-  o.n0 = ti * p.bi;
+  o.n0 = static_cast<int64_t>(ti) * p.bi;
   return o;
 }
 
@@ -181,38 +183,50 @@ struct NoTable {
   int32_t unused;
 };
 
-// Constant-table version of epilogue_chunk (fast requant only): every
-// per-channel read indexes the kernel-parameter table directly.
-__device__ __forceinline__ void epilogue_chunk_tab(const uint32_t (&v)[16], int8_t* dst,
-                                                   const EpiTable& tab, int bias_off, int nc,
-                                                   int cnt, const TcGemmArgs& p) {
+// Epilogue variants of k_gemm_s8.
+enum : int {
+  kEpiGeneral = 0,  // tables in smem or global, runtime fast/general requant
+  kEpiTable = 1,    // fast requant, tables a kernel parameter, runtime offsets
+  kEpiStatic = 2    // as kEpiTable with every offset a compile-time constant:
+                    // 2D A, one N tile (N == BN), 16-byte aligned rows
+};
+template <int MODE>
+struct TabOf {
+  using type = EpiTable;
+};
+template <>
+struct TabOf<kEpiGeneral> {
+  using type = NoTable;
+};
+
+__device__ __forceinline__ void store16(int8_t* dst, const uint4 w) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    *reinterpret_cast<uint4*>(dst) = w;
+  } else {
+    const uint32_t packed[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[4 * g + j] = static_cast<int8_t>(packed[g] >> (8 * j));
+  }
+}
+
+// Constant-table version of epilogue_chunk (fast requant only), channel
+// offset known at run time.  `border`: the row's class is not the table's
+// base class; its bias difference sits at dbias[cls_off + channel].
+__device__ __forceinline__ void epilogue_chunk_tab(uint32_t (&v)[16], int8_t* dst,
+                                                   const EpiTable& tab, bool border, int cls_off,
+                                                   int nc, int cnt, const TcGemmArgs& p) {
+  if (border) add_class_delta(v, tab, cls_off + nc, cnt);
   if (cnt == 16) {
-    uint32_t packed[4];
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      int32_t r[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int ch = nc + 4 * g + k;
-        r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]), tab.mh[ch], tab.bs[bias_off + ch]);
-      }
-      uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
-      if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
-      packed[g] = w;
-    }
-    if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-      *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    } else {
-#pragma unroll
-      for (int g = 0; g < 4; ++g)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dst[4 * g + j] = static_cast<int8_t>(packed[g] >> (8 * j));
-    }
+    store16(dst, p.clamp ? requant16_tab<true>(v, tab, nc, p.lo4, p.hi4)
+                         : requant16_tab<false>(v, tab, nc, p.lo4, p.hi4));
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       if (j < cnt) {
-        int32_t r = rq_tab(static_cast<int32_t>(v[j]), tab.mh[nc + j], tab.bs[bias_off + nc + j]);
+        const int2 bs = tab.bs[nc + j];
+        int32_t r = rq_tab(static_cast<int32_t>(v[j]) + bs.x, tab.mh[nc + j], bs.y);
         r = max(r, -128);
         r = min(r, 127);
         uint32_t w = static_cast<uint32_t>(r) & 0xFFu;
@@ -223,11 +237,34 @@ __device__ __forceinline__ void epilogue_chunk_tab(const uint32_t (&v)[16], int8
   }
 }
 
-template <int BN, int BK, bool FAST_ONLY, class Tab>
+// One output row of BN channels with compile-time table offsets: every
+// per-channel constant is a constant-bank operand of the instruction using
+// it.  Tensor-memory loads run one 16-column chunk ahead of the arithmetic.
+template <int BN, bool CLAMP>
+__device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_t taddr,
+                                                    int8_t* orow, bool valid,
+                                                    const TcGemmArgs& p) {
+  uint32_t v0[16], v1[16];
+  tmem_ld16_nowait(taddr, v0);
+#pragma unroll
+  for (int c = 0; c < BN; c += 32) {
+    tmem_wait_ld(v0);
+    if (c + 16 < BN) tmem_ld16_nowait(taddr + c + 16, v1);
+    const uint4 w0 = requant16_tab<CLAMP>(v0, tab, c, p.lo4, p.hi4);
+    if (valid) *reinterpret_cast<uint4*>(orow + c) = w0;
+    if (c + 16 < BN) {
+      tmem_wait_ld(v1);
+      if (c + 32 < BN) tmem_ld16_nowait(taddr + c + 32, v0);
+      const uint4 w1 = requant16_tab<CLAMP>(v1, tab, c + 16, p.lo4, p.hi4);
+      if (valid) *reinterpret_cast<uint4*>(orow + c + 16) = w1;
+    }
+  }
+}
+
+template <int BN, int BK, int MODE, bool CLAMP>
 __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
     k_gemm_s8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const TcGemmArgs p, const __grid_constant__ Tab tab) {
-  constexpr bool kTab = sizeof(Tab) == sizeof(EpiTable);
+              const TcGemmArgs p, const __grid_constant__ typename TabOf<MODE>::type tab) {
   constexpr int A_BYTES = kBM * BK;
   constexpr int B_BYTES = BN * BK;
   constexpr uint32_t kLayout = SwizzleFor<BK>::kLayout;
@@ -295,8 +332,8 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
-        const int32_t tn = static_cast<int32_t>(t % p.tiles_n);
-        const int64_t tm = t / p.tiles_n;
+        const uint32_t tm = p.fd_tiles_n.div(static_cast<uint32_t>(t));
+        const int32_t tn = static_cast<int32_t>(t - static_cast<int64_t>(tm) * p.tiles_n);
         TileOrigin o{0, 0, 0};
         if (p.conv4d) o = tile_origin(p, tm);
         for (int tap = 0; tap < p.taps && ok; ++tap) {
@@ -314,7 +351,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
                           o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
             else
               tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK,
-                          static_cast<int32_t>(tm * kBM));
+                          static_cast<int32_t>(tm) * kBM);
             tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
             ++issued;
             if (++s == stages) {
@@ -381,7 +418,8 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
     const int grp = (warp - 2) >> 2;
     const int q = warp & 3;  // tensor-memory lane quarter this warp may read
     const int row = q * 32 + lane;
-    const bool fast = FAST_ONLY || *p.all_fast != 0;
+    const uint32_t tlane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const bool fast = MODE != kEpiGeneral || *p.all_fast != 0;
     const RqChannel* rqb = p.param_smem ? srq : p.rq;
     const int32_t* bb = p.param_smem ? sbias : p.bias;
     int64_t i = grp;
@@ -397,48 +435,53 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
       if (!ready) break;
       tc_fence_after();
+      const uint32_t tb = tlane + static_cast<uint32_t>(b * BN);
 
-      const int32_t tn = static_cast<int32_t>(t % p.tiles_n);
-      const int64_t tm = t / p.tiles_n;
-      bool valid;
-      int8_t* orow;
-      const int32_t* brow = bb;
-      int cls_off = 0;
-      if (p.conv4d) {
-        const TileOrigin o = tile_origin(p, tm);
-        const int32_t x = o.x0 + (row & ((1 << p.bw_log2) - 1));
-        const int32_t y = o.y0 + ((row >> p.bw_log2) & ((1 << p.bh_log2) - 1));
-        const int64_t n = o.n0 + (row >> (p.bw_log2 + p.bh_log2));
-        valid = x < p.Wo && y < p.Ho && n < p.nimg;
-        orow = p.out + ((n * p.Ho + y) * p.Wo + x) * static_cast<int64_t>(p.N);
-        if (valid && p.ycls != nullptr) {
-          cls_off = (p.ycls[y] * p.n_xcls + p.xcls[x]) * p.N;
-          brow = bb + cls_off;
-        }
+      if constexpr (MODE == kEpiStatic) {
+        const int64_t r = t * kBM + row;
+        epilogue_row_static<BN, CLAMP>(tab, tb, p.out + r * p.ldo, r < p.rows, p);
       } else {
-        const int64_t r = tm * kBM + row;
-        valid = r < p.rows;
-        orow = p.out + r * p.ldo;
-      }
-      const int32_t n0 = tn * BN;
+        const uint32_t tm = p.fd_tiles_n.div(static_cast<uint32_t>(t));
+        const int32_t tn = static_cast<int32_t>(t - static_cast<int64_t>(tm) * p.tiles_n);
+        bool valid;
+        int8_t* orow;
+        const int32_t* brow = bb;
+        int cls_off = 0;
+        bool border = false;
+        if (p.conv4d) {
+          const TileOrigin o = tile_origin(p, tm);
+          const int32_t x = o.x0 + (row & ((1 << p.bw_log2) - 1));
+          const int32_t y = o.y0 + ((row >> p.bw_log2) & ((1 << p.bh_log2) - 1));
+          const int64_t n = o.n0 + (row >> (p.bw_log2 + p.bh_log2));
+          valid = x < p.Wo && y < p.Ho && n < p.nimg;
+          orow = p.out + ((n * p.Ho + y) * p.Wo + x) * static_cast<int64_t>(p.N);
+          if (valid && p.ycls != nullptr) {
+            const int cls = p.ycls[y] * p.n_xcls + p.xcls[x];
+            cls_off = cls * p.N;
+            border = cls != p.base_cls;
+            brow = bb + cls_off;
+          }
+        } else {
+          const int64_t r = static_cast<int64_t>(tm) * kBM + row;
+          valid = r < p.rows;
+          orow = p.out + r * p.ldo;
+        }
+        const int32_t n0 = tn * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(b * BN + c),
-                  v);
-        const int32_t nc = n0 + c;
-        if (valid && nc < p.N) {
-          const int cnt = min(16, p.N - nc);
-          if constexpr (kTab) {
-            epilogue_chunk_tab(v, orow + nc, tab, cls_off, nc, cnt, p);
-          } else if constexpr (FAST_ONLY) {
-            epilogue_chunk<true>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
-          } else {
-            if (fast)
-              epilogue_chunk<true>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
-            else
-              epilogue_chunk<false>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(tb + static_cast<uint32_t>(c), v);
+          const int32_t nc = n0 + c;
+          if (valid && nc < p.N) {
+            const int cnt = min(16, p.N - nc);
+            if constexpr (MODE == kEpiTable) {
+              epilogue_chunk_tab(v, orow + nc, tab, border, cls_off, nc, cnt, p);
+            } else {
+              if (fast)
+                epilogue_chunk<true>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
+              else
+                epilogue_chunk<false>(v, orow + nc, brow + nc, rqb + nc, cnt, p);
+            }
           }
         }
       }
@@ -467,9 +510,37 @@ int pow2_ceil(int v) {
   return p;
 }
 
-// Two variants per tile shape: the constant-table epilogue (fast requant,
-// tables as a kernel parameter) when the host holds a table for the op, and
-// the general one (tables in smem or global, runtime fast/slow flag).
+// Sets the dynamic shared memory limit of one kernel variant, once per
+// device.
+template <int BN, int BK, int MODE, bool CLAMP>
+cudaError_t ensure_smem_attr() {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((done.load() & bit) != 0) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<BN, BK, MODE, CLAMP>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemLimit);
+  if (e == cudaSuccess) done.fetch_or(bit);
+  return e;
+}
+
+template <int BN, int BK, int MODE, bool CLAMP>
+cudaError_t launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const TcGemmArgs& args,
+                           const typename TabOf<MODE>::type& tab, int64_t grid, int smem,
+                           cudaStream_t s) {
+  const cudaError_t e = ensure_smem_attr<BN, BK, MODE, CLAMP>();
+  if (e != cudaSuccess) return e;
+  k_gemm_s8<BN, BK, MODE, CLAMP>
+      <<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb, args, tab);
+  return cudaGetLastError();
+}
+
+// Epilogue variant per op: the static constant-table epilogue for 2D
+// operands with a single N tile, the run-time-offset table epilogue for
+// other ops whose host holds a table, the general one (tables in smem or
+// global, runtime fast/general flag) otherwise.
 template <int BN, int BK>
 cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args,
                    const EpiTable* table, int num_sms, cudaStream_t s) {
@@ -482,30 +553,17 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   // one persistent CTA per SM.
   const int smem = std::max(overhead + stages * stage_bytes, 120 * 1024);
   args.stages = stages;
-  static std::atomic<uint32_t> attr_set{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint32_t bit = (table != nullptr ? 2u : 1u) << (2 * (dev & 15));
-  if ((attr_set.load() & bit) == 0) {
-    cudaError_t e =
-        table != nullptr
-            ? cudaFuncSetAttribute(k_gemm_s8<BN, BK, true, EpiTable>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit)
-            : cudaFuncSetAttribute(k_gemm_s8<BN, BK, false, NoTable>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return e;
-    attr_set.fetch_or(bit);
-  }
   const int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
   if (grid <= 0) return cudaSuccess;
-  if (table != nullptr)
-    k_gemm_s8<BN, BK, true, EpiTable>
-        <<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb, args, *table);
-  else
-    k_gemm_s8<BN, BK, false, NoTable>
-        <<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb, args,
-                                                                         NoTable{0});
-  return cudaGetLastError();
+  if (table == nullptr)
+    return launch_variant<BN, BK, kEpiGeneral, false>(ma, mb, args, NoTable{0}, grid, smem, s);
+  const bool is_static = !args.conv4d && args.tiles_n == 1 && args.N == BN &&
+                         args.ldo == BN && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0;
+  if (!is_static)
+    return launch_variant<BN, BK, kEpiTable, false>(ma, mb, args, *table, grid, smem, s);
+  if (args.clamp)
+    return launch_variant<BN, BK, kEpiStatic, true>(ma, mb, args, *table, grid, smem, s);
+  return launch_variant<BN, BK, kEpiStatic, false>(ma, mb, args, *table, grid, smem, s);
 }
 
 template <int BK>
@@ -520,11 +578,9 @@ cudaError_t run_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
   }
 }
 
-}  // namespace
-
-cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
-                           const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
-                           cudaStream_t s) {
+cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
+                                const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                                cudaStream_t s) {
   const int N = d.out_c;
   const bool is_fc = d.kind == PSPML_OP_FULLY_CONNECTED;
   const int Kc = is_fc ? d.in_h * d.in_w * d.in_c : d.in_c;
@@ -549,6 +605,7 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t
   a.rq = pp.rq;
   a.all_fast = pp.rq_all_fast;
   a.ncls = pp.ncls;
+  a.base_cls = pp.base_cls;
   a.param_smem = static_cast<int32_t>(param_smem_bytes(N, pp.ncls));
   a.lo4 = splat4(d.act_min);
   a.hi4 = splat4(d.act_max);
@@ -576,6 +633,8 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t
     const int64_t tiles_img = (batch + bi - 1) / bi;
     const int64_t tiles_m = tiles_img * a.tiles_x * a.tiles_y;
     a.tiles_total = tiles_m * a.tiles_n;
+    a.fd_per_img = FastDiv(static_cast<uint32_t>(a.tiles_x * a.tiles_y));
+    a.fd_tiles_x = FastDiv(static_cast<uint32_t>(a.tiles_x));
     const uint64_t dims[4] = {static_cast<uint64_t>(d.in_c), static_cast<uint64_t>(d.in_w),
                               static_cast<uint64_t>(d.in_h), static_cast<uint64_t>(batch)};
     const uint64_t strides[3] = {static_cast<uint64_t>(d.in_c),
@@ -605,12 +664,38 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t
     if (encode_tensor_map(&mb, pp.filter, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  if (a.tiles_total >= (1ll << 31)) return cudaErrorInvalidValue;
+  a.fd_tiles_n = FastDiv(static_cast<uint32_t>(a.tiles_n));
   const EpiTable* table = pp.all_fast_known ? pp.table : nullptr;
   switch (bk) {
     case 128: return run_tc_bn<128>(bn, ma, mb, a, table, num_sms, s);
     case 64: return run_tc_bn<64>(bn, ma, mb, a, table, num_sms, s);
     default: return run_tc_bn<32>(bn, ma, mb, a, table, num_sms, s);
   }
+}
+
+}  // namespace
+
+// Tile indices are 32-bit in the kernel: batches with 2^31 or more tiles
+// (or A rows) run as several launches over batch slices.
+cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
+                           const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                           cudaStream_t s) {
+  const bool is_fc = d.kind == PSPML_OP_FULLY_CONNECTED;
+  const int64_t rows_per = is_fc ? 1 : static_cast<int64_t>(d.out_h) * d.out_w;
+  // Rows bound the 2D tile count; a 4D tile holds at least one output row
+  // segment, so rows also bound the 4D count.  (2^31 - 2^12) / 32 N tiles.
+  const int64_t max_rows = ((1ll << 31) - 4096) / std::max(1, (d.out_c + 31) / 32);
+  const int64_t chunk = std::max<int64_t>(1, max_rows / rows_per);
+  const int64_t in_per = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
+  const int64_t out_per = static_cast<int64_t>(d.out_h) * d.out_w * d.out_c;
+  for (int64_t b0 = 0; b0 < batch; b0 += chunk) {
+    const cudaError_t e =
+        launch_tc_gemm_once(d, pp, std::min(chunk, batch - b0), in + b0 * in_per,
+                            out + b0 * out_per, dev_err, num_sms, s);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace pspml

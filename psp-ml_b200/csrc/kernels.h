@@ -43,28 +43,80 @@ bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc);
 // reads are warp-uniform, and the constant bank serves them without
 // occupying the L1 data pipe (staging them in shared memory made that pipe
 // the bottleneck: every lane reloads the same 20 bytes per output).
-// Two 64-bit constant loads per output: {M, C_hi} per channel and
-// {bias, shift} per (border class, channel).  The low word of C is 2^30 for
-// every channel whose right shift is >= 2, which the host checks before it
-// builds a table.
+// Per channel {M, C_hi} and {bias of the base border class, shift}; the
+// other border classes add a per-(class, channel) bias difference.  The low
+// word of C is 2^30 for every channel whose right shift is >= 2, which the
+// host checks before it builds a table.  When a kernel's channel block is
+// fixed, the table offsets are compile-time constants and the epilogue reads
+// the entries as constant-bank operands with no load instruction at all.
 constexpr int kTabRq = 512;
-constexpr int kTabBias = 2560;
+constexpr int kTabDelta = 4096;
 struct EpiTable {
-  int2 mh[kTabRq];    // {M, high word of C - 2^32}
-  int2 bs[kTabBias];  // [ncls][N] {folded bias, right shift - 1}
+  int2 mh[kTabRq];           // {M, high word of C - 2^32}
+  int2 bs[kTabRq];           // {folded bias of class base_cls, right shift - 1}
+  int32_t dbias[kTabDelta];  // [ncls][N]: folded bias of the class - that of base_cls
 };
 
-// Fast requant with the table's split constants (C low word = 2^30).
-__device__ __forceinline__ int32_t rq_tab(int32_t acc, const int2 mh, const int2 bs) {
-  const int32_t a = acc + bs.x;
+// Fast requant with the table's split constants (C low word = 2^30); `a` is
+// the accumulator plus the folded bias.
+__device__ __forceinline__ int32_t rq_tab(int32_t a, const int2 mh, int32_t sr) {
   const int64_t c =
       static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(mh.y)) << 32) |
                            0x40000000u);
   const int64_t t = static_cast<int64_t>(a) * mh.x + c;
   const uint32_t lo = static_cast<uint32_t>(t);
   const int32_t hi = static_cast<int32_t>(t >> 32);
-  return (hi + static_cast<int32_t>((~static_cast<uint32_t>(a) | lo) >> 31)) >> bs.y;
+  return (hi + static_cast<int32_t>((~static_cast<uint32_t>(a) | lo) >> 31)) >> sr;
 }
+
+// Requantises 16 accumulators of channels ch .. ch+15 (table entries, bias
+// of the base class) into 16 packed bytes.
+template <bool CLAMP>
+__device__ __forceinline__ uint4 requant16_tab(const uint32_t* v, const EpiTable& tab, int ch,
+                                               uint32_t lo4, uint32_t hi4) {
+  uint32_t packed[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    int32_t r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = ch + 4 * g + k;
+      const int2 bs = tab.bs[c];
+      r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]) + bs.x, tab.mh[c], bs.y);
+    }
+    uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
+    if constexpr (CLAMP) w = clamp4(w, lo4, hi4);
+    packed[g] = w;
+  }
+  return make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
+// Adds the bias difference of a non-base border class (table offset `off`
+// = class * N + first channel) to the first `cnt` of 16 accumulators.
+__device__ __forceinline__ void add_class_delta(uint32_t* v, const EpiTable& tab, int off,
+                                                int cnt) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    if (j < cnt) v[j] += static_cast<uint32_t>(tab.dbias[off + j]);
+}
+
+// Unsigned division by a divisor fixed at launch, for numerators below 2^31:
+// q = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1 (the round-up multiplier method of
+// Granlund and Montgomery, "Division by invariant integers using
+// multiplication", 1994).
+struct FastDiv {
+  uint32_t d = 1, m = 1;
+  int32_t l = 0;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t div) : d(div) {
+    while ((1ull << l) < div) ++l;
+    m = static_cast<uint32_t>((((1ull << 32) * ((1ull << l) - div)) / div) + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    return (__umulhi(n, m) + n) >> l;
+  }
+};
 
 // Everything a kernel needs beyond the activations, on the device.
 struct PreparedOp {
@@ -83,6 +135,7 @@ struct PreparedOp {
   uint8_t* ycls = nullptr;          // [out_h] (tensor-core conv with ncls > 1)
   uint8_t* xcls = nullptr;          // [out_w]
   int32_t ncls = 1, n_xcls = 1;
+  int32_t base_cls = 0;             // border class of an interior pixel (the table's base)
 };
 
 // Input-channel / kernel shapes k_small_conv_s8 is instantiated for.

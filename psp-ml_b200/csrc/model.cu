@@ -243,7 +243,8 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     const int n = m->ops[i].d.out_c;
     const bool tc =
         p.path == OpPath::kTc2d || p.path == OpPath::kTc4d || p.path == OpPath::kDwTc;
-    if (!tc || !p.all_fast_known || n > kTabRq || p.ncls * n > kTabBias) continue;
+    if (!tc || !p.all_fast_known || n > kTabRq || (p.ncls > 1 && p.ncls * n > kTabDelta))
+      continue;
     std::vector<RqChannel> rq(n);
     std::vector<int32_t> bias(static_cast<size_t>(p.ncls) * n);
     st = cuda_status(cudaMemcpy(rq.data(), p.rq, static_cast<size_t>(n) * sizeof(RqChannel),
@@ -259,10 +260,15 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     if (!low_word_fixed) continue;
     auto t = std::make_unique<EpiTable>();
     std::memset(t.get(), 0, sizeof(EpiTable));
-    for (int c = 0; c < n; ++c) t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
-    for (int k = 0; k < p.ncls; ++k)
-      for (int c = 0; c < n; ++c)
-        t->bs[k * n + c] = make_int2(bias[static_cast<size_t>(k) * n + c], rq[c].sr);
+    const size_t base = static_cast<size_t>(p.base_cls) * n;
+    for (int c = 0; c < n; ++c) {
+      t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
+      t->bs[c] = make_int2(bias[base + c], rq[c].sr);
+    }
+    if (p.ncls > 1)
+      for (int k = 0; k < p.ncls; ++k)
+        for (int c = 0; c < n; ++c)
+          t->dbias[k * n + c] = bias[static_cast<size_t>(k) * n + c] - bias[base + c];
     p.table = t.get();
     m->tables.push_back(std::move(t));
   }

@@ -274,6 +274,7 @@ cudaError_t prepare_op(const pspml_op_desc& d, OpPath path, const int8_t* filter
       bc = &bc_store;
       p.ncls = bc->n_ycls * bc->n_xcls;
       p.n_xcls = bc->n_xcls;
+      p.base_cls = bc->ycls[d.out_h / 2] * bc->n_xcls + bc->xcls[d.out_w / 2];
       p.bias_eff = c.take<int32_t>(static_cast<size_t>(p.ncls) * n * 4);
       if ((e = rq_and()) != cudaSuccess) break;
       p.ycls = c.take<uint8_t>(d.out_h);
@@ -294,6 +295,7 @@ cudaError_t prepare_op(const pspml_op_desc& d, OpPath path, const int8_t* filter
       bc = &bc_store;
       p.ncls = bc->n_ycls * bc->n_xcls;
       p.n_xcls = bc->n_xcls;
+      p.base_cls = bc->ycls[d.out_h / 2] * bc->n_xcls + bc->xcls[d.out_w / 2];
       p.bias_eff = c.take<int32_t>(static_cast<size_t>(p.ncls) * n * 4);
       if ((e = rq_and()) != cudaSuccess) break;
       p.ycls = c.take<uint8_t>(d.out_h);

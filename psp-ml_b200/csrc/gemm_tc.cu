@@ -69,6 +69,7 @@ struct TcGemmArgs {
   int32_t clamp;        // act range narrower than int8
   unsigned* err;
   int32_t stages;
+  int32_t b_res;  // the whole B operand (one N tile) stays in smem, loaded once
 };
 
 constexpr int kParamSmemMax = 32 * 1024;
@@ -277,9 +278,10 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int stages = p.stages;
+  const int kiters = p.taps * p.kblocks;
   uint8_t* sA = smem;
-  uint8_t* sB = smem + stages * A_BYTES;
-  uint8_t* sP = sB + stages * B_BYTES;  // staged requant + bias tables
+  uint8_t* sB = smem + stages * A_BYTES;  // B ring, or all of B when b_res
+  uint8_t* sP = sB + (p.b_res ? kiters : stages) * B_BYTES;  // staged requant + bias tables
   RqChannel* srq = reinterpret_cast<RqChannel*>(sP);
   int32_t* sbias = reinterpret_cast<int32_t*>(sP + static_cast<size_t>(p.N) * sizeof(RqChannel));
   uint64_t* full = reinterpret_cast<uint64_t*>(sP + p.param_smem);
@@ -287,7 +289,8 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + NB;
   uint64_t* mma_done = tempty + NB;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* bres_full = mma_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -303,6 +306,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       mbar_init(&tempty[a], 4);
     }
     mbar_init(mma_done, 1);
+    mbar_init(bres_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -322,7 +326,6 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int kiters = p.taps * p.kblocks;
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -331,6 +334,16 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       uint32_t ph = 0;
       int64_t issued = 0;
       bool ok = true;
+      if (p.b_res) {
+        // Every SM would otherwise fetch the same few KB of weights from the
+        // same L2 slices for every tile.
+        mbar_arrive_expect_tx(bres_full, static_cast<uint32_t>(kiters * B_BYTES));
+        for (int it = 0; it < kiters; ++it) {
+          const int tap = it / p.kblocks;
+          const int kb = it - tap * p.kblocks;
+          tma_load_2d(sB + it * B_BYTES, &tmB, bres_full, tap * p.Kc + kb * BK, 0);
+        }
+      }
       for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
         const uint32_t tm = p.fd_tiles_n.div(static_cast<uint32_t>(t));
         const int32_t tn = static_cast<int32_t>(t - static_cast<int64_t>(tm) * p.tiles_n);
@@ -345,14 +358,15 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+            mbar_arrive_expect_tx(&full[s], p.b_res ? A_BYTES : A_BYTES + B_BYTES);
             if (p.conv4d)
               tma_load_4d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
                           o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
             else
               tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK,
                           static_cast<int32_t>(tm) * kBM);
-            tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
+            if (!p.b_res)
+              tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
             ++issued;
             if (++s == stages) {
               s = 0;
@@ -367,6 +381,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
         for (int64_t g = first; g < issued; ++g)
           mbar_wait(&full[g % stages], static_cast<uint32_t>((g / stages) & 1), nullptr);
       }
+      if (p.b_res) mbar_wait(bres_full, 0, nullptr);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
@@ -375,6 +390,10 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
+      if (p.b_res && !mbar_wait(bres_full, 0, abort_flag)) {
+        record_error(p.err, abort_flag, kDevErrMmaWait);
+        ok = false;
+      }
       int64_t i = 0;  // local tile index
       for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x, ++i) {
         const int b = static_cast<int>(i % NB);
@@ -393,7 +412,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * A_BYTES);
-          const uint32_t b0 = smem_u32(sB + s * B_BYTES);
+          const uint32_t b0 = smem_u32(sB + (p.b_res ? it : s) * B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t ad = make_sdesc(a0 + kk * 32, 16, kSbo, kLayout);
@@ -544,9 +563,14 @@ cudaError_t launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const T
 template <int BN, int BK>
 cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args,
                    const EpiTable* table, int num_sms, cudaStream_t s) {
-  constexpr int stage_bytes = kBM * BK + BN * BK;
   if (table != nullptr) args.param_smem = 0;
-  const int overhead = 1024 + 64 * 8 + 64 + args.param_smem;
+  // Resident B when a single N tile's weights fit next to >= 4 A stages.
+  const int bres_bytes = args.taps * args.kblocks * BN * BK;
+  const int base_overhead = 1024 + 64 * 8 + 64 + args.param_smem;
+  args.b_res = args.tiles_n == 1 && bres_bytes <= 96 * 1024 &&
+               base_overhead + bres_bytes + 4 * kBM * BK <= kSmemLimit;
+  const int stage_bytes = args.b_res ? kBM * BK : kBM * BK + BN * BK;
+  const int overhead = base_overhead + (args.b_res ? bres_bytes : 0);
   int stages = (kSmemLimit - overhead) / stage_bytes;
   stages = std::min(stages, kMaxStages);
   // At least 120 KB so that a second CTA never shares the SM: the grid is

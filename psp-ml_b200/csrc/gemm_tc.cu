@@ -329,11 +329,15 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
+    // One thread; the loop body is kept short (no divisions, incremental
+    // coordinates): at small K it issues a tile every few hundred cycles
+    // and its own latency sets the pace.
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
       int64_t issued = 0;
       bool ok = true;
+      const uint32_t a_tx = p.b_res ? A_BYTES : A_BYTES + B_BYTES;
       if (p.b_res) {
         // Every SM would otherwise fetch the same few KB of weights from the
         // same L2 slices for every tile.
@@ -344,35 +348,51 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
           tma_load_2d(sB + it * B_BYTES, &tmB, bres_full, tap * p.Kc + kb * BK, 0);
         }
       }
-      for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x) {
-        const uint32_t tm = p.fd_tiles_n.div(static_cast<uint32_t>(t));
-        const int32_t tn = static_cast<int32_t>(t - static_cast<int64_t>(tm) * p.tiles_n);
+      // Tile t = tm * tiles_n + tn, advanced by gridDim.x per step.
+      const int32_t tiles_n = p.tiles_n;
+      const int32_t step_m = static_cast<int32_t>(gridDim.x) / tiles_n;
+      const int32_t step_n = static_cast<int32_t>(gridDim.x) - step_m * tiles_n;
+      int32_t tm = static_cast<int32_t>(blockIdx.x) / tiles_n;
+      int32_t tn = static_cast<int32_t>(blockIdx.x) - tm * tiles_n;
+      const int32_t kblocks = p.kblocks;
+      for (int64_t t = blockIdx.x; t < p.tiles_total; t += gridDim.x) {
         TileOrigin o{0, 0, 0};
-        if (p.conv4d) o = tile_origin(p, tm);
-        for (int tap = 0; tap < p.taps && ok; ++tap) {
-          const int ky = tap / p.kw;
-          const int kx = tap - ky * p.kw;
-          for (int kb = 0; kb < p.kblocks; ++kb) {
-            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
-              record_error(p.err, abort_flag, kDevErrTmaWait);
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&full[s], p.b_res ? A_BYTES : A_BYTES + B_BYTES);
-            if (p.conv4d)
-              tma_load_4d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
-                          o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
-            else
-              tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK,
-                          static_cast<int32_t>(tm) * kBM);
-            if (!p.b_res)
-              tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
-            ++issued;
-            if (++s == stages) {
-              s = 0;
-              ph ^= 1u;
+        if (p.conv4d) o = tile_origin(p, static_cast<uint32_t>(tm));
+        int tap = 0, kb = 0, ky = 0, kx = 0;
+        for (int it = 0; it < kiters; ++it) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+            record_error(p.err, abort_flag, kDevErrTmaWait);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], a_tx);
+          if (p.conv4d)
+            tma_load_4d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
+                        o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
+          else
+            tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, tm * kBM);
+          if (!p.b_res)
+            tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
+          ++issued;
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+          if (++kb == kblocks) {
+            kb = 0;
+            ++tap;
+            if (++kx == p.kw) {
+              kx = 0;
+              ++ky;
             }
           }
+        }
+        if (!ok) break;
+        tm += step_m;
+        tn += step_n;
+        if (tn >= tiles_n) {
+          tn -= tiles_n;
+          ++tm;
         }
       }
       if (!ok) {
@@ -394,11 +414,12 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
         record_error(p.err, abort_flag, kDevErrMmaWait);
         ok = false;
       }
-      int64_t i = 0;  // local tile index
-      for (int64_t t = blockIdx.x; t < p.tiles_total && ok; t += gridDim.x, ++i) {
-        const int b = static_cast<int>(i % NB);
-        const uint32_t use = static_cast<uint32_t>(i / NB);
-        if (!mbar_wait(&tempty[b], (use & 1u) ^ 1u, abort_flag)) {
+      const uint32_t a_base = smem_u32(sA);
+      const uint32_t b_base = smem_u32(sB);
+      int b = 0;
+      uint32_t use_par = 0;  // parity of the current pass over the NB buffers
+      for (int64_t t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
+        if (!mbar_wait(&tempty[b], use_par ^ 1u, abort_flag)) {
           record_error(p.err, abort_flag, kDevErrMmaWait);
           break;
         }
@@ -411,8 +432,8 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * A_BYTES);
-          const uint32_t b0 = smem_u32(sB + (p.b_res ? it : s) * B_BYTES);
+          const uint32_t a0 = a_base + static_cast<uint32_t>(s * A_BYTES);
+          const uint32_t b0 = b_base + static_cast<uint32_t>((p.b_res ? it : s) * B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t ad = make_sdesc(a0 + kk * 32, 16, kSbo, kLayout);
@@ -427,6 +448,10 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
         }
         if (!ok) break;
         umma_commit(&tfull[b]);
+        if (++b == NB) {
+          b = 0;
+          use_par ^= 1u;
+        }
       }
       // All MMAs issued by this thread complete before tensor memory is freed.
       umma_commit(mma_done);

@@ -96,12 +96,17 @@ struct SwizzleFor<32> {
 };
 
 // Tensor-memory accumulator buffers and epilogue groups per tile width.
-template <int BN>
+// MT accumulators of 128 rows x BN columns per tile (a tile has 128 * MT
+// rows: one TMA box, MT MMAs per k step, one handoff).
+template <int BN, int MT>
 struct EpiShape {
-  static constexpr int kBufs = (512 / BN) >= 8 ? 8 : (512 / BN);
-  static constexpr int kGroups = kBufs >= 4 ? 4 : kBufs;
+  static constexpr int kCols = BN * MT;  // tensor-memory columns per buffer
+  static constexpr int kBufs = (512 / kCols) >= 8 ? 8 : (512 / kCols);
+  // Three groups for 256-row tiles: 14 warps leave 128 registers a thread
+  // (an SM sub-partition holds at most four of them).
+  static constexpr int kGroups = MT == 2 ? 3 : (kBufs >= 4 ? 4 : kBufs);
   static constexpr int kThreads = 64 + 128 * kGroups;
-  static constexpr uint32_t kTmemCols = kBufs * BN;
+  static constexpr uint32_t kTmemCols = kBufs * kCols;
 };
 
 __device__ __forceinline__ void record_error(unsigned* err, volatile int* abort_flag,
@@ -262,17 +267,19 @@ __device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_
   }
 }
 
-template <int BN, int BK, int MODE, bool CLAMP>
-__global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
+template <int BN, int BK, int MT, int MODE, bool CLAMP>
+__global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
     k_gemm_s8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const TcGemmArgs p, const __grid_constant__ typename TabOf<MODE>::type tab) {
-  constexpr int A_BYTES = kBM * BK;
+  constexpr int TM = kBM * MT;  // rows per tile
+  constexpr int A_BYTES = TM * BK;
   constexpr int B_BYTES = BN * BK;
   constexpr uint32_t kLayout = SwizzleFor<BK>::kLayout;
   constexpr uint32_t kSbo = 8 * BK;  // bytes between 8-row groups
-  constexpr int NB = EpiShape<BN>::kBufs;
-  constexpr int G = EpiShape<BN>::kGroups;
-  constexpr uint32_t kTmemCols = EpiShape<BN>::kTmemCols;
+  constexpr int NB = EpiShape<BN, MT>::kBufs;
+  constexpr int G = EpiShape<BN, MT>::kGroups;
+  constexpr int kCols = EpiShape<BN, MT>::kCols;
+  constexpr uint32_t kTmemCols = EpiShape<BN, MT>::kTmemCols;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -370,7 +377,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
             tma_load_4d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
                         o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
           else
-            tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, tm * kBM);
+            tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, tm * TM);
           if (!p.b_res)
             tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
           ++issued;
@@ -424,7 +431,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kCols);
         for (int it = 0; it < kiters; ++it) {
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             record_error(p.err, abort_flag, kDevErrMmaWait);
@@ -436,9 +443,12 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
           const uint32_t b0 = b_base + static_cast<uint32_t>((p.b_res ? it : s) * B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
-            const uint64_t ad = make_sdesc(a0 + kk * 32, 16, kSbo, kLayout);
             const uint64_t bd = make_sdesc(b0 + kk * 32, 16, kSbo, kLayout);
-            umma_i8(d_tmem, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              const uint64_t ad = make_sdesc(a0 + mt * kBM * BK + kk * 32, 16, kSbo, kLayout);
+              umma_i8(d_tmem + mt * BN, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&empty[s]);
           if (++s == stages) {
@@ -479,12 +489,18 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
       ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
       if (!ready) break;
       tc_fence_after();
-      const uint32_t tb = tlane + static_cast<uint32_t>(b * BN);
+      const uint32_t tb0 = tlane + static_cast<uint32_t>(b * kCols);
 
       if constexpr (MODE == kEpiStatic) {
-        const int64_t r = t * kBM + row;
-        epilogue_row_static<BN, CLAMP>(tab, tb, p.out + r * p.ldo, r < p.rows, p);
+#pragma unroll 1
+        for (int mt = 0; mt < MT; ++mt) {
+          const int64_t r = t * TM + mt * kBM + row;
+          epilogue_row_static<BN, CLAMP>(tab, tb0 + mt * BN, p.out + r * p.ldo, r < p.rows, p);
+        }
       } else {
+#pragma unroll 1
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint32_t tb = tb0 + static_cast<uint32_t>(mt * BN);
         const uint32_t tm = p.fd_tiles_n.div(static_cast<uint32_t>(t));
         const int32_t tn = static_cast<int32_t>(t - static_cast<int64_t>(tm) * p.tiles_n);
         bool valid;
@@ -506,7 +522,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
             brow = bb + cls_off;
           }
         } else {
-          const int64_t r = static_cast<int64_t>(tm) * kBM + row;
+          const int64_t r = static_cast<int64_t>(tm) * TM + mt * kBM + row;
           valid = r < p.rows;
           orow = p.out + r * p.ldo;
         }
@@ -528,6 +544,7 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
             }
           }
         }
+      }
       }
       tc_fence_before();
       __syncwarp();
@@ -556,28 +573,28 @@ int pow2_ceil(int v) {
 
 // Sets the dynamic shared memory limit of one kernel variant, once per
 // device.
-template <int BN, int BK, int MODE, bool CLAMP>
+template <int BN, int BK, int MT, int MODE, bool CLAMP>
 cudaError_t ensure_smem_attr() {
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load() & bit) != 0) return cudaSuccess;
-  const cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<BN, BK, MODE, CLAMP>,
+  const cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<BN, BK, MT, MODE, CLAMP>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemLimit);
   if (e == cudaSuccess) done.fetch_or(bit);
   return e;
 }
 
-template <int BN, int BK, int MODE, bool CLAMP>
+template <int BN, int BK, int MT, int MODE, bool CLAMP>
 cudaError_t launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const TcGemmArgs& args,
                            const typename TabOf<MODE>::type& tab, int64_t grid, int smem,
                            cudaStream_t s) {
-  const cudaError_t e = ensure_smem_attr<BN, BK, MODE, CLAMP>();
+  const cudaError_t e = ensure_smem_attr<BN, BK, MT, MODE, CLAMP>();
   if (e != cudaSuccess) return e;
-  k_gemm_s8<BN, BK, MODE, CLAMP>
-      <<<static_cast<unsigned>(grid), EpiShape<BN>::kThreads, smem, s>>>(ma, mb, args, tab);
+  k_gemm_s8<BN, BK, MT, MODE, CLAMP>
+      <<<static_cast<unsigned>(grid), EpiShape<BN, MT>::kThreads, smem, s>>>(ma, mb, args, tab);
   return cudaGetLastError();
 }
 
@@ -585,16 +602,17 @@ cudaError_t launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const T
 // operands with a single N tile, the run-time-offset table epilogue for
 // other ops whose host holds a table, the general one (tables in smem or
 // global, runtime fast/general flag) otherwise.
-template <int BN, int BK>
+template <int BN, int BK, int MT>
 cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args,
                    const EpiTable* table, int num_sms, cudaStream_t s) {
+  constexpr int A_BYTES = kBM * MT * BK;
   if (table != nullptr) args.param_smem = 0;
   // Resident B when a single N tile's weights fit next to >= 4 A stages.
   const int bres_bytes = args.taps * args.kblocks * BN * BK;
   const int base_overhead = 1024 + 64 * 8 + 64 + args.param_smem;
   args.b_res = args.tiles_n == 1 && bres_bytes <= 96 * 1024 &&
-               base_overhead + bres_bytes + 4 * kBM * BK <= kSmemLimit;
-  const int stage_bytes = args.b_res ? kBM * BK : kBM * BK + BN * BK;
+               base_overhead + bres_bytes + 4 * A_BYTES <= kSmemLimit;
+  const int stage_bytes = args.b_res ? A_BYTES : A_BYTES + BN * BK;
   const int overhead = base_overhead + (args.b_res ? bres_bytes : 0);
   int stages = (kSmemLimit - overhead) / stage_bytes;
   stages = std::min(stages, kMaxStages);
@@ -605,25 +623,32 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   const int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
   if (grid <= 0) return cudaSuccess;
   if (table == nullptr)
-    return launch_variant<BN, BK, kEpiGeneral, false>(ma, mb, args, NoTable{0}, grid, smem, s);
+    return launch_variant<BN, BK, MT, kEpiGeneral, false>(ma, mb, args, NoTable{0}, grid, smem,
+                                                          s);
   const bool is_static = !args.conv4d && args.tiles_n == 1 && args.N == BN &&
                          args.ldo == BN && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0;
   if (!is_static)
-    return launch_variant<BN, BK, kEpiTable, false>(ma, mb, args, *table, grid, smem, s);
+    return launch_variant<BN, BK, MT, kEpiTable, false>(ma, mb, args, *table, grid, smem, s);
   if (args.clamp)
-    return launch_variant<BN, BK, kEpiStatic, true>(ma, mb, args, *table, grid, smem, s);
-  return launch_variant<BN, BK, kEpiStatic, false>(ma, mb, args, *table, grid, smem, s);
+    return launch_variant<BN, BK, MT, kEpiStatic, true>(ma, mb, args, *table, grid, smem, s);
+  return launch_variant<BN, BK, MT, kEpiStatic, false>(ma, mb, args, *table, grid, smem, s);
 }
 
+// 256-row tiles (MT = 2) for narrow 2D GEMMs, whose per-tile handoff cost
+// would otherwise dominate; 128-row tiles elsewhere.
 template <int BK>
-cudaError_t run_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+cudaError_t run_tc_bn(int bn, int mt, const CUtensorMap& ma, const CUtensorMap& mb,
                       const TcGemmArgs& args, const EpiTable* table, int num_sms,
                       cudaStream_t s) {
+  if (mt == 2) {
+    if (bn == 32) return run_tc<32, BK, 2>(ma, mb, args, table, num_sms, s);
+    return run_tc<64, BK, 2>(ma, mb, args, table, num_sms, s);
+  }
   switch (bn) {
-    case 32: return run_tc<32, BK>(ma, mb, args, table, num_sms, s);
-    case 64: return run_tc<64, BK>(ma, mb, args, table, num_sms, s);
-    case 128: return run_tc<128, BK>(ma, mb, args, table, num_sms, s);
-    default: return run_tc<256, BK>(ma, mb, args, table, num_sms, s);
+    case 32: return run_tc<32, BK, 1>(ma, mb, args, table, num_sms, s);
+    case 64: return run_tc<64, BK, 1>(ma, mb, args, table, num_sms, s);
+    case 128: return run_tc<128, BK, 1>(ma, mb, args, table, num_sms, s);
+    default: return run_tc<256, BK, 1>(ma, mb, args, table, num_sms, s);
   }
 }
 
@@ -661,6 +686,7 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
   a.clamp = (d.act_min > -128 || d.act_max < 127) ? 1 : 0;
   a.err = dev_err;
 
+  int mt = 1;
   const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                             : CU_TENSOR_MAP_SWIZZLE_32B;
@@ -695,14 +721,15 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
       return cudaErrorInvalidValue;
   } else {
     const int64_t rows = is_fc ? batch : batch * d.out_h * d.out_w;
-    if (rows >= (1ll << 31) - kBM) return cudaErrorInvalidValue;
+    if (rows >= (1ll << 31) - 2 * kBM) return cudaErrorInvalidValue;
+    mt = bn <= 64 && rows > kBM ? 2 : 1;
     a.conv4d = 0;
     a.rows = rows;
     a.ldo = N;
-    a.tiles_total = ((rows + kBM - 1) / kBM) * a.tiles_n;
+    a.tiles_total = ((rows + kBM * mt - 1) / (kBM * mt)) * a.tiles_n;
     const uint64_t dims[2] = {static_cast<uint64_t>(Kc), static_cast<uint64_t>(rows)};
     const uint64_t strides[1] = {static_cast<uint64_t>(Kc)};
-    const uint32_t box[2] = {static_cast<uint32_t>(bk), static_cast<uint32_t>(kBM)};
+    const uint32_t box[2] = {static_cast<uint32_t>(bk), static_cast<uint32_t>(kBM * mt)};
     if (encode_tensor_map(&ma, in, 2, dims, strides, box, estr, swz) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
@@ -717,9 +744,9 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
   a.fd_tiles_n = FastDiv(static_cast<uint32_t>(a.tiles_n));
   const EpiTable* table = pp.all_fast_known ? pp.table : nullptr;
   switch (bk) {
-    case 128: return run_tc_bn<128>(bn, ma, mb, a, table, num_sms, s);
-    case 64: return run_tc_bn<64>(bn, ma, mb, a, table, num_sms, s);
-    default: return run_tc_bn<32>(bn, ma, mb, a, table, num_sms, s);
+    case 128: return run_tc_bn<128>(bn, mt, ma, mb, a, table, num_sms, s);
+    case 64: return run_tc_bn<64>(bn, mt, ma, mb, a, table, num_sms, s);
+    default: return run_tc_bn<32>(bn, mt, ma, mb, a, table, num_sms, s);
   }
 }
 

@@ -75,14 +75,17 @@ __device__ __forceinline__ int8_t finish1(int32_t a, const RqChannel& q, const G
 }
 
 // ------------------------------------------------------ depthwise 3x3 (dp4a)
-// Thread: 4 channels (one word) x PX consecutive output pixels of one row.
-// Block: 128 threads over (pixel group, channel word) pairs of one output
-// row (blockIdx.y) of one image (blockIdx.z + n_base).  Weights [9][C].
+// Thread: 4 channels (one word) x PX consecutive output pixels x a strip of
+// output rows (blockIdx.y).  It keeps the three input rows of the current
+// output row in registers and loads the S new rows of the next output row
+// while it computes, so the load latency overlaps the arithmetic.  Block:
+// 128 threads over (pixel group, channel word) pairs of one image
+// (blockIdx.z + n_base).  Weights [9][C]; out-of-image taps read zp_in.
 template <int S, int PX, bool FAST>
 __global__ void __launch_bounds__(128)
     k_dw3x3_s8(const uint32_t* __restrict__ in, const uint32_t* __restrict__ f,
                const int32_t* __restrict__ bias_eff, const RqChannel* __restrict__ rq,
-               uint32_t* __restrict__ out, const Geom g, int64_t n_base) {
+               uint32_t* __restrict__ out, const Geom g, int32_t rows_per, int64_t n_base) {
   constexpr int NIN = (PX - 1) * S + 3;
   const int cwn = g.C >> 2;
   const int pair = blockIdx.x * 128 + threadIdx.x;
@@ -90,7 +93,8 @@ __global__ void __launch_bounds__(128)
   if (pair >= groups * cwn) return;
   const int cw = pair % cwn;
   const int pg = pair / cwn;
-  const int oy = blockIdx.y;
+  const int oy0 = blockIdx.y * rows_per;
+  const int oy1 = min(oy0 + rows_per, g.Ho);
   const int64_t n = n_base + blockIdx.z;
   const int ox0 = pg * PX;
 
@@ -101,45 +105,81 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int j = 0; j < 4; ++j) wm[t][j] = w & (0xFFu << (8 * j));
   }
-  int32_t acc[PX][4];
-#pragma unroll
-  for (int p = 0; p < PX; ++p)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[p][j] = 0;
+  const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff) + cw);
+  const RqChannel q0 = load_rq(rq + 4 * cw), q1 = load_rq(rq + 4 * cw + 1),
+                  q2 = load_rq(rq + 4 * cw + 2), q3 = load_rq(rq + 4 * cw + 3);
 
   const uint32_t zpw = splat4(g.zp_in);
   const int ix0 = ox0 * S - g.pl;
   const uint32_t* img = in + n * static_cast<int64_t>(g.H) * g.W * cwn + cw;
-#pragma unroll
-  for (int ky = 0; ky < 3; ++ky) {
-    const int iy = oy * S - g.pt + ky;
+  auto load_row = [&](int iy, uint32_t (&x)[NIN]) {
     const bool row_ok = iy >= 0 && iy < g.H;
     const uint32_t* rowp = img + static_cast<int64_t>(row_ok ? iy : 0) * g.W * cwn;
-    uint32_t x[NIN];
 #pragma unroll
     for (int c = 0; c < NIN; ++c) {
       const int ix = ix0 + c;
       x[c] = (row_ok && ix >= 0 && ix < g.W) ? __ldg(rowp + ix * cwn) : zpw;
     }
+  };
+  uint32_t r0[NIN], r1[NIN], r2[NIN];
+  const int iy0 = oy0 * S - g.pt;
+  load_row(iy0, r0);
+  load_row(iy0 + 1, r1);
+  load_row(iy0 + 2, r2);
+  uint32_t* obase = out + (n * g.Ho) * static_cast<int64_t>(g.Wo) * cwn + cw;
+#pragma unroll 1
+  for (int oy = oy0; oy < oy1; ++oy) {
+    // Rows of the next output row: input rows (oy+1)*S - pt + {0,1,2}, of
+    // which the first 3 - S are already held.
+    uint32_t p0[NIN], p1[NIN];
+    const int niy = (oy + 1) * S - g.pt;
+#pragma unroll
+    for (int c = 0; c < NIN; ++c) p0[c] = p1[c] = zpw;
+    if (oy + 1 < oy1) {
+      if (S == 1) {
+        load_row(niy + 2, p0);
+      } else {
+        load_row(niy + 1, p0);
+        load_row(niy + 2, p1);
+      }
+    }
+    int32_t acc[PX][4];
+#pragma unroll
+    for (int p = 0; p < PX; ++p)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[p][j] = 0;
 #pragma unroll
     for (int p = 0; p < PX; ++p)
 #pragma unroll
       for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          acc[p][j] = __dp4a(static_cast<int>(x[p * S + kx]), static_cast<int>(wm[ky * 3 + kx][j]),
+        for (int j = 0; j < 4; ++j) {
+          acc[p][j] = __dp4a(static_cast<int>(r0[p * S + kx]), static_cast<int>(wm[kx][j]),
                              acc[p][j]);
-  }
-
-  const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff) + cw);
-  const RqChannel q0 = load_rq(rq + 4 * cw), q1 = load_rq(rq + 4 * cw + 1),
-                  q2 = load_rq(rq + 4 * cw + 2), q3 = load_rq(rq + 4 * cw + 3);
-  uint32_t* orow = out + ((n * g.Ho + oy) * static_cast<int64_t>(g.Wo)) * cwn + cw;
+          acc[p][j] = __dp4a(static_cast<int>(r1[p * S + kx]),
+                             static_cast<int>(wm[3 + kx][j]), acc[p][j]);
+          acc[p][j] = __dp4a(static_cast<int>(r2[p * S + kx]),
+                             static_cast<int>(wm[6 + kx][j]), acc[p][j]);
+        }
+    uint32_t* orow = obase + static_cast<int64_t>(oy) * g.Wo * cwn;
 #pragma unroll
-  for (int p = 0; p < PX; ++p)
-    if (ox0 + p < g.Wo)
-      orow[static_cast<int64_t>(ox0 + p) * cwn] =
-          finish4<FAST>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
+    for (int p = 0; p < PX; ++p)
+      if (ox0 + p < g.Wo)
+        orow[static_cast<int64_t>(ox0 + p) * cwn] =
+            finish4<FAST>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
+#pragma unroll
+    for (int c = 0; c < NIN; ++c) {
+      if (S == 1) {
+        r0[c] = r1[c];
+        r1[c] = r2[c];
+        r2[c] = p0[c];
+      } else {
+        r0[c] = r2[c];
+        r1[c] = p0[c];
+        r2[c] = p1[c];
+      }
+    }
+  }
 }
 
 // --------------------------------------------------- small-channel conv (dp4a)
@@ -498,25 +538,31 @@ cudaError_t launch_small_conv(const pspml_op_desc& d, const PreparedOp& p, int64
 cudaError_t launch_dw3x3(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                          const int8_t* in, int8_t* out, cudaStream_t s) {
   const Geom g = geom_of(d);
-  constexpr int PX = 8;
+  constexpr int PX = 4;
   const int groups = (g.Wo + PX - 1) / PX;
   const int pairs = groups * (g.C / 4);
+  const int rows_per = std::min(g.Ho, 16);
+  const unsigned strips = static_cast<unsigned>((g.Ho + rows_per - 1) / rows_per);
   for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
     const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
-    const dim3 grid((pairs + 127) / 128, g.Ho, nz);
+    const dim3 grid((pairs + 127) / 128, strips, nz);
     const auto* i32 = reinterpret_cast<const uint32_t*>(in);
     const auto* f32 = reinterpret_cast<const uint32_t*>(p.filter);
     auto* o32 = reinterpret_cast<uint32_t*>(out);
     if (p.all_fast_known) {
       if (g.sh == 1)
-        k_dw3x3_s8<1, PX, true><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+        k_dw3x3_s8<1, PX, true>
+            <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
       else
-        k_dw3x3_s8<2, PX, true><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+        k_dw3x3_s8<2, PX, true>
+            <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
     } else {
       if (g.sh == 1)
-        k_dw3x3_s8<1, PX, false><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+        k_dw3x3_s8<1, PX, false>
+            <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
       else
-        k_dw3x3_s8<2, PX, false><<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, n0);
+        k_dw3x3_s8<2, PX, false>
+            <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
     }
   }
   return cudaGetLastError();

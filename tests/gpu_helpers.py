@@ -97,3 +97,34 @@ def run_op_gpu(ctx, d, batch, x, filt=None, bias=None, mult=None, shift=None):
     torch.cuda.synchronize()
     ctx.check_device()
     return out.cpu().numpy()[: batch * out_elems(d)]
+
+
+def run_op_model(ctx, d, batch, x, filt, bias, mult, shift, micro=None):
+    """Runs one weighted op as a one-op compiled model (weights uploaded with
+    the model; the host builds the constant requant table when every
+    channel takes the fast form, so this exercises the constant-table
+    kernels); returns the int8 output (host)."""
+    import torch
+
+    parts = [np.ascontiguousarray(filt, np.int8).view(np.uint8).reshape(-1),
+             np.ascontiguousarray(bias, np.int32).view(np.uint8).reshape(-1),
+             np.ascontiguousarray(mult, np.int32).view(np.uint8).reshape(-1),
+             np.ascontiguousarray(shift, np.int32).view(np.uint8).reshape(-1)]
+    offs, pos = [], 0
+    for a in parts:
+        offs.append(pos)
+        pos += (a.size + 255) // 256 * 256
+    blob = np.zeros(pos, np.uint8)
+    for o, a in zip(offs, parts):
+        blob[o:o + a.size] = a
+    dd = np.array(d).reshape(1).copy()
+    dd["filter_off"], dd["bias_off"], dd["mult_off"], dd["shift_off"] = offs
+    model = capi.Model(ctx, dd, blob, micro or batch)
+    xi = torch.from_numpy(np.ascontiguousarray(x, np.int8).reshape(-1)).cuda()
+    out = torch.full((batch * out_elems(d),), 99, dtype=torch.int8, device="cuda")
+    model.forward_device(xi.data_ptr(), out.data_ptr(), batch,
+                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    model.close()
+    return out.cpu().numpy()

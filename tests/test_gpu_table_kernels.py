@@ -1,0 +1,57 @@
+"""Layer-level parity of the constant-table kernels on the B200.
+
+A compiled model builds a host requantisation table for every op whose
+channels all take the fast requant form, and then runs the GEMM and the
+tensor-core depthwise kernel with compile-time table offsets (border
+classes as bias differences, 256-row GEMM tiles for narrow outputs).  These
+tests run single ops through that path and compare every output byte with
+the oracle (the whole-network tests only see the logits, after global
+average pooling)."""
+import numpy as np
+import pytest
+
+from gpu_helpers import conv_desc, make_desc, random_quant, run_op_model
+from pspml import capi
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(got, want):
+    mism = np.flatnonzero(got != want)
+    assert mism.size == 0, (f"{mism.size} of {want.size} differ; first at {mism[:5]}: "
+                            f"got {got[mism[:5]]} want {want[mism[:5]]}")
+
+
+@pytest.mark.parametrize("B,H,W,C,zp_in,act", [
+    (2, 5, 256, 32, -128, (-128, 127)),
+    (3, 4, 128, 64, 0, (-128, 127)),
+    (2, 3, 200, 128, 7, (-20, 90)),      # partial second tile, clamp
+    (1, 6, 384, 96, -3, (-128, 127)),    # three channel groups, three tiles
+    (2, 1, 130, 32, 5, (0, 127)),        # one row: every tile row is a border row
+])
+def test_depthwise_static_table(ctx, oracle_mod, B, H, W, C, zp_in, act):
+    r = np.random.default_rng(7000 + H * W + C)
+    d = conv_desc(capi.OP_DEPTHWISE_CONV2D, H, W, C, C, k=3, stride=1, zp_in=zp_in,
+                  zp_out=-5, act=act)
+    x = r.integers(-128, 128, B * H * W * C).astype(np.int8)
+    w = r.integers(-127, 128, 9 * C).astype(np.int8)
+    b, m, s = random_quant(r, C)
+    got = run_op_model(ctx, d, B, x, w, b, m, s)
+    _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))
+
+
+@pytest.mark.parametrize("B,H,W,K,N,act", [
+    (2, 8, 64, 32, 64, (-128, 127)),     # 256-row tiles
+    (3, 5, 33, 64, 32, (-10, 100)),      # 256-row tiles, ragged last tile, clamp
+    (2, 6, 40, 128, 128, (-128, 127)),
+    (1, 4, 50, 64, 256, (0, 127)),
+])
+def test_pointwise_static_table(ctx, oracle_mod, B, H, W, K, N, act):
+    r = np.random.default_rng(8000 + H * W + K + N)
+    d = make_desc(kind=capi.OP_CONV2D, in_h=H, in_w=W, in_c=K, out_h=H, out_w=W, out_c=N,
+                  zp_in=-128, zp_out=3, act_min=act[0], act_max=act[1])
+    x = r.integers(-128, 128, B * H * W * K).astype(np.int8)
+    w = r.integers(-127, 128, N * K).astype(np.int8)
+    b, m, s = random_quant(r, N)
+    got = run_op_model(ctx, d, B, x, w, b, m, s)
+    _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))

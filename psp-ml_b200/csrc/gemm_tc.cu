@@ -19,11 +19,12 @@
 //   warp 0           TMA producer (one thread), STAGES-deep smem ring
 //   warp 1           tensor-memory allocator + MMA issuer (one thread)
 //   warps 2..2+4G-1  G epilogue groups of 4 warps (one per tensor-memory
-//                    lane quarter).  Group g takes every G-th tile of the
-//                    CTA; NB >= G accumulator buffers in tensor memory let
-//                    the MMAs run ahead of the epilogues.
+//                    lane quarter).  The groups take the CTA's tiles in
+//                    turn; NB accumulator buffers in tensor memory let the
+//                    MMAs run ahead of the epilogues.
 // The epilogue is the critical path for the small-K layers of these
-// networks (K = 32..512), so it gets up to 16 warps.
+// networks (K = 32..512), so it gets up to 16 warps.  Tiles of 256 rows (two
+// M = 128 MMAs per k step) halve the per-tile handoffs for narrow outputs.
 #include <algorithm>
 #include <atomic>
 
@@ -69,7 +70,8 @@ struct TcGemmArgs {
   int32_t clamp;        // act range narrower than int8
   unsigned* err;
   int32_t stages;
-  int32_t b_res;  // the whole B operand (one N tile) stays in smem, loaded once
+  int32_t b_res;  // the CTA's N tile of B stays in smem, loaded once (the grid is a
+                  // multiple of tiles_n, so CTA b always works on N tile b % tiles_n)
 };
 
 constexpr int kParamSmemMax = 32 * 1024;
@@ -194,7 +196,8 @@ enum : int {
   kEpiGeneral = 0,  // tables in smem or global, runtime fast/general requant
   kEpiTable = 1,    // fast requant, tables a kernel parameter, runtime offsets
   kEpiStatic = 2    // as kEpiTable with every offset a compile-time constant:
-                    // 2D A, one N tile (N == BN), 16-byte aligned rows
+                    // 2D A, up to four N tiles (N == tiles_n * BN) with a
+                    // fixed N tile per CTA, 16-byte aligned rows
 };
 template <int MODE>
 struct TabOf {
@@ -246,22 +249,23 @@ __device__ __forceinline__ void epilogue_chunk_tab(uint32_t (&v)[16], int8_t* ds
 // One output row of BN channels with compile-time table offsets: every
 // per-channel constant is a constant-bank operand of the instruction using
 // it.  Tensor-memory loads run one 16-column chunk ahead of the arithmetic.
-template <int BN, bool CLAMP>
+template <int BN, int NOFF, bool CLAMP>
 __device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_t taddr,
                                                     int8_t* orow, bool valid,
                                                     const TcGemmArgs& p) {
+  orow += NOFF;
   uint32_t v0[16], v1[16];
   tmem_ld16_nowait(taddr, v0);
 #pragma unroll
   for (int c = 0; c < BN; c += 32) {
     tmem_wait_ld(v0);
     if (c + 16 < BN) tmem_ld16_nowait(taddr + c + 16, v1);
-    const uint4 w0 = requant16_tab<CLAMP>(v0, tab, c, p.lo4, p.hi4);
+    const uint4 w0 = requant16_tab<CLAMP>(v0, tab, NOFF + c, p.lo4, p.hi4);
     if (valid) *reinterpret_cast<uint4*>(orow + c) = w0;
     if (c + 16 < BN) {
       tmem_wait_ld(v1);
       if (c + 32 < BN) tmem_ld16_nowait(taddr + c + 32, v0);
-      const uint4 w1 = requant16_tab<CLAMP>(v1, tab, c + 16, p.lo4, p.hi4);
+      const uint4 w1 = requant16_tab<CLAMP>(v1, tab, NOFF + c + 16, p.lo4, p.hi4);
       if (valid) *reinterpret_cast<uint4*>(orow + c + 16) = w1;
     }
   }
@@ -352,7 +356,8 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
         for (int it = 0; it < kiters; ++it) {
           const int tap = it / p.kblocks;
           const int kb = it - tap * p.kblocks;
-          tma_load_2d(sB + it * B_BYTES, &tmB, bres_full, tap * p.Kc + kb * BK, 0);
+          tma_load_2d(sB + it * B_BYTES, &tmB, bres_full, tap * p.Kc + kb * BK,
+                      static_cast<int32_t>(blockIdx.x % p.tiles_n) * BN);
         }
       }
       // Tile t = tm * tiles_n + tn, advanced by gridDim.x per step.
@@ -492,10 +497,21 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
       const uint32_t tb0 = tlane + static_cast<uint32_t>(b * kCols);
 
       if constexpr (MODE == kEpiStatic) {
+        // Up to four N tiles; this CTA's is fixed (blockIdx.x % tiles_n).
+        const uint32_t tm = p.fd_tiles_n.div(static_cast<uint32_t>(t));
+        const int tn = static_cast<int>(blockIdx.x % p.tiles_n);
 #pragma unroll 1
         for (int mt = 0; mt < MT; ++mt) {
-          const int64_t r = t * TM + mt * kBM + row;
-          epilogue_row_static<BN, CLAMP>(tab, tb0 + mt * BN, p.out + r * p.ldo, r < p.rows, p);
+          const int64_t r = static_cast<int64_t>(tm) * TM + mt * kBM + row;
+          int8_t* orow = p.out + r * p.ldo;
+          const uint32_t ta = tb0 + static_cast<uint32_t>(mt * BN);
+          const bool ok = r < p.rows;
+          switch (tn) {
+            case 0: epilogue_row_static<BN, 0, CLAMP>(tab, ta, orow, ok, p); break;
+            case 1: epilogue_row_static<BN, BN, CLAMP>(tab, ta, orow, ok, p); break;
+            case 2: epilogue_row_static<BN, 2 * BN, CLAMP>(tab, ta, orow, ok, p); break;
+            default: epilogue_row_static<BN, 3 * BN, CLAMP>(tab, ta, orow, ok, p); break;
+          }
         }
       } else {
 #pragma unroll 1
@@ -599,7 +615,7 @@ cudaError_t launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const T
 }
 
 // Epilogue variant per op: the static constant-table epilogue for 2D
-// operands with a single N tile, the run-time-offset table epilogue for
+// operands with up to four N tiles, the run-time-offset table epilogue for
 // other ops whose host holds a table, the general one (tables in smem or
 // global, runtime fast/general flag) otherwise.
 template <int BN, int BK, int MT>
@@ -607,11 +623,16 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
                    const EpiTable* table, int num_sms, cudaStream_t s) {
   constexpr int A_BYTES = kBM * MT * BK;
   if (table != nullptr) args.param_smem = 0;
-  // Resident B when a single N tile's weights fit next to >= 4 A stages.
+  // A grid that is a multiple of tiles_n (or one tile per CTA) keeps every
+  // CTA on one N tile; its weights then stay resident when they fit next to
+  // >= 4 A stages.
+  int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
+  if (grid < args.tiles_total && args.tiles_n > 1 && num_sms >= args.tiles_n)
+    grid = num_sms / args.tiles_n * args.tiles_n;
+  const bool fixed_n = grid % args.tiles_n == 0 || grid == args.tiles_total;
   const int bres_bytes = args.taps * args.kblocks * BN * BK;
   const int base_overhead = 1024 + 64 * 8 + 64 + args.param_smem;
-  args.b_res = args.tiles_n == 1 && bres_bytes <= 96 * 1024 &&
-               base_overhead + bres_bytes + 4 * A_BYTES <= kSmemLimit;
+  args.b_res = fixed_n && base_overhead + bres_bytes + 4 * A_BYTES <= kSmemLimit;
   const int stage_bytes = args.b_res ? A_BYTES : A_BYTES + BN * BK;
   const int overhead = base_overhead + (args.b_res ? bres_bytes : 0);
   int stages = (kSmemLimit - overhead) / stage_bytes;
@@ -620,13 +641,18 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   // one persistent CTA per SM.
   const int smem = std::max(overhead + stages * stage_bytes, 120 * 1024);
   args.stages = stages;
-  const int64_t grid = std::min<int64_t>(args.tiles_total, num_sms);
   if (grid <= 0) return cudaSuccess;
-  if (table == nullptr)
-    return launch_variant<BN, BK, MT, kEpiGeneral, false>(ma, mb, args, NoTable{0}, grid, smem,
-                                                          s);
-  const bool is_static = !args.conv4d && args.tiles_n == 1 && args.N == BN &&
-                         args.ldo == BN && (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0;
+  if (table == nullptr) {
+    // 256-row tiles only run with a constant table (the host picks MT).
+    if constexpr (MT == 1)
+      return launch_variant<BN, BK, MT, kEpiGeneral, false>(ma, mb, args, NoTable{0}, grid,
+                                                            smem, s);
+    else
+      return cudaErrorInvalidValue;
+  }
+  const bool is_static = !args.conv4d && fixed_n && args.tiles_n <= 4 &&
+                         args.N == args.tiles_n * BN && args.ldo == args.N &&
+                         (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0;
   if (!is_static)
     return launch_variant<BN, BK, MT, kEpiTable, false>(ma, mb, args, *table, grid, smem, s);
   if (args.clamp)
@@ -659,7 +685,12 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
   const bool is_fc = d.kind == PSPML_OP_FULLY_CONNECTED;
   const int Kc = is_fc ? d.in_h * d.in_w * d.in_c : d.in_c;
   const int taps = is_fc ? 1 : d.kernel_h * d.kernel_w;
-  const int bn = N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
+  // With a constant table, N = 257..512 runs as up to four 128-column tiles
+  // (each CTA on one): an epilogue warp then reads 2 KB of the table per
+  // tile, and B stays resident.  (For N <= 256 one 256-column tile is
+  // faster: splitting it makes every CTA pair read A twice.)
+  const bool tab = pp.all_fast_known && pp.table != nullptr;
+  const int bn = N <= 32 ? 32 : N <= 64 ? 64 : (N <= 128 || (tab && N > 256 && N <= 512)) ? 128 : 256;
   const int bk = Kc >= 128 ? 128 : (Kc > 32 ? 64 : 32);
 
   TcGemmArgs a{};
@@ -722,7 +753,7 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
   } else {
     const int64_t rows = is_fc ? batch : batch * d.out_h * d.out_w;
     if (rows >= (1ll << 31) - 2 * kBM) return cudaErrorInvalidValue;
-    mt = bn <= 64 && rows > kBM ? 2 : 1;
+    mt = bn <= 64 && rows > kBM && pp.all_fast_known && pp.table != nullptr ? 2 : 1;
     a.conv4d = 0;
     a.rows = rows;
     a.ldo = N;

@@ -77,7 +77,9 @@ typedef enum pspml_op_kind {
  *                    shift [out_c] int32 (TFLite convention: >0 left shift)
  *  pools: zp_out must equal zp_in (TFLite keeps the input's quantisation).
  *  act_min/act_max clamp the requantised output (ReLU: act_min = zp_out).
- * Offsets are byte offsets into the weight blob, 16-byte aligned, or -1. */
+ * Offsets are byte offsets into the weight blob, 16-byte aligned, or -1.
+ * `flags` is 0 for the int8 ops; the f32 ops below read PSPML_F32_* bits
+ * from it (their zp/act fields are ignored). */
 typedef struct pspml_op_desc {
   int32_t kind;
   int32_t in_h, in_w, in_c;
@@ -87,7 +89,7 @@ typedef struct pspml_op_desc {
   int32_t pad_top, pad_left, pad_bottom, pad_right;
   int32_t zp_in, zp_out;
   int32_t act_min, act_max;
-  int32_t reserved0;
+  int32_t flags;
   int64_t filter_off, bias_off, mult_off, shift_off;
 } pspml_op_desc;
 
@@ -192,6 +194,41 @@ int pspml_max_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
 int pspml_average_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d,
                             int64_t batch, const int8_t* in, int8_t* out,
                             void* stream);
+
+/* ---- f32 ops: the reference's own MNIST path, bit-identical to it ------
+ * NHWC float tensors, device pointers, asynchronous on `stream`.  Every
+ * output is one sequence of separately rounded products and sums in the
+ * reference's order (no fused multiply-add), so results equal the
+ * reference's exactly.  Bits of pspml_op_desc.flags: */
+#define PSPML_F32_RELU 1       /* then `if (v < 0) v = 0` (keeps -0.0)      */
+#define PSPML_F32_GEMM_ORDER 2 /* conv: im2col_padded -> matmul_bt_tiled ->
+                                  bias_add order (psp-ml/src/kernels/
+                                  mod.rs:176-479, what the reference's
+                                  codegen emits): the sum starts at 0, runs
+                                  over k in (ky, kx, ci) order including
+                                  out-of-image taps (as 0) and the zero
+                                  columns up to a multiple of 4, then adds
+                                  the bias.  Without it: naive::conv2d
+                                  (naive.rs:13-92), the sum starts at the
+                                  bias and skips out-of-image taps.        */
+
+/* Replaces the reference's conv lowering (mod.rs:176-479 with
+ * PSPML_F32_GEMM_ORDER) or naive::conv2d[_relu] (naive.rs:13-92).
+ * filter [out_c][kernel_h][kernel_w][in_c]; bias [out_c] or NULL. */
+int pspml_conv2d_f32(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
+                     const float* in, const float* filter, const float* bias,
+                     float* out, void* stream);
+
+/* Replaces naive::max_pool2d (naive.rs:98-132): -inf start, strict `>`. */
+int pspml_max_pool2d_f32(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
+                         const float* in, float* out, void* stream);
+
+/* Replaces naive::fully_connected[_relu] (naive.rs:147-184): the sum starts
+ * at bias[o] and adds the inputs in order.  filter [out_c][in_h*in_w*in_c]. */
+int pspml_fully_connected_f32(pspml_ctx* ctx, const pspml_op_desc* d,
+                              int64_t batch, const float* in,
+                              const float* filter, const float* bias,
+                              float* out, void* stream);
 
 /* ------------------------------------------------------------ model level
  * The compiled-model counterpart of the generated forward()

@@ -343,4 +343,51 @@ int pspml_average_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batc
                      "average pool");
 }
 
+// ---- f32 ops (the reference's own MNIST path)
+
+int pspml_conv2d_f32(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch, const float* in,
+                     const float* filter, const float* bias, float* out, void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_CONV2D) return set_error(PSPML_ERR_INVALID_ARG, "not a CONV2D op");
+  if ((st = check_op_ptrs(ctx, in, out, batch))) return st;
+  if (filter == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null filter");
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  return cuda_status(
+      launch_conv2d_f32(*d, batch, in, filter, bias, out, static_cast<cudaStream_t>(stream)),
+      "f32 conv");
+}
+
+int pspml_max_pool2d_f32(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch, const float* in,
+                         float* out, void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_MAX_POOL2D) return set_error(PSPML_ERR_INVALID_ARG, "not MAX_POOL2D");
+  if ((st = check_op_ptrs(ctx, in, out, batch))) return st;
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  return cuda_status(launch_max_pool2d_f32(*d, batch, in, out, static_cast<cudaStream_t>(stream)),
+                     "f32 max pool");
+}
+
+int pspml_fully_connected_f32(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
+                              const float* in, const float* filter, const float* bias,
+                              float* out, void* stream) {
+  clear_error();
+  int st = validate_desc(d);
+  if (st) return st;
+  if (d->kind != PSPML_OP_FULLY_CONNECTED)
+    return set_error(PSPML_ERR_INVALID_ARG, "not a FULLY_CONNECTED op");
+  if ((st = check_op_ptrs(ctx, in, out, batch))) return st;
+  if (filter == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null filter");
+  if (batch == 0) return PSPML_OK;
+  cudaSetDevice(ctx->device);
+  return cuda_status(launch_fully_connected_f32(*d, batch, in, filter, bias, out,
+                                                static_cast<cudaStream_t>(stream)),
+                     "f32 fully connected");
+}
+
 }  // extern "C"

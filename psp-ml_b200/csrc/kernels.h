@@ -193,6 +193,16 @@ cudaError_t launch_maxpool(const pspml_op_desc& d, int64_t batch, const int8_t* 
 cudaError_t launch_avgpool(const pspml_op_desc& d, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s);
 
+// ---- f32 kernels of the reference's own MNIST path (f32.cu)
+cudaError_t launch_conv2d_f32(const pspml_op_desc& d, int64_t batch, const float* in,
+                              const float* filter, const float* bias, float* out,
+                              cudaStream_t s);
+cudaError_t launch_max_pool2d_f32(const pspml_op_desc& d, int64_t batch, const float* in,
+                                  float* out, cudaStream_t s);
+cudaError_t launch_fully_connected_f32(const pspml_op_desc& d, int64_t batch, const float* in,
+                                       const float* w, const float* bias, float* out,
+                                       cudaStream_t s);
+
 // ---- preparation kernels (prep.cu)
 cudaError_t launch_fold_bias(const pspml_op_desc& d, const int8_t* filter, const int32_t* bias,
                              const BorderClasses& bc, int32_t* bias_eff, cudaStream_t s);

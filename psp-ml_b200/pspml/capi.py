@@ -37,12 +37,16 @@ OP_MAX_POOL2D = 4
 OP_AVERAGE_POOL2D = 5
 OP_RESHAPE = 6
 
+# pspml_op_desc.flags bits of the f32 ops
+F32_RELU = 1
+F32_GEMM_ORDER = 2
+
 # Byte-for-byte layout of struct pspml_op_desc.
 OP_DESC_FIELDS_I32 = (
     "kind", "in_h", "in_w", "in_c", "out_h", "out_w", "out_c",
     "kernel_h", "kernel_w", "stride_h", "stride_w",
     "pad_top", "pad_left", "pad_bottom", "pad_right",
-    "zp_in", "zp_out", "act_min", "act_max", "reserved0",
+    "zp_in", "zp_out", "act_min", "act_max", "flags",
 )
 OP_DESC_FIELDS_I64 = ("filter_off", "bias_off", "mult_off", "shift_off")
 OP_DESC_DTYPE = np.dtype(
@@ -95,6 +99,9 @@ _PROTOS = {
                                          [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "pspml_max_pool2d_s8": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
     "pspml_average_pool2d_s8": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
+    "pspml_conv2d_f32": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "pspml_max_pool2d_f32": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
+    "pspml_fully_connected_f32": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),
     "pspml_model_create": (ctypes.c_int, [_vp, _vp, _i32, _vp, _sz, _i32, ctypes.POINTER(_vp)]),
     "pspml_model_destroy": (ctypes.c_int, [_vp]),
     "pspml_model_info": (ctypes.c_int, [_vp, ctypes.POINTER(_sz), ctypes.POINTER(_sz),

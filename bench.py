@@ -135,19 +135,22 @@ class ClockSampler:
 def oracle_rate(net, descs, blob, target_s=12.0, probe=4):
     """Oracle inferences/s on all host cores over a bounded sample."""
     from oracle import oracle as orc
+    threads = host_threads()
     x = net.make_input(probe, tag="cpu-probe")
     t0 = time.perf_counter()
-    orc.net_forward_s8(descs, blob, x)
+    orc.net_forward_s8(descs, blob, x, threads=threads)
     dt = max(time.perf_counter() - t0, 1e-6)
     n = int(min(4096, max(probe, target_s * probe / dt)))
     x = net.make_input(n, tag="cpu-sample")
     t0 = time.perf_counter()
-    orc.net_forward_s8(descs, blob, x)
+    orc.net_forward_s8(descs, blob, x, threads=threads)
     dt = time.perf_counter() - t0
     return n / dt, n, dt
 
 
 def host_threads():
+    """Host cores this process may use (passed explicitly to the oracle:
+    torchrun sets OMP_NUM_THREADS=1 for its workers)."""
     try:
         return len(os.sched_getaffinity(0))
     except Exception:
@@ -166,16 +169,16 @@ def run_reference(args, wl, rank, world):
     rate0, _, _ = oracle_rate(net, descs, blob, target_s=min(5.0, budget), probe=4)
     n = int(max(4, min(2048, rate0 * min(budget, 20.0))))
     x = net.make_input(n, tag="reference-arm")
+    threads = host_threads()
     for _ in range(args.warmup):
-        orc.net_forward_s8(descs, blob, x[: max(1, n // 8)])
+        orc.net_forward_s8(descs, blob, x[: max(1, n // 8)], threads=threads)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        orc.net_forward_s8(descs, blob, x)
+        orc.net_forward_s8(descs, blob, x, threads=threads)
         times.append(time.perf_counter() - t0)
     ms = 1000.0 * statistics.mean(times)
     value = n / (ms / 1000.0)
-    threads = host_threads()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,

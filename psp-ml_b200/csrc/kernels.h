@@ -100,6 +100,17 @@ __device__ __forceinline__ void add_class_delta(uint32_t* v, const EpiTable& tab
     if (j < cnt) v[j] += static_cast<uint32_t>(tab.dbias[off + j]);
 }
 
+// Constant table of a fused depthwise + pointwise pair (dwpw_tc.cu): the
+// depthwise op's split constants and per-class bias differences (up to 9
+// border classes x 128 channels), the pointwise op's split constants.
+struct DwPwTable {
+  int2 dw_mh[128];
+  int2 dw_bs[128];
+  int32_t dw_dbias[9 * 128];
+  int2 pw_mh[256];
+  int2 pw_bs[256];
+};
+
 // Unsigned division by a divisor fixed at launch, for numerators below 2^31:
 // q = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
 // m = floor(2^32 (2^l - d) / d) + 1 (the round-up multiplier method of
@@ -151,6 +162,17 @@ cudaError_t prepare_dw_tc(const pspml_op_desc& d, const int8_t* filter, const in
 cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                          const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                          cudaStream_t s);
+
+// Fused depthwise 3x3 + pointwise 1x1 pair (dwpw_tc.cu).
+bool dwpw_pair_supported(const pspml_op_desc& dw, const pspml_op_desc& pw);
+size_t dwpw_packed_bytes(const pspml_op_desc& pw);
+// [N][C] pointwise filter -> [C/16][N][16] (K-major core-matrix order).
+cudaError_t pack_pw_kmajor(const int8_t* filter, int32_t N, int32_t C, uint8_t* out,
+                           cudaStream_t s);
+cudaError_t launch_dwpw(const pspml_op_desc& dw, const PreparedOp& pdw, const pspml_op_desc& pw,
+                        const uint8_t* wpw_packed, const DwPwTable& tab, int64_t batch,
+                        const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                        cudaStream_t s);
 
 // Path for op `d` given operand alignment (16-byte aligned pointers allow the
 // TMA / vector paths).

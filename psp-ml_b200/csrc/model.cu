@@ -78,9 +78,26 @@ int forward_chunk(pspml_model* m, const int8_t* in, int8_t* out, int64_t mb, cud
   std::vector<int8_t*> ptrs;
   op_pointers(m, in, out, &ptrs);
   if (events) cudaEventRecord((*events)[0], s);
+  auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   for (size_t i = 0; i < m->ops.size(); ++i) {
+    const ModelOp& op = m->ops[i];
     const int8_t* src = i == 0 ? in : ptrs[i - 1];
-    const int st = run_op(m, m->ops[i], mb, src, ptrs[i], s);
+    if (op.fuse == 1 && aligned(src) && aligned(ptrs[i + 1])) {
+      // Depthwise + pointwise in one kernel; the pair's time is the
+      // depthwise op's, the pointwise op records none.
+      const ModelOp& pw = m->ops[i + 1];
+      const int st = cuda_status(launch_dwpw(op.d, op.prep, pw.d, op.wpw, *op.pair_table, mb, src,
+                                             ptrs[i + 1], m->ctx->dev_err, m->ctx->num_sms, s),
+                                 "fused depthwise + pointwise");
+      if (st) return st;
+      if (events) {
+        cudaEventRecord((*events)[i + 1], s);
+        cudaEventRecord((*events)[i + 2], s);
+      }
+      ++i;
+      continue;
+    }
+    const int st = run_op(m, op, mb, src, ptrs[i], s);
     if (st) return st;
     if (events) cudaEventRecord((*events)[i + 1], s);
   }
@@ -133,6 +150,7 @@ int pspml_model_destroy(pspml_model* m) {
     if (s) cudaStreamDestroy(s);
   if (m->arena) cudaFree(m->arena);
   if (m->weights) cudaFree(m->weights);
+  if (m->pair_weights) cudaFree(m->pair_weights);
   delete m;
   return PSPML_OK;
 }
@@ -271,6 +289,57 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
           t->dbias[k * n + c] = bias[static_cast<size_t>(k) * n + c] - bias[base + c];
     p.table = t.get();
     m->tables.push_back(std::move(t));
+  }
+
+  // Depthwise + pointwise pairs that run as one kernel: both ops hold a
+  // constant table, the shapes are instantiated, and the pointwise op reads
+  // only the depthwise output (the op list is a chain).
+  if (!st) {
+    std::vector<int> pairs;
+    size_t pair_bytes = 0;
+    for (int i = 0; i + 1 < n_ops; ++i) {
+      ModelOp& a = m->ops[i];
+      ModelOp& b = m->ops[i + 1];
+      if (a.fuse || b.fuse || a.d.kind != PSPML_OP_DEPTHWISE_CONV2D) continue;
+      if (a.prep.path != OpPath::kDwTc || b.prep.path != OpPath::kTc2d) continue;
+      if (a.prep.table == nullptr || b.prep.table == nullptr || !a.prep.all_fast_known ||
+          !b.prep.all_fast_known)
+        continue;
+      if (!dwpw_pair_supported(a.d, b.d) || a.prep.ncls > 9) continue;
+      auto t = std::make_unique<DwPwTable>();
+      std::memset(t.get(), 0, sizeof(DwPwTable));
+      const int C = a.d.in_c, N = b.d.out_c;
+      for (int c = 0; c < C; ++c) {
+        t->dw_mh[c] = a.prep.table->mh[c];
+        t->dw_bs[c] = a.prep.table->bs[c];
+      }
+      for (int k = 0; k < a.prep.ncls; ++k)
+        for (int c = 0; c < C; ++c) t->dw_dbias[k * C + c] = a.prep.table->dbias[k * C + c];
+      for (int c = 0; c < N; ++c) {
+        t->pw_mh[c] = b.prep.table->mh[c];
+        t->pw_bs[c] = b.prep.table->bs[c];
+      }
+      a.fuse = 1;
+      b.fuse = 2;
+      a.pair_table = t.get();
+      m->pair_tables.push_back(std::move(t));
+      pairs.push_back(i);
+      pair_bytes += align_up(dwpw_packed_bytes(b.d), 256);
+    }
+    if (!pairs.empty()) {
+      st = cuda_status(cudaMalloc(&m->pair_weights, pair_bytes), "cudaMalloc(pair weights)");
+      size_t off = 0;
+      for (int i : pairs) {
+        if (st) break;
+        const ModelOp& b = m->ops[i + 1];
+        m->ops[i].wpw = m->pair_weights + off;
+        st = cuda_status(pack_pw_kmajor(b.prep.filter, b.d.out_c, b.d.in_c,
+                                        m->pair_weights + off, ctx->stream),
+                         "pack pair weights");
+        off += align_up(dwpw_packed_bytes(b.d), 256);
+      }
+      if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "pack pair weights");
+    }
   }
 
   // Arena: op i's output lives from op i until the last op reading it

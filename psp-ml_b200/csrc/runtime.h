@@ -43,6 +43,11 @@ struct ModelOp {
   int64_t out_elems = 0;      // per sample
   int64_t in_elems = 0;
   bool alias_input = false;   // reshape: output is the input buffer
+  // Fused depthwise + pointwise pair: 1 on the depthwise op (which then
+  // runs both ops in one kernel), 2 on the pointwise op (skipped).
+  int fuse = 0;
+  const pspml::DwPwTable* pair_table = nullptr;
+  const uint8_t* wpw = nullptr;  // packed pointwise weights of the pair
 };
 
 }  // namespace pspml
@@ -63,5 +68,7 @@ struct pspml_model {
   cudaEvent_t ev_done = nullptr;
   std::vector<cudaEvent_t> op_events;
   std::vector<std::unique_ptr<pspml::EpiTable>> tables;  // constant-table epilogues
+  std::vector<std::unique_ptr<pspml::DwPwTable>> pair_tables;
+  uint8_t* pair_weights = nullptr;  // device: packed pointwise weights of fused pairs
   std::mutex mu;
 };

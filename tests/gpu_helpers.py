@@ -104,12 +104,21 @@ def run_op_model(ctx, d, batch, x, filt, bias, mult, shift, micro=None):
     the model; the host builds the constant requant table when every
     channel takes the fast form, so this exercises the constant-table
     kernels); returns the int8 output (host)."""
+    return run_chain_model(ctx, [(d, filt, bias, mult, shift)], batch, x, micro)
+
+
+def run_chain_model(ctx, ops, batch, x, micro=None):
+    """Runs a chain of weighted ops [(desc, filter, bias, mult, shift)] as
+    one compiled model; returns the last op's int8 output (host)."""
     import torch
 
-    parts = [np.ascontiguousarray(filt, np.int8).view(np.uint8).reshape(-1),
-             np.ascontiguousarray(bias, np.int32).view(np.uint8).reshape(-1),
-             np.ascontiguousarray(mult, np.int32).view(np.uint8).reshape(-1),
-             np.ascontiguousarray(shift, np.int32).view(np.uint8).reshape(-1)]
+    parts, descs = [], []
+    for d, filt, bias, mult, shift in ops:
+        parts += [np.ascontiguousarray(filt, np.int8).view(np.uint8).reshape(-1),
+                  np.ascontiguousarray(bias, np.int32).view(np.uint8).reshape(-1),
+                  np.ascontiguousarray(mult, np.int32).view(np.uint8).reshape(-1),
+                  np.ascontiguousarray(shift, np.int32).view(np.uint8).reshape(-1)]
+        descs.append(np.array(d).reshape(1).copy())
     offs, pos = [], 0
     for a in parts:
         offs.append(pos)
@@ -117,11 +126,13 @@ def run_op_model(ctx, d, batch, x, filt, bias, mult, shift, micro=None):
     blob = np.zeros(pos, np.uint8)
     for o, a in zip(offs, parts):
         blob[o:o + a.size] = a
-    dd = np.array(d).reshape(1).copy()
-    dd["filter_off"], dd["bias_off"], dd["mult_off"], dd["shift_off"] = offs
+    dd = np.concatenate(descs)
+    for i in range(len(ops)):
+        (dd["filter_off"][i], dd["bias_off"][i], dd["mult_off"][i],
+         dd["shift_off"][i]) = offs[4 * i:4 * i + 4]
     model = capi.Model(ctx, dd, blob, micro or batch)
     xi = torch.from_numpy(np.ascontiguousarray(x, np.int8).reshape(-1)).cuda()
-    out = torch.full((batch * out_elems(d),), 99, dtype=torch.int8, device="cuda")
+    out = torch.full((batch * out_elems(ops[-1][0]),), 99, dtype=torch.int8, device="cuda")
     model.forward_device(xi.data_ptr(), out.data_ptr(), batch,
                          torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()

@@ -10,7 +10,7 @@ average pooling)."""
 import numpy as np
 import pytest
 
-from gpu_helpers import conv_desc, make_desc, random_quant, run_op_model
+from gpu_helpers import conv_desc, make_desc, random_quant, run_chain_model, run_op_model
 from pspml import capi
 
 pytestmark = pytest.mark.gpu
@@ -55,3 +55,30 @@ def test_pointwise_static_table(ctx, oracle_mod, B, H, W, K, N, act):
     b, m, s = random_quant(r, N)
     got = run_op_model(ctx, d, B, x, w, b, m, s)
     _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))
+
+
+@pytest.mark.parametrize("B,H,W,C,N,dw_act,pw_act", [
+    (2, 4, 256, 32, 64, (-128, 127), (-128, 127)),   # config-3 block 0
+    (2, 3, 256, 64, 64, (-128, 127), (-128, 127)),   # block 1
+    (2, 2, 200, 64, 64, (-100, 120), (-20, 90)),      # partial tile, both clamps
+    (1, 5, 130, 32, 64, (0, 127), (-128, 127)),
+    (3, 3, 128, 128, 128, (-128, 127), (-128, 127)),  # not fused: two kernels
+])
+def test_depthwise_pointwise_pair(ctx, oracle_mod, B, H, W, C, N, dw_act, pw_act):
+    """A depthwise conv followed by a 1x1 conv: the compiled model runs the
+    pair as one kernel where the shapes allow (the depthwise output stays in
+    shared memory); the pointwise output must equal the oracle's two ops in
+    sequence."""
+    r = np.random.default_rng(9000 + H * W + C + N)
+    dw = conv_desc(capi.OP_DEPTHWISE_CONV2D, H, W, C, C, k=3, stride=1, zp_in=-7, zp_out=4,
+                   act=dw_act)
+    pw = make_desc(kind=capi.OP_CONV2D, in_h=H, in_w=W, in_c=C, out_h=H, out_w=W, out_c=N,
+                   zp_in=4, zp_out=-2, act_min=pw_act[0], act_max=pw_act[1])
+    x = r.integers(-128, 128, B * H * W * C).astype(np.int8)
+    wd = r.integers(-127, 128, 9 * C).astype(np.int8)
+    bd, md, sd = random_quant(r, C)
+    wp = r.integers(-127, 128, N * C).astype(np.int8)
+    bp, mp, sp = random_quant(r, N)
+    got = run_chain_model(ctx, [(dw, wd, bd, md, sd), (pw, wp, bp, mp, sp)], B, x)
+    mid = oracle_mod.op_s8(dw, B, x, wd, bd, md, sd)
+    _check(got, oracle_mod.op_s8(pw, B, mid, wp, bp, mp, sp))

@@ -70,10 +70,15 @@ def peaks():
 
 
 # ------------------------------------------------------------ layer model
-def layer_model(net):
-    """Per-sample algorithmic bytes and ops of every op (weights per launch)."""
+def layer_model(net, fused=None):
+    """Per-sample algorithmic bytes and ops of every kernel launch (weights
+    per launch).  `fused[i] == 1` marks op i as running op i+1 in the same
+    kernel: the pair is one entry ("<op>+pw") whose bytes are op i's input
+    and op i+1's output (the intermediate stays on chip); op i+1 then has
+    no launch of its own."""
     out = []
-    for l in net.layers:
+    fused = fused or [0] * len(net.layers)
+    for i, l in enumerate(net.layers):
         ie = int(np.prod(l.in_shape))
         oe = int(np.prod(l.out_shape))
         alias = l.kind == capi.OP_RESHAPE
@@ -81,6 +86,18 @@ def layer_model(net):
                         weight_bytes=l.weight_bytes, ops_per_sample=2 * l.macs_per_sample,
                         launches_per_chunk=0 if alias else 1,
                         tensor=l.kind in (capi.OP_CONV2D, capi.OP_FULLY_CONNECTED)))
+    for i, l in enumerate(net.layers):
+        if fused[i] == 1 and i + 1 < len(net.layers):
+            nxt = net.layers[i + 1]
+            a, b = out[i], out[i + 1]
+            a["name"] = f"{l.name}+pw"
+            a["bytes_per_sample"] = int(np.prod(l.in_shape)) + int(np.prod(nxt.out_shape))
+            a["weight_bytes"] += b["weight_bytes"]
+            a["ops_per_sample"] += b["ops_per_sample"]
+            a["tensor"] = True
+            b["launches_per_chunk"] = 0
+            b["bytes_per_sample"] = 0
+            b["ops_per_sample"] = 0
     return out
 
 
@@ -254,7 +271,7 @@ def run_ours(args, wl, rank, world, local_rank):
     y_dev = torch.empty(max(1, n_local) * out_e, dtype=torch.int8, device=dev)
     torch.cuda.synchronize()
 
-    ops = layer_model(net)
+    ops = layer_model(net, [model.op_fused(i) for i in range(len(net.layers))])
     n_ops = len(ops)
     chunks = -(-n_local // micro)
 

@@ -249,6 +249,13 @@ int pspml_model_destroy(pspml_model* m);
 int pspml_model_info(const pspml_model* m, size_t* in_bytes_per_sample,
                      size_t* out_bytes_per_sample, size_t* arena_bytes);
 
+/* How op `op` runs (no counterpart in the reference, whose ops are one call
+ * each): *fused = 0 on its own, 1 if its kernel also computes op + 1 (a
+ * depthwise conv fused with the 1x1 conv after it), 2 if op - 1's kernel
+ * computes it.  Per-op times of pspml_forward_timed put a fused pair's time
+ * on the first op. */
+int pspml_model_op_fused(const pspml_model* m, int32_t op, int32_t* fused);
+
 /* Device-resident forward: `batch` samples from dev_in to dev_out,
  * micro-batched, asynchronous on `stream`. */
 int pspml_forward_device(pspml_model* m, const int8_t* dev_in, int8_t* dev_out,

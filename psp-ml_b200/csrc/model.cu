@@ -414,6 +414,14 @@ int pspml_model_info(const pspml_model* m, size_t* in_bytes_per_sample,
   return PSPML_OK;
 }
 
+int pspml_model_op_fused(const pspml_model* m, int32_t op, int32_t* fused) {
+  clear_error();
+  if (m == nullptr || fused == nullptr || op < 0 || op >= static_cast<int32_t>(m->ops.size()))
+    return set_error(PSPML_ERR_INVALID_ARG, "bad model op query");
+  *fused = m->ops[op].fuse;
+  return PSPML_OK;
+}
+
 int pspml_forward_device(pspml_model* m, const int8_t* dev_in, int8_t* dev_out, int64_t batch,
                          void* stream) {
   clear_error();

@@ -106,6 +106,7 @@ _PROTOS = {
     "pspml_model_destroy": (ctypes.c_int, [_vp]),
     "pspml_model_info": (ctypes.c_int, [_vp, ctypes.POINTER(_sz), ctypes.POINTER(_sz),
                                         ctypes.POINTER(_sz)]),
+    "pspml_model_op_fused": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_i32)]),
     "pspml_forward_device": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp]),
     "pspml_forward": (ctypes.c_int, [_vp, _vp, _vp, _i64, ctypes.POINTER(Timing)]),
     "pspml_forward_sharded": (ctypes.c_int, [ctypes.POINTER(_vp), _i32, _vp, _vp, _i64,
@@ -223,6 +224,13 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    def op_fused(self, op: int) -> int:
+        """0: op runs on its own; 1: its kernel also computes op + 1; 2: op - 1's
+        kernel computes it."""
+        f = ctypes.c_int32()
+        call("pspml_model_op_fused", self.handle, op, ctypes.byref(f))
+        return f.value
 
     def forward_device(self, dev_in: int, dev_out: int, batch: int, stream: int = 0) -> None:
         call("pspml_forward_device", self.handle, dev_in, dev_out, batch, stream)

@@ -281,6 +281,65 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// Constant-table variant for 32 output channels and a patch of at most 16
+// bytes (the stem conv): weights and requant constants are kernel-parameter
+// operands at compile-time offsets, so the only loads are the input patch
+// (the smem/global tables made the L1 pipe the bottleneck).
+template <int KH, int KW, int CI, bool CLAMP>
+__global__ void __launch_bounds__(128)
+    k_small_conv_tab_s8(const int8_t* __restrict__ in, int8_t* __restrict__ out, const Geom g,
+                        int64_t n_base, const __grid_constant__ SmallConvTable tab) {
+  constexpr int K = KH * KW * CI;
+  constexpr int NW = (K + 3) / 4;
+  static_assert(NW <= 4, "patch of at most 16 bytes");
+  const int pix = blockIdx.x * 128 + threadIdx.x;
+  if (pix >= g.Ho * g.Wo) return;
+  const int oy = pix / g.Wo, ox = pix - (pix / g.Wo) * g.Wo;
+  const int64_t n = n_base + blockIdx.z;
+  const int8_t* img = in + n * static_cast<int64_t>(g.H) * g.W * CI;
+  uint32_t x[NW];
+#pragma unroll
+  for (int i = 0; i < NW; ++i) x[i] = 0;
+  const uint32_t zpb = static_cast<uint32_t>(g.zp_in) & 0xFFu;
+#pragma unroll
+  for (int ky = 0; ky < KH; ++ky) {
+    const int iy = oy * g.sh - g.pt + ky;
+#pragma unroll
+    for (int kx = 0; kx < KW; ++kx) {
+      const int ix = ox * g.sw - g.pl + kx;
+      const bool ok = iy >= 0 && iy < g.H && ix >= 0 && ix < g.W;
+      const int8_t* px = img + (static_cast<int64_t>(ok ? iy : 0) * g.W + (ok ? ix : 0)) * CI;
+#pragma unroll
+      for (int ci = 0; ci < CI; ++ci) {
+        const int k = (ky * KW + kx) * CI + ci;
+        const uint32_t b = ok ? static_cast<uint32_t>(static_cast<uint8_t>(__ldg(px + ci))) : zpb;
+        x[k >> 2] |= b << (8 * (k & 3));
+      }
+    }
+  }
+  uint32_t words[8];
+#pragma unroll
+  for (int c4 = 0; c4 < 8; ++c4) {
+    int32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int co = 4 * c4 + j;
+      int32_t acc = 0;
+#pragma unroll
+      for (int w = 0; w < NW; ++w)
+        acc = __dp4a(static_cast<int>(x[w]), static_cast<int>(tab.w[co][w]), acc);
+      const int2 bs = tab.bs[co];
+      r[j] = rq_tab(acc + bs.x, tab.mh[co], bs.y);
+    }
+    uint32_t w4 = pack_sat4(r[0], r[1], r[2], r[3]);
+    if constexpr (CLAMP) w4 = clamp4(w4, g.lo4, g.hi4);
+    words[c4] = w4;
+  }
+  uint4* op = reinterpret_cast<uint4*>(out + ((n * g.Ho + oy) * static_cast<int64_t>(g.Wo) + ox) * 32);
+  op[0] = make_uint4(words[0], words[1], words[2], words[3]);
+  op[1] = make_uint4(words[4], words[5], words[6], words[7]);
+}
+
 // ------------------------------------------------------------- direct conv
 // Fallback for any conv: one thread per (sample, oy, ox) and COB output
 // channels; weights of the chunk in shared memory as int32 [K][COB].
@@ -522,9 +581,26 @@ bool small_conv_supported(const pspml_op_desc& d) {
   return d.in_c == 1 || d.in_c == 2 || d.in_c == 3 || d.in_c == 4 || d.in_c == 8;
 }
 
+template <int CI>
+cudaError_t small_conv_tab(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
+                           int8_t* out, cudaStream_t s) {
+  for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
+    const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
+    const dim3 grid((g.Ho * g.Wo + 127) / 128, 1, nz);
+    if (g.clamp)
+      k_small_conv_tab_s8<3, 3, CI, true><<<grid, 128, 0, s>>>(in, out, g, n0, *p.sc_table);
+    else
+      k_small_conv_tab_s8<3, 3, CI, false><<<grid, 128, 0, s>>>(in, out, g, n0, *p.sc_table);
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_small_conv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                               const int8_t* in, int8_t* out, cudaStream_t s) {
   const Geom g = geom_of(d);
+  if (p.sc_table != nullptr && p.all_fast_known && d.out_c == 32 && d.in_c == 1 &&
+      d.kernel_h == 3 && d.kernel_w == 3 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0)
+    return small_conv_tab<1>(g, p, batch, in, out, s);
   switch (d.in_c) {
     case 1: return small_conv_cob<3, 3, 1>(g, p, batch, in, out, s);
     case 2: return small_conv_cob<3, 3, 2>(g, p, batch, in, out, s);

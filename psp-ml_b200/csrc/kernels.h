@@ -111,6 +111,15 @@ struct DwPwTable {
   int2 pw_bs[256];
 };
 
+// Constant table of a small-channel conv with 32 output channels and a
+// patch of at most 16 bytes (the stem): split requant constants, folded
+// bias (all taps, zp-filled halo) and the patch-order weight words.
+struct SmallConvTable {
+  int2 mh[32];
+  int2 bs[32];  // {folded bias, right shift - 1}
+  uint32_t w[32][4];
+};
+
 // Unsigned division by a divisor fixed at launch, for numerators below 2^31:
 // q = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
 // m = floor(2^32 (2^l - d) / d) + 1 (the round-up multiplier method of
@@ -147,6 +156,7 @@ struct PreparedOp {
   uint8_t* xcls = nullptr;          // [out_w]
   int32_t ncls = 1, n_xcls = 1;
   int32_t base_cls = 0;             // border class of an interior pixel (the table's base)
+  const SmallConvTable* sc_table = nullptr;  // host copy (kSmallConv with 32 outputs)
 };
 
 // Input-channel / kernel shapes k_small_conv_s8 is instantiated for.

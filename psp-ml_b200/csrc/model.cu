@@ -291,6 +291,41 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     m->tables.push_back(std::move(t));
   }
 
+  // Constant tables of the small-channel convs with 32 outputs and a patch
+  // of at most 16 bytes (the stem): requant constants, folded bias and the
+  // patch-order weight words.
+  for (int i = 0; i < n_ops && !st; ++i) {
+    PreparedOp& p = m->ops[i].prep;
+    const pspml_op_desc& d = m->ops[i].d;
+    if (p.path != OpPath::kSmallConv || !p.all_fast_known || d.out_c != 32 || d.in_c != 1 ||
+        d.kernel_h != 3 || d.kernel_w != 3 || p.nw < 3)
+      continue;
+    std::vector<RqChannel> rq(32);
+    std::vector<int32_t> bias(32);
+    std::vector<uint32_t> w(static_cast<size_t>(32) * p.nw);
+    st = cuda_status(cudaMemcpy(rq.data(), p.rq, 32 * sizeof(RqChannel), cudaMemcpyDeviceToHost),
+                     "table copy");
+    if (!st)
+      st = cuda_status(cudaMemcpy(bias.data(), p.bias_eff, 32 * 4, cudaMemcpyDeviceToHost),
+                       "table copy");
+    if (!st)
+      st = cuda_status(cudaMemcpy(w.data(), p.wpack, w.size() * 4, cudaMemcpyDeviceToHost),
+                       "table copy");
+    if (st) break;
+    bool low_word_fixed = true;
+    for (const RqChannel& q : rq) low_word_fixed = low_word_fixed && q.c_lo == 0x40000000u;
+    if (!low_word_fixed) continue;
+    auto t = std::make_unique<SmallConvTable>();
+    std::memset(t.get(), 0, sizeof(SmallConvTable));
+    for (int c = 0; c < 32; ++c) {
+      t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
+      t->bs[c] = make_int2(bias[c], rq[c].sr);
+      for (int j = 0; j < 4 && j < p.nw; ++j) t->w[c][j] = w[static_cast<size_t>(c) * p.nw + j];
+    }
+    p.sc_table = t.get();
+    m->sc_tables.push_back(std::move(t));
+  }
+
   // Depthwise + pointwise pairs that run as one kernel: both ops hold a
   // constant table, the shapes are instantiated, and the pointwise op reads
   // only the depthwise output (the op list is a chain).

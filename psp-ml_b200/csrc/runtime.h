@@ -69,6 +69,7 @@ struct pspml_model {
   std::vector<cudaEvent_t> op_events;
   std::vector<std::unique_ptr<pspml::EpiTable>> tables;  // constant-table epilogues
   std::vector<std::unique_ptr<pspml::DwPwTable>> pair_tables;
+  std::vector<std::unique_ptr<pspml::SmallConvTable>> sc_tables;
   uint8_t* pair_weights = nullptr;  // device: packed pointwise weights of fused pairs
   std::mutex mu;
 };

@@ -82,3 +82,22 @@ def test_depthwise_pointwise_pair(ctx, oracle_mod, B, H, W, C, N, dw_act, pw_act
     got = run_chain_model(ctx, [(dw, wd, bd, md, sd), (pw, wp, bp, mp, sp)], B, x)
     mid = oracle_mod.op_s8(dw, B, x, wd, bd, md, sd)
     _check(got, oracle_mod.op_s8(pw, B, mid, wp, bp, mp, sp))
+
+
+@pytest.mark.parametrize("B,H,W,stride,zp_in,act", [
+    (2, 96, 512, 2, 0, (-128, 127)),     # the config-3 stem
+    (3, 17, 33, 2, -5, (-20, 100)),      # odd sizes, clamp
+    (2, 9, 10, 1, 3, (0, 127)),
+])
+def test_stem_conv_static_table(ctx, oracle_mod, B, H, W, stride, zp_in, act):
+    """3x3 conv with one input and 32 output channels: the compiled model
+    runs it with the weights and requant constants as kernel-parameter
+    operands."""
+    r = np.random.default_rng(7700 + H * W + stride)
+    d = conv_desc(capi.OP_CONV2D, H, W, 1, 32, k=3, stride=stride, zp_in=zp_in, zp_out=-128,
+                  act=act)
+    x = r.integers(-128, 128, B * H * W).astype(np.int8)
+    w = r.integers(-127, 128, 32 * 9).astype(np.int8)
+    b, m, s = random_quant(r, 32)
+    got = run_op_model(ctx, d, B, x, w, b, m, s)
+    _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))

@@ -34,7 +34,8 @@ constexpr int kAStage = 6 * kRegion;   // 3 rows x 2 halves
 constexpr int kBBytes = 9 * 2 * 32 * 16;  // 9 taps x 2 halves x 32 rows x 16 B
 constexpr int kNB = 8;                 // accumulator buffers
 constexpr int kG = 4;                  // epilogue groups
-constexpr int kThreads = 64 + 128 * kG;
+constexpr int kMma2 = 2 + 4 * kG;             // second MMA-issuing warp (odd tiles)
+constexpr int kThreads = 64 + 128 * kG + 32;
 constexpr int kSmemLimit = 232448;
 
 struct DwTcArgs {
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[a], 4);
     }
     mbar_init(bfull, 1);
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -235,17 +236,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mbar_wait(bfull, 0, nullptr);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == kMma2) {
+    // ------------------------------------------------------- MMA issuers
+    // Two threads issue the MMAs, one for the even and one for the odd
+    // local tiles (separate accumulators, each commits its own MMAs): one
+    // thread issuing nine MMAs per tile had set the kernel's pace.
     if (lane == 0) {
       const uint32_t idesc = make_idesc_s8(128, 32);
       bool ok = mbar_wait(bfull, 0, abort_flag);
       if (!ok) dw_record_error(p.err, abort_flag, kDevErrMmaWait);
       const uint32_t b0 = smem_u32(sB);
-      int s = 0;
-      uint32_t ph = 0;
-      int64_t i = 0;
-      for (int64_t t = slot; ok && t < p.tiles_per_group; t += nslots, ++i) {
+      int64_t i = warp == 1 ? 0 : 1;
+      for (int64_t t = slot + i * nslots; ok && t < p.tiles_per_group; t += 2 * nslots, i += 2) {
+        const int s = static_cast<int>(i % stages);
+        const uint32_t ph = static_cast<uint32_t>((i / stages) & 1);
         const int b = static_cast<int>(i % kNB);
         const uint32_t use = static_cast<uint32_t>(i / kNB);
         if (!mbar_wait(&tempty[b], (use & 1u) ^ 1u, abort_flag) ||
@@ -265,10 +269,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&empty[s]);
         umma_commit(&tfull[b]);
-        if (++s == stages) {
-          s = 0;
-          ph ^= 1u;
-        }
       }
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, nullptr);

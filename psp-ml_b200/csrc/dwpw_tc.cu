@@ -13,12 +13,13 @@
 //   3. pointwise: C/32 MMAs (M=128, N=N, K=32) of that tile against the
 //      resident 1x1 weights; the epilogue requantises and stores NHWC.
 // The depthwise output never reaches HBM, and one pipeline serves both
-// convs.  The MMA thread issues the pointwise MMAs one tile behind the
-// depthwise ones so the tensor pipe has work while the epilogue builds the
-// A tile.
+// convs.  Two MMA threads take the even and the odd tiles; each issues the
+// pointwise MMAs of its previous tile after the depthwise MMAs of the next,
+// so the tensor pipe has work while the epilogue builds the A tile.
 //
-// Roles: warp 0 TMA (halo rows, weights once), warp 1 MMA, G groups of 4
-// epilogue warps (one per tensor-memory lane quarter) taking tiles in turn.
+// Roles: warp 0 TMA (halo rows, weights once), warps 1 and 2 + 4G MMA, G
+// groups of 4 epilogue warps (one per tensor-memory lane quarter) taking
+// tiles in turn.
 // Every wait is bounded; on expiry the kernel records an error, drains its
 // copies and MMAs, frees tensor memory and exits.
 #include <algorithm>
@@ -58,7 +59,8 @@ struct DwPwShape {
   static constexpr int kCols = C + N;  // tensor-memory columns per tile
   static constexpr int kBufs = (512 / kCols) >= 8 ? 8 : (512 / kCols);
   static constexpr int kGroups = kBufs >= 4 ? 4 : kBufs;
-  static constexpr int kThreads = 64 + 128 * kGroups;
+  static constexpr int kMma2 = 2 + 4 * kGroups;  // second MMA-issuing warp (odd tiles)
+  static constexpr int kThreads = 64 + 128 * kGroups + 32;
   static constexpr int kStage = 6 * CG * kRegionF;  // 3 rows x CG groups x 2 halves
   static constexpr int kApw = 128 * C;              // one pointwise A tile
   static constexpr int kFixed = CG * kDwGroupBytes + C * N + kBufs * kApw;
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
       mbar_init(&tmem_empty[a], 4);
     }
     mbar_init(wfull, 1);
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -196,8 +198,11 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
       }
       mbar_wait(wfull, 0, nullptr);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == S::kMma2) {
+    // ------------------------------------------------------- MMA issuers
+    // Two threads, one for the even and one for the odd local tiles (each
+    // issues and commits the MMAs of its own tiles): a single issuing thread
+    // set the pace.
     if (lane == 0) {
       const uint32_t idesc_dw = make_idesc_s8(128, 32);
       const uint32_t idesc_pw = make_idesc_s8(128, N);
@@ -207,10 +212,8 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
       const uint32_t bpw0 = smem_u32(sBpw);
       const uint32_t apw0 = smem_u32(sApw);
       const uint32_t in0 = smem_u32(sIn);
-      int s = 0;
-      uint32_t ph = 0;
-      int b = 0, pb = 0;             // buffer of this tile / of the previous tile
-      uint32_t par = 0, ppar = 0;    // their use parities
+      int pb = 0;           // buffer of this thread's previous tile
+      uint32_t ppar = 0;    // its use parity
       bool have_prev = false;
       // Pointwise MMAs of the tile in buffer `bb` (its A tile built by the
       // epilogue).
@@ -228,7 +231,13 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
         umma_commit(&pw_full[bb]);
         return true;
       };
-      for (int64_t t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+      int64_t i = warp == 1 ? 0 : 1;  // local tile index
+      for (int64_t t = blockIdx.x + i * gridDim.x; ok && t < p.tiles;
+           t += 2 * static_cast<int64_t>(gridDim.x), i += 2) {
+        const int s = static_cast<int>(i % stages);
+        const uint32_t ph = static_cast<uint32_t>((i / stages) & 1);
+        const int b = static_cast<int>(i % NB);
+        const uint32_t par = static_cast<uint32_t>((i / NB) & 1);
         if (!mbar_wait(&tmem_empty[b], par ^ 1u, abort_flag) ||
             !mbar_wait(&in_full[s], ph, abort_flag)) {
           fused_record_error(p.err, abort_flag, kDevErrMmaWait);
@@ -251,10 +260,6 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
         }
         umma_commit(&in_empty[s]);
         umma_commit(&dw_full[b]);
-        if (++s == stages) {
-          s = 0;
-          ph ^= 1u;
-        }
         if (have_prev && !pointwise(pb, ppar)) {
           fused_record_error(p.err, abort_flag, kDevErrMmaWait);
           ok = false;
@@ -263,10 +268,6 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
         have_prev = true;
         pb = b;
         ppar = par;
-        if (++b == NB) {
-          b = 0;
-          par ^= 1u;
-        }
       }
       if (ok && have_prev && !pointwise(pb, ppar))
         fused_record_error(p.err, abort_flag, kDevErrMmaWait);

@@ -487,6 +487,11 @@ cudaError_t launch_dw_tc_once(const pspml_op_desc& d, const PreparedOp& pp, int6
 cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
                          const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                          cudaStream_t s) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) &
+                        15u) == 0;
+  if (aligned && dwrs_dw_supported(d) && pp.table != nullptr && pp.all_fast_known &&
+      pp.ncls <= 9)
+    return launch_dwrs_dw(d, pp, batch, in, out, dev_err, num_sms, s);
   const int64_t tiles_per = static_cast<int64_t>(d.out_h) * ((d.out_w + 127) / 128);
   const int64_t chunk = std::max<int64_t>(1, ((1ll << 31) - 1) / tiles_per);
   const int64_t in_per = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;

@@ -502,6 +502,8 @@ cudaError_t launch_dwpw(const pspml_op_desc& dw, const PreparedOp& pdw, const ps
                         const uint8_t* wpw_packed, const DwPwTable& tab, int64_t batch,
                         const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                         cudaStream_t s) {
+  if (dwrs_pair_supported(dw, pw))
+    return launch_dwrs_pair(dw, pdw, pw, wpw_packed, tab, batch, in, out, dev_err, num_sms, s);
   const int64_t tiles_per = static_cast<int64_t>(dw.out_h) * ((dw.out_w + 127) / 128);
   const int64_t chunk = std::max<int64_t>(1, ((1ll << 31) - 1) / tiles_per);
   const int64_t in_per = static_cast<int64_t>(dw.in_h) * dw.in_w * dw.in_c;

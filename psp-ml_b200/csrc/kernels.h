@@ -184,6 +184,20 @@ cudaError_t launch_dwpw(const pspml_op_desc& dw, const PreparedOp& pdw, const ps
                         const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                         cudaStream_t s);
 
+// Row-streaming depthwise 3x3 stride 1 (dwrs_tc.cu): every input row is
+// one A operand whose N = 96 MMA updates the three output rows it feeds.
+// Depthwise alone (C in {32, 64}) or fused with a 64-output 1x1 conv
+// (C = 64); SAME rows (pad 1 top and bottom), rows of >= 128 px.
+bool dwrs_dw_supported(const pspml_op_desc& d);
+bool dwrs_pair_supported(const pspml_op_desc& dw, const pspml_op_desc& pw);
+cudaError_t launch_dwrs_dw(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                           const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                           cudaStream_t s);
+cudaError_t launch_dwrs_pair(const pspml_op_desc& dw, const PreparedOp& pdw,
+                             const pspml_op_desc& pw, const uint8_t* wpw_packed,
+                             const DwPwTable& tab, int64_t batch, const int8_t* in, int8_t* out,
+                             unsigned* dev_err, int num_sms, cudaStream_t s);
+
 // Path for op `d` given operand alignment (16-byte aligned pointers allow the
 // TMA / vector paths).
 OpPath choose_path(const pspml_op_desc& d, bool aligned16);

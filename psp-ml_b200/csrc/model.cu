@@ -398,6 +398,9 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
       }
       int last = i + 1;
       while (last < n_ops && m->ops[last].d.kind == PSPML_OP_RESHAPE) ++last;
+      // A fused pair reads this buffer while it writes the output of its
+      // second op, so the buffer lives until that op.
+      if (last < n_ops && m->ops[last].fuse == 1) ++last;
       bufs.push_back(Buf{i, static_cast<int64_t>(align_up(
                                 static_cast<size_t>(max_micro_batch) * op.out_elems, 256)),
                          i, last, 0});

@@ -81,6 +81,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// A wait for a barrier on a short dependency chain: polls without the
+// suspend-time hint, so the thread resumes as soon as the phase completes.
+// Same bounds as mbar_wait.
+__device__ __forceinline__ bool mbar_try_wait_poll(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity,
+                                               const volatile int* abort) {
+  if (mbar_try_wait_poll(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_poll(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -213,6 +241,21 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
                  "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
                :
                : "memory");
+}
+
+// Writes 16 zero columns into this warp's 32 TMEM lanes (no wait).
+__device__ __forceinline__ void tmem_st16_zero(uint32_t taddr) {
+  const uint32_t z = 0;
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(z)
+      : "memory");
+}
+
+// Waits for every outstanding tcgen05.st of this thread.
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor for tcgen05.mma (K-major operand).

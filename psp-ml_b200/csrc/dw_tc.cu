@@ -492,6 +492,10 @@ cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t b
   if (aligned && dwrs_dw_supported(d) && pp.table != nullptr && pp.all_fast_known &&
       pp.ncls <= 9)
     return launch_dwrs_dw(d, pp, batch, in, out, dev_err, num_sms, s);
+  // Shapes only the row-streaming kernel takes, without a constant table
+  // (a channel outside the fast requant form): the generic kernel reads the
+  // same prepared requant constants.
+  if (!aligned || !dw_tc_supported(d)) return launch_dw_generic(d, pp, batch, in, out, s);
   const int64_t tiles_per = static_cast<int64_t>(d.out_h) * ((d.out_w + 127) / 128);
   const int64_t chunk = std::max<int64_t>(1, ((1ll << 31) - 1) / tiles_per);
   const int64_t in_per = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;

@@ -1,41 +1,53 @@
-// dwrs_tc.cu - int8 depthwise 3x3 stride-1 conv streamed by rows on the
-// tensor cores, alone or fused with the 1x1 conv after it.
+// dwrs_tc.cu - int8 depthwise 3x3 conv (stride 1 or 2) streamed by rows
+// on the tensor cores, alone or fused with the 1x1 conv after it.
 //
 // Block-diagonal weights turn the depthwise conv of a 32-channel group
 // into GEMMs (see dw_tc.cu).  This kernel makes every input row a single
-// A operand: input row y feeds output rows y-1, y and y+1 through the
-// vertical taps ky = 2, 1, 0, so one MMA with N = 96 (three 32-column
-// blocks of block-diagonal weights, one per ky) updates all three output
-// rows at once.  Per input row and group that is 3 MMAs (one per
-// horizontal tap kx; the tap shift is a 16-byte move of the A descriptor
-// start in the no-swizzle layout) instead of 9 per output row, and every
-// input row is loaded once instead of three times.
+// A operand: input row y feeds the output rows r with S*r - pad_top + ky = y
+// (ky = 0..2), so one MMA whose N covers those rows (32 columns of
+// block-diagonal weights per row, each with its ky) updates all of them at
+// once.  Per input row and group that is 3 MMAs, one per horizontal tap kx
+// (the tap is a 16-byte move of the A descriptor start in the no-swizzle
+// layout), and every input row is loaded once.
 //
-// Tensor memory: per group, a ring of three 32-column accumulator blocks;
-// output row r lives in block r % 3.  Which weight block meets which
-// accumulator block rotates with y % 3: the kernel keeps the weights of each
-// kx as five ky blocks [2 1 0 2 1] and takes the three-block window that
-// starts at block (1, 0, 2)[y % 3].  A block must hold zeros before its row
-// takes its first contribution, so the epilogue zeroes it right after
-// reading the finished row, before the requantisation arithmetic; every MMA
-// accumulates.  The first and last input rows of a strip skip the output
-// rows outside the image (a narrower N).
+// Stride 1: an input row feeds three output rows; accumulators sit in a
+// ring of three 32-column tensor-memory blocks per group (row r in block
+// r % 3).  Which weight block meets which accumulator block rotates with
+// y % 3, so the weights of each kx are kept as five ky blocks [2 1 0 2 1]
+// and the MMA takes the three-block window that starts at (1, 0, 2)[y % 3].
+// Stride 2: an input row feeds one (ky = 1) or two (ky = 2 and 0) output
+// rows; a ring of two blocks, weights as [2 0 2 1].  The input is viewed as
+// [C][2][W/2][H][N] so that one box holds the even and another the odd
+// pixels of a row, each as consecutive 16-byte rows: tap kx reads the even
+// or odd box at a 0 or 16-byte offset.
 //
-// Work unit: a strip = one sample x one 128-pixel column tile x all rows.
-// Two slots run independent strips so that one slot's MMAs overlap the
-// other's epilogue.  Per slot: one TMA thread (input rows, 16-channel boxes
-// of 130 pixels, zero filled outside the image), one MMA thread and two
-// epilogue sets of four warps (one per tensor-memory lane quarter) that
-// take the slot's rows in turn.  Every epilogue warp handles all channels
-// of its 32 pixels, so all of them run one code path: with a path per
-// channel range the unrolled requantisation code of four paths interleaved
-// on each scheduler and instruction fetch stalled.
+// A block must hold zeros before its row takes its first contribution, so
+// the epilogue zeroes it right after reading the finished row, before the
+// requantisation arithmetic; every MMA accumulates.  Output rows outside
+// the image get no MMA.
 //
-// Fused pointwise: the epilogue writes the requantised depthwise row into a
-// shared-memory A tile [C/16][128][16 B]; the MMA thread runs C/32 MMAs
-// (M=128, N=NPW, K=32) against the resident 1x1 weights into a pointwise
-// accumulator; the epilogue requantises that and stores NHWC.  The
-// depthwise output never reaches global memory.
+// Work unit: a strip = one sample x one 128-pixel column tile (x one
+// 64-channel block when the channels come in blocks) x all rows.  Two
+// slots run independent strips so that one slot's MMAs overlap the other's
+// epilogue.  Per slot: one TMA thread (16-channel boxes of 130 pixels, zero
+// filled outside the image), one MMA thread and two epilogue sets of four
+// warps (one per tensor-memory lane quarter) that take the slot's rows in
+// turn.  Every epilogue warp handles all channels of its 32 pixels, so all
+// of them run one code path: with a path per channel range the unrolled
+// requantisation code of four paths interleaved on each scheduler and
+// instruction fetch stalled.  Rows narrower than 128 pixels leave lanes of
+// the tile idle; warps whose 32 pixels are all outside the row skip the
+// arithmetic.
+//
+// Fused pointwise (stride 1, 64 channels): the epilogue writes the
+// requantised depthwise row into a shared-memory A tile [C/16][128][16 B];
+// the MMA thread runs C/32 MMAs (M=128, N=NPW, K=32) against the resident
+// 1x1 weights into a pointwise accumulator; the epilogue requantises that
+// and stores NHWC.  The depthwise output never reaches global memory.
+//
+// Requantisation constants come from a kernel-parameter table: at
+// compile-time offsets for a single channel block, at warp-uniform run-time
+// offsets when the channels come in blocks.
 //
 // Zero points: the TMA zero fill stands for the padding, so the folded bias
 // depends on the pixel's border class (in-image taps); the epilogue adds the
@@ -56,21 +68,20 @@ namespace pspml {
 
 namespace {
 
-constexpr int kRsRegion = 2176;           // one input row of 16 channels: 130 px x 16 B, padded
-constexpr int kRsHalf = 5 * 32 * 16;      // one K-half of a five-block weight column (2560 B)
-constexpr int kRsTap = 2 * kRsHalf;       // weights of one (group, kx)
+constexpr int kRsRegion = 2176;  // one input box of 16 channels: up to 130 px x 16 B, padded
 constexpr int kRsSmemLimit = 232448;
 constexpr int kRsMaxStages = 8;
 constexpr int kRsMaxSets = 4;
 
 struct RsArgs {
-  int32_t strips;  // batch * tiles_x
-  int32_t tiles_x, H, W;
-  int32_t pad_l;
+  int32_t strips;  // batch * tiles_x (per channel block)
+  int32_t tiles_x;
+  int32_t Hin, Ho, Wo;  // input rows, output rows and width
+  int32_t pad_t, pad_l;
   FastDiv fd_tiles_x;
   const uint8_t* wdw;  // [C/32][9][2][32][16] (dw_tc packing)
   const uint8_t* wpw;  // [C/16][NPW][16] (pointwise, K-major core matrices)
-  int8_t* out;         // [B][H][W][out channels]
+  int8_t* out;         // [B][Ho][Wo][out channels]
   const uint8_t* ycls;
   const uint8_t* xcls;
   int32_t n_xcls, base_cls;
@@ -80,10 +91,10 @@ struct RsArgs {
 };
 
 // Barriers of one slot.  Rows are numbered per slot across its strips; row
-// g belongs to epilogue set g % RS and lives in accumulator block r % 3 (r:
-// row within the image).  Every barrier that a set waits on completes only
-// for that set's rows, in order, and its next completion needs the set's
-// previous one consumed, so no parity wait can fall two phases behind.
+// g belongs to epilogue set g % RS and lives in accumulator block r % R (r:
+// output row).  Every barrier that a set waits on completes only for that
+// set's rows, in order, and its next completion needs the set's previous
+// one consumed, so no parity wait can fall two phases behind.
 struct RsBars {
   uint64_t in_full[kRsMaxStages];
   uint64_t in_empty[kRsMaxStages];
@@ -94,24 +105,38 @@ struct RsBars {
   uint64_t pw_empty;                 // set -> MMA: pointwise accumulator read
 };
 
-// CG: 32-channel groups (C = 32 CG); NPW: pointwise outputs (0: depthwise
-// only); NS: slots (independent strips); RS: epilogue sets per slot (four
-// warps each, one per tensor-memory lane quarter, taking rows in turn).
-template <int CG, int NPW, int NS, int RS>
+// CG: 32-channel groups per strip; NPW: pointwise outputs (0: depthwise
+// only); S: stride; NCB: channel blocks of the op (CTA b takes block
+// b % NCB, so all its warps use compile-time table offsets of one block);
+// NS: slots; RS: epilogue sets per slot (four warps each, one per
+// tensor-memory lane quarter, taking rows in turn).
+template <int CG, int NPW, int S, int NCB>
 struct RsShape {
-  static constexpr int C = CG * 32;
-  static constexpr int kInRow = CG * 2 * kRsRegion;
-  static constexpr int kBdw = CG * 3 * kRsTap;
-  static constexpr int kBpw = NPW * C;
+  static constexpr int NS = 2;
+  static constexpr int RS = 2;
+  static constexpr int C = CG * 32;                    // channels of a strip
+  static constexpr int R = S == 1 ? 3 : 2;             // accumulator ring blocks
+  static constexpr int NBB = S == 1 ? 5 : 4;           // weight blocks per kx
+  static constexpr int kHalf = NBB * 32 * 16;          // one K-half of a kx's weights
+  static constexpr int kTap = 2 * kHalf;               // weights of one (group, kx)
+  static constexpr int kBoxes = S == 1 ? 1 : 2;        // boxes per 16 channels and row
+  static constexpr int kInRow = CG * 2 * kBoxes * kRsRegion;
   static constexpr int kApw = NPW > 0 ? 128 * C : 0;
-  static constexpr int kFixed = kBdw + kBpw + NS * RS * kApw;
   static constexpr int kSlotCols = 512 / NS;
   static constexpr int kThreads = 128 + NS * RS * 128;
-  static_assert(CG * 96 + NPW <= kSlotCols, "tensor memory per slot");
-  static_assert(NS == 1 || NS == 2, "slots");
-  static_assert(RS == 2 || RS == 4, "epilogue sets");
+  static_assert(CG * R * 32 + NPW <= kSlotCols, "tensor memory per slot");
+  static constexpr int kBdw = CG * 3 * kTap;           // resident weights of one block
+  static_assert(NCB == 1 || NPW == 0, "channel blocks are for the depthwise conv alone");
+  static_assert(NCB == 1 || NCB == 2 || NCB == 4, "channel blocks");
+  static_assert(NPW == 0 || S == 1, "fused pointwise after a stride-1 depthwise conv");
   static_assert(RS <= kRsMaxSets, "epilogue sets");
 };
+
+// Weight block order per kx: ky of each 32-row block.
+__host__ __device__ constexpr int rs_block_ky(int S, int blk) {
+  return S == 1 ? (blk == 2 ? 0 : ((blk == 1 || blk == 4) ? 1 : 2))
+                : (blk == 1 ? 0 : (blk == 3 ? 1 : 2));
+}
 
 __device__ __forceinline__ void rs_record_error(unsigned* err, volatile int* abort_flag,
                                                 unsigned code) {
@@ -127,7 +152,7 @@ __device__ __forceinline__ void rs_fence_async_smem() {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int lane) {
   int ok = 0;
-  if (lane == 0) ok = mbar_wait_poll(bar, parity, abort_flag) ? 1 : 0;
+  if (lane == 0) ok = mbar_wait(bar, parity, abort_flag) ? 1 : 0;
   return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
 }
 
@@ -151,15 +176,40 @@ __device__ __forceinline__ uint4 rs_requant16(const uint32_t* v, const int2* mh,
   return make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
 
+// Strip i -> (sample, column tile).
+struct RsStrip {
+  uint32_t n;
+  int tx;
+};
+__device__ __forceinline__ RsStrip rs_strip(const RsArgs& p, int i) {
+  RsStrip st;
+  st.n = p.fd_tiles_x.div(static_cast<uint32_t>(i));
+  st.tx = i - static_cast<int>(st.n) * p.tiles_x;
+  return st;
+}
+
+// Strips of slot k of this CTA: the CTAs of one channel block share its
+// strips.
+__device__ __forceinline__ void rs_strip_range(int ncb, int k, int ns, int* first, int* step) {
+  const int per_block = static_cast<int>(gridDim.x) / ncb;
+  *first = static_cast<int>(blockIdx.x) / ncb + k * per_block;
+  *step = ns * per_block;
+}
+
 // Epilogue of one warp: set `set` of slot `k`, lane quarter q, every
-// channel.  All epilogue warps of a kernel run this one code path.
-template <int CG, int NPW, int NS, int RS, bool DWCLAMP, bool PWCLAMP>
+// channel of the strip.  All epilogue warps of a kernel run this one code
+// path.
+template <int CG, int NPW, int S, int NCB, int CB, bool DWCLAMP, bool PWCLAMP>
 __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& tab, RsBars& bars,
                                             uint8_t* sA, uint32_t tm_slot, int k, int set, int q,
                                             int lane, volatile int* abort_flag) {
-  using S = RsShape<CG, NPW, NS, RS>;
-  constexpr int C = S::C;
+  using Sh = RsShape<CG, NPW, S, NCB>;
+  constexpr int C = Sh::C;
+  constexpr int R = Sh::R;
+  constexpr int RS = Sh::RS;
   constexpr int NV = C / 16;
+  constexpr int Cop = NCB * C;   // channels of the op
+  constexpr int cbase = CB * C;  // this CTA's channel block
   constexpr int NP = NPW / 16;
   const int row = q * 32 + lane;
   const uint32_t tl = tm_slot + (static_cast<uint32_t>(q * 32) << 16);
@@ -169,73 +219,79 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
 #pragma unroll
     for (int g = 0; g < CG; ++g)
 #pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        tmem_st16_zero(tl + g * 96 + j * 32);
-        tmem_st16_zero(tl + g * 96 + j * 32 + 16);
+      for (int j = 0; j < R; ++j) {
+        tmem_st16_zero(tl + g * R * 32 + j * 32);
+        tmem_st16_zero(tl + g * R * 32 + j * 32 + 16);
       }
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
     if (lane == 0)
 #pragma unroll
-      for (int j = 0; j < 3; ++j) mbar_arrive(&bars.dw_free[j]);
+      for (int j = 0; j < R; ++j) mbar_arrive(&bars.dw_free[j]);
   }
 
   uint32_t full_ph = 0;  // bit j: parity of the next wait on dw_full[set][j]
   uint32_t pw_ph = 0;
-  uint8_t* atile = sA + set * S::kApw + row * 16;
-  const int first = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
-  const int step = NS * static_cast<int>(gridDim.x);
-  const int H = p.H;
+  uint8_t* atile = sA + set * Sh::kApw + row * 16;
+  int first, step;
+  rs_strip_range(NCB, k, Sh::NS, &first, &step);
+  const int Ho = p.Ho;
   uint32_t g = 0;  // row number within the slot
   for (int i = first; i < p.strips; i += step) {
-    const uint32_t n = p.fd_tiles_x.div(static_cast<uint32_t>(i));
-    const int tx = i - static_cast<int>(n) * p.tiles_x;
-    const int x = tx * 128 + row;
-    const bool valid = x < p.W;
-    // Border classes: rows 0 and H-1 and the interior rows (SAME 3x3).
+    const RsStrip st = rs_strip(p, i);
+    const int x = st.tx * 128 + row;
+    const bool valid = x < p.Wo;
+    const bool any_valid = __any_sync(0xFFFFFFFFu, valid);
+    // Border classes: the first, the last and the interior output rows.
     int cls_top = 0, cls_mid = 0, cls_bot = 0;
     if (valid) {
       const int xc = p.xcls[x];
       cls_top = p.ycls[0] * p.n_xcls + xc;
-      cls_mid = p.ycls[H > 1 ? 1 : 0] * p.n_xcls + xc;
-      cls_bot = p.ycls[H - 1] * p.n_xcls + xc;
+      cls_mid = p.ycls[Ho > 1 ? 1 : 0] * p.n_xcls + xc;
+      cls_bot = p.ycls[Ho - 1] * p.n_xcls + xc;
     }
-    const int64_t pix0 = (static_cast<int64_t>(n) * H) * p.W + x;
-    for (int r = 0; r < H; ++r, ++g) {
+    const int64_t pix0 = (static_cast<int64_t>(st.n) * Ho) * p.Wo + x;
+    for (int r = 0; r < Ho; ++r, ++g) {
       if (static_cast<int>(g % RS) != set) continue;
-      const int rb = r % 3;
+      const int rb = r % R;
       if (!warp_wait(&bars.dw_full[set * 3 + rb], (full_ph >> rb) & 1u, abort_flag, lane)) {
         if (lane == 0) rs_record_error(p.err, abort_flag, kDevErrEpiWait);
         return;
       }
       full_ph ^= 1u << rb;
       tc_fence_after();
+      // (The fused path, rows of >= 128 px, always loads: a guard there
+      // made the compiler spill.)
+      const bool load = NPW > 0 || any_valid;
       uint32_t v[NV][16];
+      if (load) {
 #pragma unroll
-      for (int h = 0; h < NV; ++h)
-        tmem_ld16_nowait(tl + static_cast<uint32_t>((h / 2) * 96 + rb * 32 + (h % 2) * 16), v[h]);
+        for (int h = 0; h < NV; ++h)
+          tmem_ld16_nowait(tl + static_cast<uint32_t>((h / 2) * R * 32 + rb * 32 + (h % 2) * 16),
+                           v[h]);
 #pragma unroll
-      for (int h = 0; h < NV; ++h) tmem_wait_ld(v[h]);
+        for (int h = 0; h < NV; ++h) tmem_wait_ld(v[h]);
 #pragma unroll
-      for (int h = 0; h < NV; ++h)
-        tmem_st16_zero(tl + static_cast<uint32_t>((h / 2) * 96 + rb * 32 + (h % 2) * 16));
-      tmem_wait_st();
+        for (int h = 0; h < NV; ++h)
+          tmem_st16_zero(tl + static_cast<uint32_t>((h / 2) * R * 32 + rb * 32 + (h % 2) * 16));
+        tmem_wait_st();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.dw_free[rb]);
 
-      const int cls = r == 0 ? cls_top : (r == H - 1 ? cls_bot : cls_mid);
-      if (valid && cls != p.base_cls) {
-        const int off = cls * C;
-#pragma unroll
-        for (int h = 0; h < NV; ++h)
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            v[h][j] += static_cast<uint32_t>(tab.dw_dbias[off + h * 16 + j]);
-      }
-      const int64_t pix = pix0 + static_cast<int64_t>(r) * p.W;
+      const int64_t pix = pix0 + static_cast<int64_t>(r) * p.Wo;
       if constexpr (NPW > 0) {
+        const int cls = r == 0 ? cls_top : (r == Ho - 1 ? cls_bot : cls_mid);
+        if (valid && cls != p.base_cls) {
+          const int off = cls * C;
+#pragma unroll
+          for (int h = 0; h < NV; ++h)
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              v[h][j] += static_cast<uint32_t>(tab.dw_dbias[off + h * 16 + j]);
+        }
 #pragma unroll
         for (int h = 0; h < NV; ++h)
           *reinterpret_cast<uint4*>(atile + h * 2048) =
@@ -251,7 +307,7 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
         pw_ph ^= 1u;
         tc_fence_after();
         uint32_t u[NP][16];
-        const uint32_t tp = tl + static_cast<uint32_t>(CG * 96);
+        const uint32_t tp = tl + static_cast<uint32_t>(CG * R * 32);
 #pragma unroll
         for (int h = 0; h < NP; ++h) tmem_ld16_nowait(tp + h * 16, u[h]);
 #pragma unroll
@@ -268,32 +324,48 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
         }
       } else {
         if (valid) {
-          int8_t* o = p.out + pix * C;
+          const int cls = r == 0 ? cls_top : (r == Ho - 1 ? cls_bot : cls_mid);
+          if (cls != p.base_cls) {
+            const int off = cls * Cop + cbase;
+#pragma unroll
+            for (int h = 0; h < NV; ++h)
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                v[h][j] += static_cast<uint32_t>(tab.dw_dbias[off + h * 16 + j]);
+          }
+          int8_t* o = p.out + pix * Cop + cbase;
+          const int2* mh = tab.dw_mh + cbase;
+          const int2* bs = tab.dw_bs + cbase;
 #pragma unroll
           for (int h = 0; h < NV; ++h)
             reinterpret_cast<uint4*>(o)[h] =
-                rs_requant16<DWCLAMP>(v[h], tab.dw_mh, tab.dw_bs, h * 16, p.dw_lo4, p.dw_hi4);
+                rs_requant16<DWCLAMP>(v[h], mh, bs, h * 16, p.dw_lo4, p.dw_hi4);
         }
       }
     }
   }
 }
 
-template <int CG, int NPW, int NS, int RS, bool DWCLAMP, bool PWCLAMP>
-__global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
+template <int CG, int NPW, int S, int NCB, bool DWCLAMP, bool PWCLAMP>
+__global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
     k_dwrs_s8(const __grid_constant__ CUtensorMap tmIn, const RsArgs p,
               const __grid_constant__ DwPwTable tab) {
-  using S = RsShape<CG, NPW, NS, RS>;
-  constexpr int C = S::C;
+  using Sh = RsShape<CG, NPW, S, NCB>;
+  constexpr int C = Sh::C;
+  constexpr int NS = Sh::NS;
+  constexpr int RS = Sh::RS;
+  constexpr int R = Sh::R;
+  constexpr int NBB = Sh::NBB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int stages = p.stages;
+  const int cb = NCB == 1 ? 0 : static_cast<int>(blockIdx.x) % NCB;  // this CTA's channel block
   uint8_t* sBdw = smem;
-  uint8_t* sBpw = sBdw + S::kBdw;
-  uint8_t* sApw = sBpw + S::kBpw;           // [slot][set][C/16][128][16]
-  uint8_t* sIn = sApw + NS * RS * S::kApw;  // [slot][stage][CG*2][kRsRegion]
-  RsBars* bars = reinterpret_cast<RsBars*>(sIn + NS * stages * S::kInRow);
+  uint8_t* sBpw = sBdw + Sh::kBdw;
+  uint8_t* sApw = sBpw + NPW * C;             // [slot][set][C/16][128][16]
+  uint8_t* sIn = sApw + NS * RS * Sh::kApw;   // [slot][stage][group][box][half][kRsRegion]
+  RsBars* bars = reinterpret_cast<RsBars*>(sIn + NS * stages * Sh::kInRow);
   uint64_t* mma_done = reinterpret_cast<uint64_t*>(bars + NS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + NS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -301,29 +373,29 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Resident weights: the depthwise weights of each (group, kx) as five ky
-  // blocks [2 1 0 2 1] (two K-halves of 160 rows x 16 B); the pointwise
-  // weights as packed.
+  // Resident weights: the depthwise weights of each (group, kx) of the
+  // channel block as NBB ky blocks (two K-halves of NBB*32 rows x 16 B);
+  // the pointwise weights as packed.
   {
-    constexpr int nB = CG * 3 * 2 * 5 * 32;  // 16-byte rows
+    constexpr int nB = CG * 3 * 2 * NBB * 32;  // 16-byte rows
     for (int i = threadIdx.x; i < nB; i += blockDim.x) {
       int t = i;
       const int rr = t % 32;
       t /= 32;
-      const int blk = t % 5;
-      t /= 5;
+      const int blk = t % NBB;
+      t /= NBB;
       const int h = t % 2;
       t /= 2;
       const int kx = t % 3;
-      const int g = t / 3;
-      const int ky = blk == 2 ? 0 : ((blk == 1 || blk == 4) ? 1 : 2);
+      const int gg = t / 3;
+      const int ky = rs_block_ky(S, blk);
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(
-          p.wdw + (g * 9 + ky * 3 + kx) * 1024 + h * 512 + rr * 16));
-      *reinterpret_cast<uint4*>(sBdw + (g * 3 + kx) * kRsTap + h * kRsHalf + (blk * 32 + rr) * 16) =
-          v;
+          p.wdw + ((cb * CG + gg) * 9 + ky * 3 + kx) * 1024 + h * 512 + rr * 16));
+      *reinterpret_cast<uint4*>(sBdw + (gg * 3 + kx) * Sh::kTap + h * Sh::kHalf +
+                                (blk * 32 + rr) * 16) = v;
     }
     if constexpr (NPW > 0) {
-      for (int i = threadIdx.x; i < S::kBpw / 16; i += blockDim.x)
+      for (int i = threadIdx.x; i < NPW * C / 16; i += blockDim.x)
         reinterpret_cast<uint4*>(sBpw)[i] = __ldg(reinterpret_cast<const uint4*>(p.wpw) + i);
     }
   }
@@ -356,7 +428,8 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int H = p.H;
+  const int Hin = p.Hin;
+  const int Ho = p.Ho;
 
   if (warp < 2) {
     // ------------------------------------------------------ TMA producer
@@ -364,31 +437,47 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
       const int k = warp;
       RsBars& b = bars[k];
       tma_prefetch_desc(&tmIn);
-      uint8_t* in_k = sIn + k * stages * S::kInRow;
-      const int first = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
-      const int step = NS * static_cast<int>(gridDim.x);
+      uint8_t* in_k = sIn + k * stages * Sh::kInRow;
+      int first, step;
+      rs_strip_range(NCB, k, NS, &first, &step);
+      const int c0 = cb * C;
       int s = 0;
       uint32_t ph = 0;
       int64_t issued = 0;
       bool ok = true;
       for (int i = first; ok && i < p.strips; i += step) {
-        const uint32_t n = p.fd_tiles_x.div(static_cast<uint32_t>(i));
-        const int tx = i - static_cast<int>(n) * p.tiles_x;
-        const int x0 = tx * 128 - p.pad_l;
-        for (int y = 0; y < H; ++y) {
-          if (!mbar_wait_poll(&b.in_empty[s], ph ^ 1u, abort_flag)) {
+        const RsStrip st = rs_strip(p, i);
+        for (int y = 0; y < Hin; ++y) {
+          if (!mbar_wait(&b.in_empty[s], ph ^ 1u, abort_flag)) {
             rs_record_error(p.err, abort_flag, kDevErrTmaWait);
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&b.in_full[s], CG * 2 * 16 * 130);
-          uint8_t* a = in_k + s * S::kInRow;
+          uint8_t* a = in_k + s * Sh::kInRow;
+          if constexpr (S == 1) {
+            mbar_arrive_expect_tx(&b.in_full[s], CG * 2 * 16 * 130);
+            const int x0 = st.tx * 128 - p.pad_l;
 #pragma unroll
-          for (int g = 0; g < CG; ++g)
+            for (int gq = 0; gq < CG; ++gq)
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
-              tma_load_4d(a + (g * 2 + h) * kRsRegion, &tmIn, &b.in_full[s], g * 32 + h * 16, x0,
-                          y, static_cast<int>(n));
+              for (int h = 0; h < 2; ++h)
+                tma_load_4d(a + (gq * 2 + h) * kRsRegion, &tmIn, &b.in_full[s],
+                            c0 + gq * 32 + h * 16, x0, y, static_cast<int>(st.n));
+          } else {
+            // Even pixels 2j (j from the tile's first output) and odd
+            // pixels 2j+1 (from one pair earlier with a left pad).
+            mbar_arrive_expect_tx(&b.in_full[s], CG * 2 * 2 * 16 * 129);
+            const int j0 = st.tx * 128;
+#pragma unroll
+            for (int gq = 0; gq < CG; ++gq)
+#pragma unroll
+              for (int eo = 0; eo < 2; ++eo)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                  tma_load_5d(a + ((gq * 2 + eo) * 2 + h) * kRsRegion, &tmIn, &b.in_full[s],
+                              c0 + gq * 32 + h * 16, eo, j0 - (eo == 1 ? p.pad_l : 0), y,
+                              static_cast<int>(st.n));
+          }
           ++issued;
           if (++s == stages) {
             s = 0;
@@ -399,8 +488,9 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
       if (!ok) {
         // Copies already issued land before the kernel exits.
         const int64_t from = issued > stages ? issued - stages : 0;
-        for (int64_t g = from; g < issued; ++g)
-          mbar_wait_poll(&b.in_full[g % stages], static_cast<uint32_t>((g / stages) & 1), nullptr);
+        for (int64_t gi = from; gi < issued; ++gi)
+          mbar_wait(&b.in_full[gi % stages], static_cast<uint32_t>((gi / stages) & 1),
+                         nullptr);
       }
     }
   } else if (warp < 4) {
@@ -408,33 +498,27 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
     if (lane == 0 && warp - 2 < NS) {
       const int k = warp - 2;
       RsBars& b = bars[k];
-      const uint32_t tm_slot = tmem_base + static_cast<uint32_t>(k * S::kSlotCols);
-      const uint32_t in0 = smem_u32(sIn + k * stages * S::kInRow);
-      const uint32_t bdw0 = smem_u32(sBdw);
+      const uint32_t tm_slot = tmem_base + static_cast<uint32_t>(k * Sh::kSlotCols);
+      const uint32_t in0 = smem_u32(sIn + k * stages * Sh::kInRow);
       const uint32_t bpw0 = smem_u32(sBpw);
-      const uint32_t apw0 = smem_u32(sApw + k * RS * S::kApw);
-      const int first = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
-      const int step = NS * static_cast<int>(gridDim.x);
+      const uint32_t apw0 = smem_u32(sApw + k * RS * Sh::kApw);
+      int first, step;
+      rs_strip_range(NCB, k, NS, &first, &step);
+      const int pt = p.pad_t;
       int s = 0;
       uint32_t ph = 0;
       uint32_t free_ph = 0;  // bit j: parity of the next wait on dw_free[j]
-      uint32_t gbase = 0;    // slot row number of the strip's first row
+      uint32_t gbase = 0;    // slot row number of the strip's first output row
       uint32_t gp = 0;       // next row for the pointwise MMAs
       bool ok = true;
-      auto need = [&](int r) -> bool {
-        const int j = r % 3;
-        const bool o = mbar_wait_poll(&b.dw_free[j], (free_ph >> j) & 1u, abort_flag);
-        free_ph ^= 1u << j;
-        return o;
-      };
       auto pointwise = [&]() -> bool {
         if constexpr (NPW > 0) {
           const uint32_t set = gp % RS;
-          if (!mbar_wait_poll(&b.apw_full[set], (gp / RS) & 1u, abort_flag)) return false;
-          if (!mbar_wait_poll(&b.pw_empty, (gp & 1u) ^ 1u, abort_flag)) return false;
+          if (!mbar_wait(&b.apw_full[set], (gp / RS) & 1u, abort_flag)) return false;
+          if (!mbar_wait(&b.pw_empty, (gp & 1u) ^ 1u, abort_flag)) return false;
           tc_fence_after();
-          const uint32_t a_t = apw0 + set * static_cast<uint32_t>(S::kApw);
-          const uint32_t d_t = tm_slot + static_cast<uint32_t>(CG * 96);
+          const uint32_t a_t = apw0 + set * static_cast<uint32_t>(Sh::kApw);
+          const uint32_t d_t = tm_slot + static_cast<uint32_t>(CG * R * 32);
           const uint32_t idesc_pw = make_idesc_s8(128, NPW);
 #pragma unroll
           for (int kc = 0; kc < C / 32; ++kc) {
@@ -447,46 +531,78 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
         }
         return true;
       };
+      // Descriptor templates: an operand's descriptor differs from these only
+      // in the start-address field (address >> 4, below 2^14 for shared
+      // memory), so each MMA adds an offset to one 64-bit value.
+      const uint64_t adesc0 = make_sdesc(in0, kRsRegion, 128, 0);
+      const uint64_t bdesc_smem = make_sdesc(smem_u32(sBdw), Sh::kHalf, 128, 0);
+      uint32_t aoff[3];  // A start of tap kx within a stage, group 0 (16-byte units)
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        if constexpr (S == 1) {
+          aoff[kx] = static_cast<uint32_t>(kx);
+        } else {
+          // pad 0: kx 0 even+0, 1 odd+0, 2 even+16; pad 1: odd+0, even+0, odd+16.
+          const int eo = ((kx == 1) ? 1 : 0) ^ pt;
+          aoff[kx] = static_cast<uint32_t>((eo * 2 * kRsRegion) / 16 + (kx == 2 ? 1 : 0));
+        }
+      }
+      constexpr uint32_t kGroupA = (2 * Sh::kBoxes * kRsRegion) / 16;
+      const uint32_t idesc1 = make_idesc_s8(128, 32);
+      const uint32_t idesc2 = make_idesc_s8(128, 64);
+      const uint32_t idesc3 = make_idesc_s8(128, 96);
+      const uint64_t bdesc0 = bdesc_smem;
       for (int i = first; ok && i < p.strips; i += step) {
         int pw_next = 0;
-        for (int y = 0; y < H; ++y) {
-          if (y == 0) {
-            ok = need(0) && (H < 2 || need(1));
-          } else if (y + 1 < H) {
-            ok = need(y + 1);
+        // Output rows [nc, nn) have started and are not complete: exactly the
+        // rows the current input row reaches.  first(r) = max(0, S r - pt),
+        // last(r) = min(Hin - 1, S r - pt + 2).
+        int nn = 0, nc = 0, nn_blk = 0, nc_blk = 0;
+        int ym = (pt + 2) % 3;  // (y + pt - 1) mod 3: the ky of row y is 1 - pt
+        for (int y = 0; y < Hin; ++y) {
+          while (ok && nn < Ho && S * nn - pt <= y) {
+            ok = mbar_wait(&b.dw_free[nn_blk], (free_ph >> nn_blk) & 1u, abort_flag);
+            free_ph ^= 1u << nn_blk;
+            ++nn;
+            if (++nn_blk == R) nn_blk = 0;
           }
-          if (ok) ok = mbar_wait_poll(&b.in_full[s], ph, abort_flag);
+          if (ok) ok = mbar_wait(&b.in_full[s], ph, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          // Block j holds the output row of y-1 .. y+1 that is j mod 3; bit j
-          // of `live` says that row is inside the image.
           uint32_t live = 0;
-#pragma unroll
-          for (int j = 0; j < 3; ++j) {
-            const int rj = y - 1 + (((j - y + 1) % 3) + 3) % 3;
-            if (rj >= 0 && rj < H) live |= 1u << j;
+          {
+            int jb = nc_blk;
+            for (int r = nc; r < nn; ++r) {
+              live |= 1u << jb;
+              if (++jb == R) jb = 0;
+            }
           }
-          const int ym = y % 3;
-          const int o = ym == 0 ? 1 : (ym == 1 ? 0 : 2);
-          const uint32_t a_row = in0 + static_cast<uint32_t>(s * S::kInRow);
+          int o;
+          if constexpr (S == 1) {
+            o = ym == 0 ? 1 : (ym == 1 ? 0 : 2);
+          } else {
+            // u even: rows u/2 - 1 (ky 2) and u/2 (ky 0); u odd: (u-1)/2 (ky 1).
+            const int u = y + pt;
+            o = (u & 1) == 0 ? ((((u >> 1) - 1) & 1) == 0 ? 0 : 1) : 3 - (((u - 1) >> 1) & 1);
+          }
+          const uint64_t astage = adesc0 + static_cast<uint64_t>((s * Sh::kInRow) / 16);
           int j = 0;
-          while (j < 3) {
+          while (j < R) {
             if (((live >> j) & 1u) == 0) {
               ++j;
               continue;
             }
             int j1 = j + 1;
-            while (j1 < 3 && ((live >> j1) & 1u) != 0) ++j1;
-            const uint32_t idesc = make_idesc_s8(128, 32 * (j1 - j));
+            while (j1 < R && ((live >> j1) & 1u) != 0) ++j1;
+            const uint32_t idesc = j1 - j == 1 ? idesc1 : (j1 - j == 2 ? idesc2 : idesc3);
+            const uint64_t bwin = bdesc0 + static_cast<uint64_t>((o + j) * 32);
 #pragma unroll
-            for (int g = 0; g < CG; ++g) {
+            for (int gq = 0; gq < CG; ++gq) {
 #pragma unroll
               for (int kx = 0; kx < 3; ++kx) {
-                const uint64_t ad =
-                    make_sdesc(a_row + (g * 2) * kRsRegion + kx * 16, kRsRegion, 128, 0);
-                const uint64_t bd =
-                    make_sdesc(bdw0 + (g * 3 + kx) * kRsTap + (o + j) * 512, kRsHalf, 128, 0);
-                umma_i8(tm_slot + static_cast<uint32_t>(g * 96 + j * 32), ad, bd, idesc, 1u);
+                umma_i8(tm_slot + static_cast<uint32_t>(gq * R * 32 + j * 32),
+                        astage + gq * kGroupA + aoff[kx],
+                        bwin + static_cast<uint64_t>(((gq * 3 + kx) * Sh::kTap) / 16), idesc, 1u);
               }
             }
             j = j1;
@@ -496,26 +612,28 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
             s = 0;
             ph ^= 1u;
           }
-          // Row y-1 is complete after input row y; the last input row also
-          // completes its own row.
-          if (y >= 1) {
-            const uint32_t gr = gbase + static_cast<uint32_t>(y - 1);
-            umma_commit(&b.dw_full[(gr % RS) * 3 + (y - 1) % 3]);
+          // Rows whose last input row this is are complete.
+          while (nc < Ho && (S * nc - pt + 2 <= y || y == Hin - 1)) {
+            const uint32_t gr = gbase + static_cast<uint32_t>(nc);
+            umma_commit(&b.dw_full[(gr % RS) * 3 + nc_blk]);
+            ++nc;
+            if (++nc_blk == R) nc_blk = 0;
           }
-          if (y == H - 1) {
-            const uint32_t gr = gbase + static_cast<uint32_t>(y);
-            umma_commit(&b.dw_full[(gr % RS) * 3 + y % 3]);
+          if (++ym == 3) ym = 0;
+          if constexpr (NPW > 0) {
+            while (ok && pw_next <= y - 2) {
+              ok = pointwise();
+              ++pw_next;
+            }
           }
-          while (ok && pw_next <= y - 2) {
+        }
+        if constexpr (NPW > 0) {
+          while (ok && pw_next < Ho) {
             ok = pointwise();
             ++pw_next;
           }
         }
-        while (ok && NPW > 0 && pw_next < H) {
-          ok = pointwise();
-          ++pw_next;
-        }
-        gbase += static_cast<uint32_t>(H);
+        gbase += static_cast<uint32_t>(Ho);
       }
       if (!ok) rs_record_error(p.err, abort_flag, kDevErrMmaWait);
       // Every MMA of this thread completes before tensor memory is freed.
@@ -528,9 +646,26 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
     const int k = ew / (RS * 4);
     const int set = (ew / 4) % RS;
     const int q = warp & 3;
-    rs_epilogue<CG, NPW, NS, RS, DWCLAMP, PWCLAMP>(
-        p, tab, bars[k], sApw + k * RS * S::kApw,
-        tmem_base + static_cast<uint32_t>(k * S::kSlotCols), k, set, q, lane, abort_flag);
+    uint8_t* sA = sApw + k * RS * Sh::kApw;
+    const uint32_t tm = tmem_base + static_cast<uint32_t>(k * Sh::kSlotCols);
+    // One code path per CTA: its channel block's table offsets are
+    // compile-time constants.
+    if (cb == 0) {
+      rs_epilogue<CG, NPW, S, NCB, 0, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q, lane,
+                                                        abort_flag);
+    } else if constexpr (NCB >= 2) {
+      if (cb == 1) {
+        rs_epilogue<CG, NPW, S, NCB, 1, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+                                                          lane, abort_flag);
+      } else if constexpr (NCB >= 4) {
+        if (cb == 2)
+          rs_epilogue<CG, NPW, S, NCB, 2, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+                                                            lane, abort_flag);
+        else
+          rs_epilogue<CG, NPW, S, NCB, 3, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+                                                            lane, abort_flag);
+      }
+    }
   }
 
   tc_fence_before();
@@ -541,7 +676,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, NS, RS>::kThreads, 1)
   }
 }
 
-template <int CG, int NPW, int NS, int RS, bool DWC, bool PWC>
+template <int CG, int NPW, int S, int NCB, bool DWC, bool PWC>
 cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int grid,
                       int smem, cudaStream_t s) {
   static std::atomic<uint64_t> done{0};
@@ -549,40 +684,70 @@ cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& ta
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load() & bit) == 0) {
-    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, NS, RS, DWC, PWC>,
+    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, S, NCB, DWC, PWC>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kRsSmemLimit);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit);
   }
-  k_dwrs_s8<CG, NPW, NS, RS, DWC, PWC>
-      <<<grid, RsShape<CG, NPW, NS, RS>::kThreads, smem, s>>>(m, a, tab);
+  k_dwrs_s8<CG, NPW, S, NCB, DWC, PWC>
+      <<<grid, RsShape<CG, NPW, S, NCB>::kThreads, smem, s>>>(m, a, tab);
   return cudaGetLastError();
 }
 
-template <int CG, int NPW, int NS, int RS>
-cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, bool dwc, bool pwc,
-                     int num_sms, cudaStream_t s) {
-  using S = RsShape<CG, NPW, NS, RS>;
-  const int overhead = 1024 + S::kFixed + NS * static_cast<int>(sizeof(RsBars)) + 64;
-  a.stages = std::min(kRsMaxStages, (kRsSmemLimit - overhead) / (NS * S::kInRow));
-  if (a.stages < 2) return cudaErrorInvalidValue;
-  const int smem = std::max(overhead + NS * a.stages * S::kInRow, 120 * 1024);
-  const int grid = static_cast<int>(
-      std::min<int64_t>((static_cast<int64_t>(a.strips) + NS - 1) / NS, num_sms));
-  if (grid <= 0) return cudaSuccess;
-  if (dwc)
-    return pwc ? rs_launch<CG, NPW, NS, RS, true, true>(m, a, tab, grid, smem, s)
-               : rs_launch<CG, NPW, NS, RS, true, false>(m, a, tab, grid, smem, s);
-  return pwc ? rs_launch<CG, NPW, NS, RS, false, true>(m, a, tab, grid, smem, s)
-             : rs_launch<CG, NPW, NS, RS, false, false>(m, a, tab, grid, smem, s);
+// Shared memory of one launch (bytes) and its input stages.
+template <int CG, int NPW, int S, int NCB>
+bool rs_smem(int* smem, int* stages) {
+  using Sh = RsShape<CG, NPW, S, NCB>;
+  const int fixed = Sh::kBdw + NPW * Sh::C + Sh::NS * Sh::RS * Sh::kApw;
+  const int overhead = 1024 + fixed + Sh::NS * static_cast<int>(sizeof(RsBars)) + 64;
+  const int st = std::min(kRsMaxStages, (kRsSmemLimit - overhead) / (Sh::NS * Sh::kInRow));
+  if (st < 3) return false;
+  *stages = st;
+  *smem = std::max(overhead + Sh::NS * st * Sh::kInRow, 120 * 1024);
+  return true;
 }
 
+template <int CG, int NPW, int S, int NCB>
+cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, bool dwc, bool pwc,
+                     int num_sms, cudaStream_t s) {
+  using Sh = RsShape<CG, NPW, S, NCB>;
+  int smem = 0;
+  if (!rs_smem<CG, NPW, S, NCB>(&smem, &a.stages)) return cudaErrorInvalidValue;
+  // NCB CTAs per group of strips, one per channel block.
+  const int per_block = static_cast<int>(std::min<int64_t>(
+      (static_cast<int64_t>(a.strips) + Sh::NS - 1) / Sh::NS, std::max(1, num_sms / NCB)));
+  const int grid = per_block * NCB;
+  if (a.strips <= 0) return cudaSuccess;
+  if (dwc)
+    return pwc ? rs_launch<CG, NPW, S, NCB, true, true>(m, a, tab, grid, smem, s)
+               : rs_launch<CG, NPW, S, NCB, true, false>(m, a, tab, grid, smem, s);
+  return pwc ? rs_launch<CG, NPW, S, NCB, false, true>(m, a, tab, grid, smem, s)
+             : rs_launch<CG, NPW, S, NCB, false, false>(m, a, tab, grid, smem, s);
+}
+
+// Shapes the kernel takes: 3x3 depthwise, stride 1 or 2 (square), at most
+// one row/column of top/left padding, 64 or more output pixels per row; C
+// in {32, 64} or a multiple of 64 up to 256 (channel blocks); stride 2
+// needs an even input width (the even/odd pixel view).
 bool rs_geometry_ok(const pspml_op_desc& d) {
-  return d.kind == PSPML_OP_DEPTHWISE_CONV2D && d.kernel_h == 3 && d.kernel_w == 3 &&
-         d.stride_h == 1 && d.stride_w == 1 && d.pad_top == 1 && d.pad_bottom == 1 &&
-         d.pad_left <= 1 && d.out_h == d.in_h && d.out_w >= 128 && d.out_w <= 65535 &&
-         d.out_h <= 4096 && d.in_c == d.out_c;
+  if (d.kind != PSPML_OP_DEPTHWISE_CONV2D || d.kernel_h != 3 || d.kernel_w != 3 ||
+      d.stride_h != d.stride_w || d.in_c != d.out_c)
+    return false;
+  const int S = d.stride_h;
+  if (S != 1 && S != 2) return false;
+  if (d.pad_top < 0 || d.pad_top > 1 || d.pad_left < 0 || d.pad_left > 1) return false;
+  // The interior output rows share one border class (the epilogue reads the
+  // classes of the first, second and last rows only).
+  if (d.pad_bottom < 0 || d.pad_bottom > (S == 1 ? 1 : 2)) return false;
+  if (S == 2 && (d.in_w % 2 != 0)) return false;
+  if (d.out_w < 64 || d.out_w > 65535 || d.out_h > 4096 || d.in_h > 65535) return false;
+  const int C = d.in_c;
+  if (!(C == 32 || C == 64 || C == 128 || C == 256)) return false;
+  // Every output row takes at least one input row: S*r - pad_top + 2 >= 0
+  // and S*(out_h-1) - pad_top <= in_h - 1.
+  if (S * (d.out_h - 1) - d.pad_top > d.in_h - 1) return false;
+  return true;
 }
 
 // One launch over `batch` samples (strip count below 2^31).
@@ -590,12 +755,16 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                     const uint8_t* wpw_packed, const DwPwTable& tab, bool pwc, int32_t pw_min,
                     int32_t pw_max, int64_t batch, const int8_t* in, int8_t* out,
                     unsigned* dev_err, int num_sms, cudaStream_t s) {
+  const int C = dw.in_c;
+  const int S = dw.stride_h;
   RsArgs a{};
   a.tiles_x = (dw.out_w + 127) / 128;
   a.strips = static_cast<int32_t>(batch * a.tiles_x);
   a.fd_tiles_x = FastDiv(static_cast<uint32_t>(a.tiles_x));
-  a.H = dw.out_h;
-  a.W = dw.out_w;
+  a.Hin = dw.in_h;
+  a.Ho = dw.out_h;
+  a.Wo = dw.out_w;
+  a.pad_t = dw.pad_top;
   a.pad_l = dw.pad_left;
   a.wdw = reinterpret_cast<const uint8_t*>(pdw.wpack);
   a.wpw = wpw_packed;
@@ -611,21 +780,45 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
   a.err = dev_err;
   const bool dwc = dw.act_min > -128 || dw.act_max < 127;
 
-  const int C = dw.in_c;
   CUtensorMap m;
-  const uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(dw.in_w),
-                            static_cast<uint64_t>(dw.in_h), static_cast<uint64_t>(batch)};
-  const uint64_t strides[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(dw.in_w) * C,
-                               static_cast<uint64_t>(dw.in_h) * dw.in_w * C};
-  const uint32_t box[4] = {16, 130, 1, 1};
-  const uint32_t estr[4] = {1, 1, 1, 1};
-  if (encode_tensor_map(&m, in, 4, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
-      CUDA_SUCCESS)
-    return cudaErrorInvalidValue;
-  if (npw == 64 && C == 32) return rs_shape<1, 64, 2, 2>(m, a, tab, dwc, pwc, num_sms, s);
-  if (npw == 64 && C == 64) return rs_shape<2, 64, 2, 2>(m, a, tab, dwc, pwc, num_sms, s);
-  if (npw == 0 && C == 32) return rs_shape<1, 0, 2, 2>(m, a, tab, dwc, false, num_sms, s);
-  if (npw == 0 && C == 64) return rs_shape<2, 0, 2, 2>(m, a, tab, dwc, false, num_sms, s);
+  if (S == 1) {
+    const uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(dw.in_w),
+                              static_cast<uint64_t>(dw.in_h), static_cast<uint64_t>(batch)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(dw.in_w) * C,
+                                 static_cast<uint64_t>(dw.in_h) * dw.in_w * C};
+    const uint32_t box[4] = {16, 130, 1, 1};
+    const uint32_t estr[4] = {1, 1, 1, 1};
+    if (encode_tensor_map(&m, in, 4, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+        CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  } else {
+    // [C][parity][W/2][H][N]: pixel 2j + parity.
+    const uint64_t dims[5] = {static_cast<uint64_t>(C), 2, static_cast<uint64_t>(dw.in_w / 2),
+                              static_cast<uint64_t>(dw.in_h), static_cast<uint64_t>(batch)};
+    const uint64_t strides[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(C) * 2,
+                                 static_cast<uint64_t>(dw.in_w) * C,
+                                 static_cast<uint64_t>(dw.in_h) * dw.in_w * C};
+    const uint32_t box[5] = {16, 1, 129, 1, 1};
+    const uint32_t estr[5] = {1, 1, 1, 1, 1};
+    if (encode_tensor_map(&m, in, 5, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+        CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  if (npw == 64 && C == 64 && S == 1)
+    return rs_shape<2, 64, 1, 1>(m, a, tab, dwc, pwc, num_sms, s);
+  if (npw == 0) {
+    if (S == 1) {
+      if (C == 32) return rs_shape<1, 0, 1, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 1, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 1, 2>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 1, 4>(m, a, tab, dwc, false, num_sms, s);
+    } else {
+      if (C == 32) return rs_shape<1, 0, 2, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 2, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 2, 2>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 2, 4>(m, a, tab, dwc, false, num_sms, s);
+    }
+  }
   return cudaErrorInvalidValue;
 }
 
@@ -633,8 +826,8 @@ cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                    const uint8_t* wpw_packed, const DwPwTable& tab, bool pwc, int32_t pw_min,
                    int32_t pw_max, int64_t out_per, int64_t batch, const int8_t* in, int8_t* out,
                    unsigned* dev_err, int num_sms, cudaStream_t s) {
-  const int64_t tiles_x = (dw.out_w + 127) / 128;
-  const int64_t chunk = std::max<int64_t>(1, ((1ll << 31) - 1) / tiles_x);
+  const int64_t per_sample = static_cast<int64_t>((dw.out_w + 127) / 128);
+  const int64_t chunk = std::max<int64_t>(1, ((1ll << 31) - 1) / per_sample);
   const int64_t in_per = static_cast<int64_t>(dw.in_h) * dw.in_w * dw.in_c;
   for (int64_t b0 = 0; b0 < batch; b0 += chunk) {
     const cudaError_t e =
@@ -647,24 +840,26 @@ cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
 
 }  // namespace
 
-bool dwrs_dw_supported(const pspml_op_desc& d) {
-  return rs_geometry_ok(d) && (d.in_c == 32 || d.in_c == 64);
-}
+// Rows narrower than the 128-pixel tile leave tile lanes idle; those
+// shapes measured faster on the CUDA-core kernels.
+bool dwrs_dw_supported(const pspml_op_desc& d) { return rs_geometry_ok(d) && d.out_w >= 128; }
 
 // The 32-channel pair measured faster on the tile-per-row kernel
 // (dwpw_tc.cu): with a third of the channels its depthwise MMAs are cheap
 // there, and its epilogue keeps four tiles in flight.
 bool dwrs_pair_supported(const pspml_op_desc& dw, const pspml_op_desc& pw) {
-  return rs_geometry_ok(dw) && pw.out_c == 64 && dw.in_c == 64;
+  return rs_geometry_ok(dw) && dw.stride_h == 1 && dw.out_w >= 128 && pw.out_c == 64 &&
+         dw.in_c == 64;
 }
 
 cudaError_t launch_dwrs_dw(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                            const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                            cudaStream_t s) {
-  if (p.table == nullptr || !p.all_fast_known || p.ncls > 9) return cudaErrorInvalidValue;
-  DwPwTable tab;
-  std::memset(&tab, 0, sizeof(tab));
   const int C = d.in_c;
+  if (p.table == nullptr || !p.all_fast_known || p.ncls > 9 || C > kDwTabC)
+    return cudaErrorInvalidValue;
+  static thread_local DwPwTable tab;
+  std::memset(&tab, 0, sizeof(tab));
   for (int c = 0; c < C; ++c) {
     tab.dw_mh[c] = p.table->mh[c];
     tab.dw_bs[c] = p.table->bs[c];

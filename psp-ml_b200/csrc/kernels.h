@@ -100,13 +100,15 @@ __device__ __forceinline__ void add_class_delta(uint32_t* v, const EpiTable& tab
     if (j < cnt) v[j] += static_cast<uint32_t>(tab.dbias[off + j]);
 }
 
-// Constant table of a fused depthwise + pointwise pair (dwpw_tc.cu): the
-// depthwise op's split constants and per-class bias differences (up to 9
-// border classes x 128 channels), the pointwise op's split constants.
+// Constant table of a depthwise conv and the pointwise conv fused after it
+// (dwpw_tc.cu, dwrs_tc.cu): the depthwise op's split constants and
+// per-class bias differences (up to 9 border classes x 256 channels), the
+// pointwise op's split constants.
+constexpr int kDwTabC = 256;
 struct DwPwTable {
-  int2 dw_mh[128];
-  int2 dw_bs[128];
-  int32_t dw_dbias[9 * 128];
+  int2 dw_mh[kDwTabC];
+  int2 dw_bs[kDwTabC];
+  int32_t dw_dbias[9 * kDwTabC];
   int2 pw_mh[256];
   int2 pw_bs[256];
 };
@@ -184,10 +186,10 @@ cudaError_t launch_dwpw(const pspml_op_desc& dw, const PreparedOp& pdw, const ps
                         const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                         cudaStream_t s);
 
-// Row-streaming depthwise 3x3 stride 1 (dwrs_tc.cu): every input row is
-// one A operand whose N = 96 MMA updates the three output rows it feeds.
-// Depthwise alone (C in {32, 64}) or fused with a 64-output 1x1 conv
-// (C = 64); SAME rows (pad 1 top and bottom), rows of >= 128 px.
+// Row-streaming depthwise 3x3 (dwrs_tc.cu): every input row is one A
+// operand whose MMA updates all the output rows it feeds.  Stride 1 or 2,
+// rows of >= 64 output pixels, C in {32, 64} or a multiple of 64 up to 256;
+// fused with a 64-output 1x1 conv for stride 1, C = 64, rows >= 128 px.
 bool dwrs_dw_supported(const pspml_op_desc& d);
 bool dwrs_pair_supported(const pspml_op_desc& dw, const pspml_op_desc& pw);
 cudaError_t launch_dwrs_dw(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,

@@ -166,7 +166,7 @@ OpPath choose_path(const pspml_op_desc& d, bool aligned16) {
       return OpPath::kDirect;
     }
     case PSPML_OP_DEPTHWISE_CONV2D:
-      if (aligned16 && dw_tc_supported(d)) return OpPath::kDwTc;
+      if (aligned16 && (dw_tc_supported(d) || dwrs_dw_supported(d))) return OpPath::kDwTc;
       if (d.in_c % 4 == 0 && d.kernel_h == 3 && d.kernel_w == 3 &&
           (d.stride_h == 1 || d.stride_h == 2) && d.stride_w == d.stride_h && aligned16)
         return OpPath::kDw3x3;

@@ -40,6 +40,38 @@ def test_depthwise_static_table(ctx, oracle_mod, B, H, W, C, zp_in, act):
     _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))
 
 
+@pytest.mark.parametrize("B,H,W,C,stride,pads,zp_in,act", [
+    (2, 8, 256, 64, 2, None, -128, (-128, 127)),         # stride 2, SAME (bottom/right pad)
+    (3, 9, 258, 64, 2, (1, 1, 1, 1), 5, (-20, 90)),      # stride 2, top/left pad, clamp
+    (2, 6, 256, 128, 2, None, 0, (-128, 127)),           # two channel blocks, stride 2
+    (2, 7, 128, 256, 1, None, -3, (0, 127)),             # four channel blocks, stride 1
+    (1, 12, 200, 128, 1, None, 9, (-128, 127)),          # partial second tile, channel blocks
+    (2, 1, 160, 64, 1, None, 2, (-128, 127)),            # one row, partial second tile
+    (2, 2, 256, 32, 2, None, -7, (-128, 127)),           # one output row, stride 2
+])
+def test_depthwise_row_streaming_shapes(ctx, oracle_mod, B, H, W, C, stride, pads, zp_in, act):
+    """Depthwise shapes of the row-streaming tensor-core kernel beyond the
+    config-3 blocks: stride 2 (even/odd pixel boxes), channel blocks (one
+    block per CTA), partial column tiles."""
+    r = np.random.default_rng(7300 + H * W + C + stride)
+    if pads is None:
+        d = conv_desc(capi.OP_DEPTHWISE_CONV2D, H, W, C, C, k=3, stride=stride, zp_in=zp_in,
+                      zp_out=-6, act=act)
+    else:
+        pt, pb, pl, pr = pads
+        ho = (H + pt + pb - 3) // stride + 1
+        wo = (W + pl + pr - 3) // stride + 1
+        d = make_desc(kind=capi.OP_DEPTHWISE_CONV2D, in_h=H, in_w=W, in_c=C, out_h=ho, out_w=wo,
+                      out_c=C, kernel_h=3, kernel_w=3, stride_h=stride, stride_w=stride,
+                      pad_top=pt, pad_left=pl, pad_bottom=pb, pad_right=pr, zp_in=zp_in,
+                      zp_out=-6, act_min=act[0], act_max=act[1])
+    x = r.integers(-128, 128, B * H * W * C).astype(np.int8)
+    w = r.integers(-127, 128, 9 * C).astype(np.int8)
+    b, m, s = random_quant(r, C)
+    got = run_op_model(ctx, d, B, x, w, b, m, s)
+    _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))
+
+
 @pytest.mark.parametrize("B,H,W,K,N,act", [
     (2, 8, 64, 32, 64, (-128, 127)),     # 256-row tiles
     (3, 5, 33, 64, 32, (-10, 100)),      # 256-row tiles, ragged last tile, clamp

@@ -74,8 +74,8 @@ constexpr int kRsMaxStages = 8;
 constexpr int kRsMaxSets = 4;
 
 struct RsArgs {
-  int32_t strips;  // batch * tiles_x (per channel block)
-  int32_t tiles_x;
+  int32_t strips;  // batch * tiles_x, or batch / P rounded up (per channel block)
+  int32_t tiles_x, batch;
   int32_t Hin, Ho, Wo;  // input rows, output rows and width
   int32_t pad_t, pad_l;
   FastDiv fd_tiles_x;
@@ -109,8 +109,9 @@ struct RsBars {
 // only); S: stride; NCB: channel blocks of the op (CTA b takes block
 // b % NCB, so all its warps use compile-time table offsets of one block);
 // NS: slots; RS: epilogue sets per slot (four warps each, one per
-// tensor-memory lane quarter, taking rows in turn).
-template <int CG, int NPW, int S, int NCB>
+// tensor-memory lane quarter, taking rows in turn); P: samples packed into
+// the 128 tile rows (rows of at most 128 / P pixels).
+template <int CG, int NPW, int S, int NCB, int P>
 struct RsShape {
   static constexpr int NS = 2;
   static constexpr int RS = 2;
@@ -119,8 +120,14 @@ struct RsShape {
   static constexpr int NBB = S == 1 ? 5 : 4;           // weight blocks per kx
   static constexpr int kHalf = NBB * 32 * 16;          // one K-half of a kx's weights
   static constexpr int kTap = 2 * kHalf;               // weights of one (group, kx)
-  static constexpr int kBoxes = S == 1 ? 1 : 2;        // boxes per 16 channels and row
-  static constexpr int kInRow = CG * 2 * kBoxes * kRsRegion;
+  static constexpr int Wt = 128 / P;                   // tile columns per sample
+  // One box per 16 channels and row (stride 1), an even and an odd box
+  // (stride 2), or with packed samples one box per tap kx, each already
+  // shifted by its tap (a 16-byte move of the descriptor would cross into
+  // the next sample's pixels).
+  static constexpr int kBoxes = P > 1 ? 3 : (S == 1 ? 1 : 2);
+  static constexpr int kRegion = P > 1 ? 128 * 16 : kRsRegion;
+  static constexpr int kInRow = CG * 2 * kBoxes * kRegion;
   static constexpr int kApw = NPW > 0 ? 128 * C : 0;
   static constexpr int kSlotCols = 512 / NS;
   static constexpr int kThreads = 128 + NS * RS * 128;
@@ -128,6 +135,9 @@ struct RsShape {
   static constexpr int kBdw = CG * 3 * kTap;           // resident weights of one block
   static_assert(NCB == 1 || NPW == 0, "channel blocks are for the depthwise conv alone");
   static_assert(NCB == 1 || NCB == 2 || NCB == 4, "channel blocks");
+  static_assert(P == 1 || P == 2 || P == 4, "packed samples");
+  static_assert(P == 1 || (NPW == 0 && S == 1),
+                "packed samples are for a stride-1 depthwise conv alone");
   static_assert(NPW == 0 || S == 1, "fused pointwise after a stride-1 depthwise conv");
   static_assert(RS <= kRsMaxSets, "epilogue sets");
 };
@@ -176,15 +186,21 @@ __device__ __forceinline__ uint4 rs_requant16(const uint32_t* v, const int2* mh,
   return make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
 
-// Strip i -> (sample, column tile).
+// Strip i -> (first sample, column tile).
 struct RsStrip {
   uint32_t n;
   int tx;
 };
+template <int P>
 __device__ __forceinline__ RsStrip rs_strip(const RsArgs& p, int i) {
   RsStrip st;
-  st.n = p.fd_tiles_x.div(static_cast<uint32_t>(i));
-  st.tx = i - static_cast<int>(st.n) * p.tiles_x;
+  if constexpr (P > 1) {
+    st.n = static_cast<uint32_t>(i) * P;
+    st.tx = 0;
+  } else {
+    st.n = p.fd_tiles_x.div(static_cast<uint32_t>(i));
+    st.tx = i - static_cast<int>(st.n) * p.tiles_x;
+  }
   return st;
 }
 
@@ -199,11 +215,11 @@ __device__ __forceinline__ void rs_strip_range(int ncb, int k, int ns, int* firs
 // Epilogue of one warp: set `set` of slot `k`, lane quarter q, every
 // channel of the strip.  All epilogue warps of a kernel run this one code
 // path.
-template <int CG, int NPW, int S, int NCB, int CB, bool DWCLAMP, bool PWCLAMP>
+template <int CG, int NPW, int S, int NCB, int P, int CB, bool DWCLAMP, bool PWCLAMP>
 __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& tab, RsBars& bars,
                                             uint8_t* sA, uint32_t tm_slot, int k, int set, int q,
                                             int lane, volatile int* abort_flag) {
-  using Sh = RsShape<CG, NPW, S, NCB>;
+  using Sh = RsShape<CG, NPW, S, NCB, P>;
   constexpr int C = Sh::C;
   constexpr int R = Sh::R;
   constexpr int RS = Sh::RS;
@@ -239,9 +255,11 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
   const int Ho = p.Ho;
   uint32_t g = 0;  // row number within the slot
   for (int i = first; i < p.strips; i += step) {
-    const RsStrip st = rs_strip(p, i);
-    const int x = st.tx * 128 + row;
-    const bool valid = x < p.Wo;
+    const RsStrip st = rs_strip<P>(p, i);
+    // Tile row -> (sample, pixel): with packed samples, sample row / Wt.
+    const uint32_t n = st.n + static_cast<uint32_t>(row / Sh::Wt);
+    const int x = st.tx * 128 + (P > 1 ? row % Sh::Wt : row);
+    const bool valid = x < p.Wo && (P == 1 || static_cast<int>(n) < p.batch);
     const bool any_valid = __any_sync(0xFFFFFFFFu, valid);
     // Border classes: the first, the last and the interior output rows.
     int cls_top = 0, cls_mid = 0, cls_bot = 0;
@@ -251,7 +269,7 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
       cls_mid = p.ycls[Ho > 1 ? 1 : 0] * p.n_xcls + xc;
       cls_bot = p.ycls[Ho - 1] * p.n_xcls + xc;
     }
-    const int64_t pix0 = (static_cast<int64_t>(st.n) * Ho) * p.Wo + x;
+    const int64_t pix0 = (static_cast<int64_t>(n) * Ho) * p.Wo + x;
     for (int r = 0; r < Ho; ++r, ++g) {
       if (static_cast<int>(g % RS) != set) continue;
       const int rb = r % R;
@@ -346,11 +364,11 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
   }
 }
 
-template <int CG, int NPW, int S, int NCB, bool DWCLAMP, bool PWCLAMP>
-__global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
+template <int CG, int NPW, int S, int NCB, int P, bool DWCLAMP, bool PWCLAMP>
+__global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
     k_dwrs_s8(const __grid_constant__ CUtensorMap tmIn, const RsArgs p,
               const __grid_constant__ DwPwTable tab) {
-  using Sh = RsShape<CG, NPW, S, NCB>;
+  using Sh = RsShape<CG, NPW, S, NCB, P>;
   constexpr int C = Sh::C;
   constexpr int NS = Sh::NS;
   constexpr int RS = Sh::RS;
@@ -446,7 +464,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
       int64_t issued = 0;
       bool ok = true;
       for (int i = first; ok && i < p.strips; i += step) {
-        const RsStrip st = rs_strip(p, i);
+        const RsStrip st = rs_strip<P>(p, i);
         for (int y = 0; y < Hin; ++y) {
           if (!mbar_wait(&b.in_empty[s], ph ^ 1u, abort_flag)) {
             rs_record_error(p.err, abort_flag, kDevErrTmaWait);
@@ -454,7 +472,22 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
             break;
           }
           uint8_t* a = in_k + s * Sh::kInRow;
-          if constexpr (S == 1) {
+          if constexpr (P > 1) {
+            // Per tap kx a box of Wt pixels per sample, already shifted.
+            mbar_arrive_expect_tx(&b.in_full[s], CG * 3 * 2 * P * 16 * Sh::Wt);
+#pragma unroll
+            for (int gq = 0; gq < CG; ++gq)
+#pragma unroll
+              for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                  for (int pm = 0; pm < P; ++pm) {
+                    uint8_t* dst = a + ((gq * 3 + kx) * 2 + h) * Sh::kRegion + pm * Sh::Wt * 16;
+                    tma_load_4d(dst, &tmIn, &b.in_full[s], c0 + gq * 32 + h * 16, kx - p.pad_l,
+                                y, static_cast<int>(st.n) + pm);
+                  }
+          } else if constexpr (S == 1) {
             mbar_arrive_expect_tx(&b.in_full[s], CG * 2 * 16 * 130);
             const int x0 = st.tx * 128 - p.pad_l;
 #pragma unroll
@@ -534,12 +567,14 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
       // Descriptor templates: an operand's descriptor differs from these only
       // in the start-address field (address >> 4, below 2^14 for shared
       // memory), so each MMA adds an offset to one 64-bit value.
-      const uint64_t adesc0 = make_sdesc(in0, kRsRegion, 128, 0);
+      const uint64_t adesc0 = make_sdesc(in0, Sh::kRegion, 128, 0);
       const uint64_t bdesc_smem = make_sdesc(smem_u32(sBdw), Sh::kHalf, 128, 0);
       uint32_t aoff[3];  // A start of tap kx within a stage, group 0 (16-byte units)
 #pragma unroll
       for (int kx = 0; kx < 3; ++kx) {
-        if constexpr (S == 1) {
+        if constexpr (P > 1) {
+          aoff[kx] = static_cast<uint32_t>((kx * 2 * Sh::kRegion) / 16);
+        } else if constexpr (S == 1) {
           aoff[kx] = static_cast<uint32_t>(kx);
         } else {
           // pad 0: kx 0 even+0, 1 odd+0, 2 even+16; pad 1: odd+0, even+0, odd+16.
@@ -547,7 +582,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
           aoff[kx] = static_cast<uint32_t>((eo * 2 * kRsRegion) / 16 + (kx == 2 ? 1 : 0));
         }
       }
-      constexpr uint32_t kGroupA = (2 * Sh::kBoxes * kRsRegion) / 16;
+      constexpr uint32_t kGroupA = (2 * Sh::kBoxes * Sh::kRegion) / 16;
       const uint32_t idesc1 = make_idesc_s8(128, 32);
       const uint32_t idesc2 = make_idesc_s8(128, 64);
       const uint32_t idesc3 = make_idesc_s8(128, 96);
@@ -651,18 +686,18 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
     // One code path per CTA: its channel block's table offsets are
     // compile-time constants.
     if (cb == 0) {
-      rs_epilogue<CG, NPW, S, NCB, 0, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q, lane,
+      rs_epilogue<CG, NPW, S, NCB, P, 0, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q, lane,
                                                         abort_flag);
     } else if constexpr (NCB >= 2) {
       if (cb == 1) {
-        rs_epilogue<CG, NPW, S, NCB, 1, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+        rs_epilogue<CG, NPW, S, NCB, P, 1, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
                                                           lane, abort_flag);
       } else if constexpr (NCB >= 4) {
         if (cb == 2)
-          rs_epilogue<CG, NPW, S, NCB, 2, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+          rs_epilogue<CG, NPW, S, NCB, P, 2, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
         else
-          rs_epilogue<CG, NPW, S, NCB, 3, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+          rs_epilogue<CG, NPW, S, NCB, P, 3, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
       }
     }
@@ -676,7 +711,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB>::kThreads, 1)
   }
 }
 
-template <int CG, int NPW, int S, int NCB, bool DWC, bool PWC>
+template <int CG, int NPW, int S, int NCB, int P, bool DWC, bool PWC>
 cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int grid,
                       int smem, cudaStream_t s) {
   static std::atomic<uint64_t> done{0};
@@ -684,21 +719,21 @@ cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& ta
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load() & bit) == 0) {
-    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, S, NCB, DWC, PWC>,
+    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kRsSmemLimit);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit);
   }
-  k_dwrs_s8<CG, NPW, S, NCB, DWC, PWC>
-      <<<grid, RsShape<CG, NPW, S, NCB>::kThreads, smem, s>>>(m, a, tab);
+  k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC>
+      <<<grid, RsShape<CG, NPW, S, NCB, P>::kThreads, smem, s>>>(m, a, tab);
   return cudaGetLastError();
 }
 
 // Shared memory of one launch (bytes) and its input stages.
-template <int CG, int NPW, int S, int NCB>
+template <int CG, int NPW, int S, int NCB, int P>
 bool rs_smem(int* smem, int* stages) {
-  using Sh = RsShape<CG, NPW, S, NCB>;
+  using Sh = RsShape<CG, NPW, S, NCB, P>;
   const int fixed = Sh::kBdw + NPW * Sh::C + Sh::NS * Sh::RS * Sh::kApw;
   const int overhead = 1024 + fixed + Sh::NS * static_cast<int>(sizeof(RsBars)) + 64;
   const int st = std::min(kRsMaxStages, (kRsSmemLimit - overhead) / (Sh::NS * Sh::kInRow));
@@ -708,22 +743,27 @@ bool rs_smem(int* smem, int* stages) {
   return true;
 }
 
-template <int CG, int NPW, int S, int NCB>
+template <int CG, int NPW, int S, int NCB, int P>
 cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, bool dwc, bool pwc,
                      int num_sms, cudaStream_t s) {
-  using Sh = RsShape<CG, NPW, S, NCB>;
+  using Sh = RsShape<CG, NPW, S, NCB, P>;
   int smem = 0;
-  if (!rs_smem<CG, NPW, S, NCB>(&smem, &a.stages)) return cudaErrorInvalidValue;
+  if (!rs_smem<CG, NPW, S, NCB, P>(&smem, &a.stages)) return cudaErrorInvalidValue;
   // NCB CTAs per group of strips, one per channel block.
   const int per_block = static_cast<int>(std::min<int64_t>(
       (static_cast<int64_t>(a.strips) + Sh::NS - 1) / Sh::NS, std::max(1, num_sms / NCB)));
   const int grid = per_block * NCB;
   if (a.strips <= 0) return cudaSuccess;
-  if (dwc)
-    return pwc ? rs_launch<CG, NPW, S, NCB, true, true>(m, a, tab, grid, smem, s)
-               : rs_launch<CG, NPW, S, NCB, true, false>(m, a, tab, grid, smem, s);
-  return pwc ? rs_launch<CG, NPW, S, NCB, false, true>(m, a, tab, grid, smem, s)
-             : rs_launch<CG, NPW, S, NCB, false, false>(m, a, tab, grid, smem, s);
+  if constexpr (NPW == 0) {
+    return dwc ? rs_launch<CG, NPW, S, NCB, P, true, false>(m, a, tab, grid, smem, s)
+               : rs_launch<CG, NPW, S, NCB, P, false, false>(m, a, tab, grid, smem, s);
+  } else {
+    if (dwc)
+      return pwc ? rs_launch<CG, NPW, S, NCB, P, true, true>(m, a, tab, grid, smem, s)
+                 : rs_launch<CG, NPW, S, NCB, P, true, false>(m, a, tab, grid, smem, s);
+    return pwc ? rs_launch<CG, NPW, S, NCB, P, false, true>(m, a, tab, grid, smem, s)
+               : rs_launch<CG, NPW, S, NCB, P, false, false>(m, a, tab, grid, smem, s);
+  }
 }
 
 // Shapes the kernel takes: 3x3 depthwise, stride 1 or 2 (square), at most
@@ -741,13 +781,20 @@ bool rs_geometry_ok(const pspml_op_desc& d) {
   // classes of the first, second and last rows only).
   if (d.pad_bottom < 0 || d.pad_bottom > (S == 1 ? 1 : 2)) return false;
   if (S == 2 && (d.in_w % 2 != 0)) return false;
-  if (d.out_w < 64 || d.out_w > 65535 || d.out_h > 4096 || d.in_h > 65535) return false;
+  if (d.out_w < 1 || d.out_w > 65535 || d.out_h > 4096 || d.in_h > 65535) return false;
   const int C = d.in_c;
   if (!(C == 32 || C == 64 || C == 128 || C == 256)) return false;
   // Every output row takes at least one input row: S*r - pad_top + 2 >= 0
   // and S*(out_h-1) - pad_top <= in_h - 1.
   if (S * (d.out_h - 1) - d.pad_top > d.in_h - 1) return false;
   return true;
+}
+
+// Samples per 128-row tile: 1 for rows of more than 64 pixels, 2 for
+// 33..64, 4 for up to 32 (stride 1, C >= 64, depthwise alone).
+int rs_packing(const pspml_op_desc& d, int npw) {
+  if (npw != 0 || d.in_c < 64 || d.out_w > 64 || d.stride_h != 1) return 1;
+  return d.out_w > 32 ? 2 : 4;
 }
 
 // One launch over `batch` samples (strip count below 2^31).
@@ -757,9 +804,13 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                     unsigned* dev_err, int num_sms, cudaStream_t s) {
   const int C = dw.in_c;
   const int S = dw.stride_h;
+  // Samples packed per 128-row tile: rows of at most 32 or 64 pixels share
+  // a tile.
+  const int P = rs_packing(dw, npw);
   RsArgs a{};
   a.tiles_x = (dw.out_w + 127) / 128;
-  a.strips = static_cast<int32_t>(batch * a.tiles_x);
+  a.batch = static_cast<int32_t>(batch);
+  a.strips = static_cast<int32_t>(P > 1 ? (batch + P - 1) / P : batch * a.tiles_x);
   a.fd_tiles_x = FastDiv(static_cast<uint32_t>(a.tiles_x));
   a.Hin = dw.in_h;
   a.Ho = dw.out_h;
@@ -786,7 +837,7 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                               static_cast<uint64_t>(dw.in_h), static_cast<uint64_t>(batch)};
     const uint64_t strides[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(dw.in_w) * C,
                                  static_cast<uint64_t>(dw.in_h) * dw.in_w * C};
-    const uint32_t box[4] = {16, 130, 1, 1};
+    const uint32_t box[4] = {16, P > 1 ? static_cast<uint32_t>(128 / P) : 130u, 1, 1};
     const uint32_t estr[4] = {1, 1, 1, 1};
     if (encode_tensor_map(&m, in, 4, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
         CUDA_SUCCESS)
@@ -804,19 +855,30 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  if (npw == 64 && C == 64 && S == 1)
-    return rs_shape<2, 64, 1, 1>(m, a, tab, dwc, pwc, num_sms, s);
-  if (npw == 0) {
+  if (npw == 64 && C == 64 && S == 1 && P == 1)
+    return rs_shape<2, 64, 1, 1, 1>(m, a, tab, dwc, pwc, num_sms, s);
+  if (npw != 0) return cudaErrorInvalidValue;
+  if (P == 1) {
     if (S == 1) {
-      if (C == 32) return rs_shape<1, 0, 1, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 64) return rs_shape<2, 0, 1, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 128) return rs_shape<2, 0, 1, 2>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 256) return rs_shape<2, 0, 1, 4>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 32) return rs_shape<1, 0, 1, 1, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 1, 1, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 1, 2, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 1, 4, 1>(m, a, tab, dwc, false, num_sms, s);
     } else {
-      if (C == 32) return rs_shape<1, 0, 2, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 64) return rs_shape<2, 0, 2, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 128) return rs_shape<2, 0, 2, 2>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 256) return rs_shape<2, 0, 2, 4>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 32) return rs_shape<1, 0, 2, 1, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 2, 1, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 2, 2, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 2, 4, 1>(m, a, tab, dwc, false, num_sms, s);
+    }
+  } else if (S == 1) {
+    if (P == 2) {
+      if (C == 64) return rs_shape<2, 0, 1, 1, 2>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 1, 2, 2>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 1, 4, 2>(m, a, tab, dwc, false, num_sms, s);
+    } else {
+      if (C == 64) return rs_shape<2, 0, 1, 1, 4>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 1, 2, 4>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 1, 4, 4>(m, a, tab, dwc, false, num_sms, s);
     }
   }
   return cudaErrorInvalidValue;
@@ -827,7 +889,8 @@ cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                    int32_t pw_max, int64_t out_per, int64_t batch, const int8_t* in, int8_t* out,
                    unsigned* dev_err, int num_sms, cudaStream_t s) {
   const int64_t per_sample = static_cast<int64_t>((dw.out_w + 127) / 128);
-  const int64_t chunk = std::max<int64_t>(1, ((1ll << 31) - 1) / per_sample);
+  // Whole packed groups per launch.
+  const int64_t chunk = std::max<int64_t>(4, ((1ll << 31) - 1) / per_sample) / 4 * 4;
   const int64_t in_per = static_cast<int64_t>(dw.in_h) * dw.in_w * dw.in_c;
   for (int64_t b0 = 0; b0 < batch; b0 += chunk) {
     const cudaError_t e =
@@ -840,9 +903,14 @@ cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
 
 }  // namespace
 
-// Rows narrower than the 128-pixel tile leave tile lanes idle; those
-// shapes measured faster on the CUDA-core kernels.
-bool dwrs_dw_supported(const pspml_op_desc& d) { return rs_geometry_ok(d) && d.out_w >= 128; }
+// Rows of 65..127 pixels leave tile lanes idle; narrower stride-1 rows
+// pack several samples per tile (C >= 64).  Packed stride-2 rows measured
+// slower than the CUDA-core kernel, so those shapes stay there.
+bool dwrs_dw_supported(const pspml_op_desc& d) {
+  if (!rs_geometry_ok(d)) return false;
+  if (d.out_w >= 128) return true;
+  return d.out_w <= 64 && d.in_c >= 64 && d.stride_h == 1;
+}
 
 // The 32-channel pair measured faster on the tile-per-row kernel
 // (dwpw_tc.cu): with a third of the channels its depthwise MMAs are cheap

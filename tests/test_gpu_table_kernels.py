@@ -48,11 +48,19 @@ def test_depthwise_static_table(ctx, oracle_mod, B, H, W, C, zp_in, act):
     (1, 12, 200, 128, 1, None, 9, (-128, 127)),          # partial second tile, channel blocks
     (2, 1, 160, 64, 1, None, 2, (-128, 127)),            # one row, partial second tile
     (2, 2, 256, 32, 2, None, -7, (-128, 127)),           # one output row, stride 2
+    (2, 6, 128, 128, 2, None, 0, (-128, 127)),           # stride 2, 64-px rows (CUDA cores)
+    (3, 5, 64, 256, 1, None, -128, (0, 127)),            # two per tile, odd batch
+    (5, 4, 32, 128, 1, None, 4, (-128, 127)),            # 32-px rows: four per tile, partial group
+    (2, 12, 64, 256, 2, None, -128, (-128, 127)),        # stride 2, 32-px rows (CUDA cores)
+    (3, 7, 50, 64, 1, None, 3, (-30, 100)),              # 50-px rows, clamp
+    (2, 9, 40, 64, 2, (1, 1, 1, 1), -2, (-128, 127)),    # stride 2 top/left pad, narrow
 ])
 def test_depthwise_row_streaming_shapes(ctx, oracle_mod, B, H, W, C, stride, pads, zp_in, act):
     """Depthwise shapes of the row-streaming tensor-core kernel beyond the
     config-3 blocks: stride 2 (even/odd pixel boxes), channel blocks (one
-    block per CTA), partial column tiles."""
+    block per CTA), partial column tiles, and stride-1 rows of at most 64
+    or 32 pixels with two or four samples packed into one 128-row tile
+    (narrow stride-2 rows run on the CUDA-core kernel)."""
     r = np.random.default_rng(7300 + H * W + C + stride)
     if pads is None:
         d = conv_desc(capi.OP_DEPTHWISE_CONV2D, H, W, C, C, k=3, stride=stride, zp_in=zp_in,

@@ -913,8 +913,10 @@ bool dwrs_dw_supported(const pspml_op_desc& d) {
 }
 
 // The 32-channel pair measured faster on the tile-per-row kernel
-// (dwpw_tc.cu): with a third of the channels its depthwise MMAs are cheap
-// there, and its epilogue keeps four tiles in flight.
+// (dwpw_tc.cu, 141 against 164 ms per config-4 step): with half the
+// depthwise channels a row carries less work and this kernel's per-row
+// chain (MMA, commit, block release) sets the pace, while that kernel
+// keeps four independent tiles in flight.
 bool dwrs_pair_supported(const pspml_op_desc& dw, const pspml_op_desc& pw) {
   return rs_geometry_ok(dw) && dw.stride_h == 1 && dw.out_w >= 128 && pw.out_c == 64 &&
          dw.in_c == 64;

@@ -35,7 +35,8 @@ from . import capi
 
 # Synthetic-input stand-ins for the reference's datasets (MNIST images are
 # not shipped with the reference; BirdNET spectrograms are not available).
-CFG_IN_SCALE = {0: 1.0 / 255.0, 2: 1.0 / 255.0, 3: 0.1}
+# float32-representable (a .tflite file stores float32 scales)
+CFG_IN_SCALE = {k: float(np.float32(v)) for k, v in {0: 1.0 / 255.0, 2: 1.0 / 255.0, 3: 0.1}.items()}
 CFG_IN_ZP = {0: -128, 2: -128, 3: 0}
 
 CFG3_WIDTHS = (64, 64, 128, 128, 256, 256, 512, 512)
@@ -232,6 +233,10 @@ def _pool_f(x, kernel, stride, mode):
     return acc if mode == "max" else acc / (kh * kw)
 
 
+def _f32(v: float) -> float:
+    return float(np.float32(v))
+
+
 class _Builder:
     """Appends layers, calibrating each weighted layer's output scale."""
 
@@ -239,7 +244,9 @@ class _Builder:
         self.name = name
         self.layers: list[Layer] = []
         self.shape = tuple(in_shape)
-        self.scale = in_scale
+        # Scales are kept float32-representable: a .tflite file stores them
+        # as float32 and TFLite derives the multipliers from those values.
+        self.scale = _f32(in_scale)
         self.zp = in_zp
         self.x = calib_x_real  # float64 activations of the calibration batch
 
@@ -248,6 +255,7 @@ class _Builder:
         q = r.integers(-127, 128, size=shape, dtype=np.int16).astype(np.int8)
         rs = rng_for(f"{self.name}/{tag}/ws")
         ws = np.exp(rs.uniform(math.log(1e-3), math.log(1e-1), size=co))
+        ws = ws.astype(np.float32).astype(np.float64)
         rb = rng_for(f"{self.name}/{tag}/b")
         bq = rb.integers(-4096, 4097, size=co, dtype=np.int64).astype(np.int32)
         return q, ws, bq
@@ -257,11 +265,11 @@ class _Builder:
             y_real = np.maximum(y_real, 0.0)
             pos = y_real[y_real > 0]
             pct = float(np.percentile(pos, 99.9)) if pos.size else 1.0
-            l.s_out = max(pct, 1e-6) / 255.0
+            l.s_out = _f32(max(pct, 1e-6) / 255.0)
             l.zp_out = -128
         else:
             pct = float(np.percentile(np.abs(y_real), 99.9)) if y_real.size else 1.0
-            l.s_out = max(pct, 1e-6) / 127.0
+            l.s_out = _f32(max(pct, 1e-6) / 127.0)
             l.zp_out = 0
         l.act_min = max(-128, l.zp_out) if l.relu else -128
         l.act_max = 127

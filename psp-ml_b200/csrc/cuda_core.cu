@@ -27,6 +27,7 @@ struct Geom {
   int32_t zp_in;
   uint32_t lo4, hi4;
   int32_t clamp;
+  int32_t act_min, act_max, zp_out;
 };
 
 Geom geom_of(const pspml_op_desc& d) {
@@ -47,6 +48,9 @@ Geom geom_of(const pspml_op_desc& d) {
   g.lo4 = splat4(d.act_min);
   g.hi4 = splat4(d.act_max);
   g.clamp = (d.act_min > -128 || d.act_max < 127) ? 1 : 0;
+  g.act_min = d.act_min;
+  g.act_max = d.act_max;
+  g.zp_out = d.zp_out;
   return g;
 }
 
@@ -54,13 +58,42 @@ unsigned grid_for(int64_t n) {
   return static_cast<unsigned>(std::max<int64_t>(1, (n + kBlock - 1) / kBlock));
 }
 
-template <bool FAST = false>
+template <int RQ = kRqGeneral>
 __device__ __forceinline__ uint32_t finish4(int32_t a0, int32_t a1, int32_t a2, int32_t a3,
                                             const int4& b, const RqChannel& q0,
                                             const RqChannel& q1, const RqChannel& q2,
                                             const RqChannel& q3, const Geom& g) {
-  uint32_t w = pack_sat4(rq_sel<FAST>(a0 + b.x, q0), rq_sel<FAST>(a1 + b.y, q1),
-                         rq_sel<FAST>(a2 + b.z, q2), rq_sel<FAST>(a3 + b.w, q3));
+  uint32_t w = pack_sat4(rq_sel<RQ>(a0 + b.x, q0), rq_sel<RQ>(a1 + b.y, q1),
+                         rq_sel<RQ>(a2 + b.z, q2), rq_sel<RQ>(a3 + b.w, q3));
+  if (g.clamp) w = clamp4(w, g.lo4, g.hi4);
+  return w;
+}
+
+// Floor form with the bias folded into each channel's 64-bit addend
+// (d = bias * M + C, as floor_entry builds it), for threads that keep their
+// channels' constants in registers: one wide multiply-add and one shift per
+// output.
+struct FloorCh {
+  int64_t d;
+  int32_t m, sr;
+};
+__device__ __forceinline__ FloorCh floor_ch(int32_t bias, const RqChannel& q) {
+  FloorCh f;
+  const int64_t c =
+      static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi)) << 32) | q.c_lo) +
+      (int64_t{1} << 32);
+  f.d = static_cast<int64_t>(bias) * q.m + c;
+  f.m = q.m;
+  f.sr = q.sr;
+  return f;
+}
+__device__ __forceinline__ int32_t rq_floor_ch(int32_t acc, const FloorCh& f) {
+  return static_cast<int32_t>((static_cast<int64_t>(acc) * f.m + f.d) >> 32) >> f.sr;
+}
+__device__ __forceinline__ uint32_t finish4_floor(int32_t a0, int32_t a1, int32_t a2, int32_t a3,
+                                                  const FloorCh (&f)[4], const Geom& g) {
+  uint32_t w = pack_sat4(rq_floor_ch(a0, f[0]), rq_floor_ch(a1, f[1]), rq_floor_ch(a2, f[2]),
+                         rq_floor_ch(a3, f[3]));
   if (g.clamp) w = clamp4(w, g.lo4, g.hi4);
   return w;
 }
@@ -81,7 +114,7 @@ __device__ __forceinline__ int8_t finish1(int32_t a, const RqChannel& q, const G
 // while it computes, so the load latency overlaps the arithmetic.  Block:
 // 128 threads over (pixel group, channel word) pairs of one image
 // (blockIdx.z + n_base).  Weights [9][C]; out-of-image taps read zp_in.
-template <int S, int PX, bool FAST>
+template <int S, int PX, int RQ>
 __global__ void __launch_bounds__(128)
     k_dw3x3_s8(const uint32_t* __restrict__ in, const uint32_t* __restrict__ f,
                const int32_t* __restrict__ bias_eff, const RqChannel* __restrict__ rq,
@@ -108,6 +141,13 @@ __global__ void __launch_bounds__(128)
   const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff) + cw);
   const RqChannel q0 = load_rq(rq + 4 * cw), q1 = load_rq(rq + 4 * cw + 1),
                   q2 = load_rq(rq + 4 * cw + 2), q3 = load_rq(rq + 4 * cw + 3);
+  FloorCh fl[4];
+  if constexpr (RQ == kRqFloor) {
+    fl[0] = floor_ch(b.x, q0);
+    fl[1] = floor_ch(b.y, q1);
+    fl[2] = floor_ch(b.z, q2);
+    fl[3] = floor_ch(b.w, q3);
+  }
 
   const uint32_t zpw = splat4(g.zp_in);
   const int ix0 = ox0 * S - g.pl;
@@ -166,7 +206,9 @@ __global__ void __launch_bounds__(128)
     for (int p = 0; p < PX; ++p)
       if (ox0 + p < g.Wo)
         orow[static_cast<int64_t>(ox0 + p) * cwn] =
-            finish4<FAST>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
+            RQ == kRqFloor
+                ? finish4_floor(acc[p][0], acc[p][1], acc[p][2], acc[p][3], fl, g)
+                : finish4<RQ>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
 #pragma unroll
     for (int c = 0; c < NIN; ++c) {
       if (S == 1) {
@@ -187,7 +229,7 @@ __global__ void __launch_bounds__(128)
 // The KHxKWxCI patch is packed into NW words in TFLite filter order
 // (ky, kx, ci); out-of-image taps hold the input zero point.  Weights of the
 // chunk sit in shared memory as [COB][NW] words (16-byte rows).
-template <int KH, int KW, int CI, int COB, bool FAST>
+template <int KH, int KW, int CI, int COB, int RQ>
 __global__ void __launch_bounds__(128)
     k_small_conv_s8(const int8_t* __restrict__ in, const uint32_t* __restrict__ wpack,
                     int32_t nw_stride, const int32_t* __restrict__ bias_eff,
@@ -268,7 +310,7 @@ __global__ void __launch_bounds__(128)
       const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff + co0) + c4);
       const int cb = co0 + 4 * c4;
       reinterpret_cast<uint32_t*>(op)[c4] =
-          finish4<FAST>(a[0], a[1], a[2], a[3], b, load_rq(rq + cb), load_rq(rq + cb + 1),
+          finish4<RQ>(a[0], a[1], a[2], a[3], b, load_rq(rq + cb), load_rq(rq + cb + 1),
                   load_rq(rq + cb + 2), load_rq(rq + cb + 3), g);
     } else {
 #pragma unroll
@@ -285,7 +327,7 @@ __global__ void __launch_bounds__(128)
 // bytes (the stem conv): weights and requant constants are kernel-parameter
 // operands at compile-time offsets, so the only loads are the input patch
 // (the smem/global tables made the L1 pipe the bottleneck).
-template <int KH, int KW, int CI, bool CLAMP>
+template <int KH, int KW, int CI, int Q>
 __global__ void __launch_bounds__(128)
     k_small_conv_tab_s8(const int8_t* __restrict__ in, int8_t* __restrict__ out, const Geom g,
                         int64_t n_base, const __grid_constant__ SmallConvTable tab) {
@@ -328,11 +370,10 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
       for (int w = 0; w < NW; ++w)
         acc = __dp4a(static_cast<int>(x[w]), static_cast<int>(tab.w[co][w]), acc);
-      const int2 bs = tab.bs[co];
-      r[j] = rq_tab(acc + bs.x, tab.mh[co], bs.y);
+      r[j] = rq_tab_q<Q>(static_cast<uint32_t>(acc), tab.mh[co], tab.bs[co]);
     }
     uint32_t w4 = pack_sat4(r[0], r[1], r[2], r[3]);
-    if constexpr (CLAMP) w4 = clamp4(w4, g.lo4, g.hi4);
+    if constexpr ((Q & kEpClamp) != 0) w4 = clamp4(w4, g.lo4, g.hi4);
     words[c4] = w4;
   }
   uint4* op = reinterpret_cast<uint4*>(out + ((n * g.Ho + oy) * static_cast<int64_t>(g.Wo) + ox) * 32);
@@ -546,7 +587,7 @@ __global__ void k_avgpool_s8(const int8_t* __restrict__ in, int8_t* __restrict__
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-template <int KH, int KW, int CI, bool FAST>
+template <int KH, int KW, int CI, int RQ>
 cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s) {
   const int cob = g.Co <= 8 ? 8 : g.Co <= 16 ? 16 : 32;
@@ -555,14 +596,14 @@ cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, co
     const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
     const dim3 grid((pix + 127) / 128, (g.Co + cob - 1) / cob, nz);
     if (cob == 8)
-      k_small_conv_s8<KH, KW, CI, 8, FAST><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
-                                                                p.rq, out, g, n0);
+      k_small_conv_s8<KH, KW, CI, 8, RQ><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
+                                                              p.rq, out, g, n0);
     else if (cob == 16)
-      k_small_conv_s8<KH, KW, CI, 16, FAST><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
-                                                                 p.rq, out, g, n0);
+      k_small_conv_s8<KH, KW, CI, 16, RQ><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
+                                                               p.rq, out, g, n0);
     else
-      k_small_conv_s8<KH, KW, CI, 32, FAST><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
-                                                                 p.rq, out, g, n0);
+      k_small_conv_s8<KH, KW, CI, 32, RQ><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
+                                                               p.rq, out, g, n0);
   }
   return cudaGetLastError();
 }
@@ -570,8 +611,11 @@ cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, co
 template <int KH, int KW, int CI>
 cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s) {
-  if (p.all_fast_known) return small_conv_cob<KH, KW, CI, true>(g, p, batch, in, out, s);
-  return small_conv_cob<KH, KW, CI, false>(g, p, batch, in, out, s);
+  switch (rq_form(p.all_fast_known, g.act_min, g.zp_out)) {
+    case kRqFloor: return small_conv_cob<KH, KW, CI, kRqFloor>(g, p, batch, in, out, s);
+    case kRqFast: return small_conv_cob<KH, KW, CI, kRqFast>(g, p, batch, in, out, s);
+    default: return small_conv_cob<KH, KW, CI, kRqGeneral>(g, p, batch, in, out, s);
+  }
 }
 
 }  // namespace
@@ -587,10 +631,13 @@ cudaError_t small_conv_tab(const Geom& g, const PreparedOp& p, int64_t batch, co
   for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
     const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
     const dim3 grid((g.Ho * g.Wo + 127) / 128, 1, nz);
-    if (g.clamp)
-      k_small_conv_tab_s8<3, 3, CI, true><<<grid, 128, 0, s>>>(in, out, g, n0, *p.sc_table);
-    else
-      k_small_conv_tab_s8<3, 3, CI, false><<<grid, 128, 0, s>>>(in, out, g, n0, *p.sc_table);
+    const SmallConvTable& t = *p.sc_table;
+    switch (ep_flags(g.act_min, g.act_max, g.zp_out)) {
+      case 0: k_small_conv_tab_s8<3, 3, CI, 0><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+      case 1: k_small_conv_tab_s8<3, 3, CI, 1><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+      case 2: k_small_conv_tab_s8<3, 3, CI, 2><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+      default: k_small_conv_tab_s8<3, 3, CI, 3><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+    }
   }
   return cudaGetLastError();
 }
@@ -625,19 +672,26 @@ cudaError_t launch_dw3x3(const pspml_op_desc& d, const PreparedOp& p, int64_t ba
     const auto* i32 = reinterpret_cast<const uint32_t*>(in);
     const auto* f32 = reinterpret_cast<const uint32_t*>(p.filter);
     auto* o32 = reinterpret_cast<uint32_t*>(out);
-    if (p.all_fast_known) {
-      if (g.sh == 1)
-        k_dw3x3_s8<1, PX, true>
+    const int form = rq_form(p.all_fast_known, g.act_min, g.zp_out);
+    if (g.sh == 1) {
+      if (form == kRqFloor)
+        k_dw3x3_s8<1, PX, kRqFloor>
+            <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
+      else if (form == kRqFast)
+        k_dw3x3_s8<1, PX, kRqFast>
             <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
       else
-        k_dw3x3_s8<2, PX, true>
+        k_dw3x3_s8<1, PX, kRqGeneral>
             <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
     } else {
-      if (g.sh == 1)
-        k_dw3x3_s8<1, PX, false>
+      if (form == kRqFloor)
+        k_dw3x3_s8<2, PX, kRqFloor>
+            <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
+      else if (form == kRqFast)
+        k_dw3x3_s8<2, PX, kRqFast>
             <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
       else
-        k_dw3x3_s8<2, PX, false>
+        k_dw3x3_s8<2, PX, kRqGeneral>
             <<<grid, 128, 0, s>>>(i32, f32, p.bias_eff, p.rq, o32, g, rows_per, n0);
     }
   }

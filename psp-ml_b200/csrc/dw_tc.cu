@@ -105,7 +105,7 @@ constexpr int kDwStaticGroups = 4;  // channel groups with a compile-time path
 
 // One tile row of channel group GRP: 32 accumulators from tensor memory,
 // border-class bias difference if any, requant, one 32-byte store.
-template <int GRP, bool CLAMP>
+template <int GRP, int Q>
 __device__ __forceinline__ void dw_row_static(const EpiTable& tab, uint32_t taddr, int8_t* dst,
                                               bool valid, bool border, int cls_off,
                                               const DwTcArgs& p) {
@@ -119,27 +119,27 @@ __device__ __forceinline__ void dw_row_static(const EpiTable& tab, uint32_t tadd
     add_class_delta(v0, tab, cls_off + c0, 16);
     add_class_delta(v1, tab, cls_off + c0 + 16, 16);
   }
-  const uint4 w0 = requant16_tab<CLAMP>(v0, tab, c0, p.lo4, p.hi4);
-  const uint4 w1 = requant16_tab<CLAMP>(v1, tab, c0 + 16, p.lo4, p.hi4);
+  const uint4 w0 = requant16_tab<Q>(v0, tab, c0, p.lo4, p.hi4);
+  const uint4 w1 = requant16_tab<Q>(v1, tab, c0 + 16, p.lo4, p.hi4);
   if (valid) {
     reinterpret_cast<uint4*>(dst)[0] = w0;
     reinterpret_cast<uint4*>(dst)[1] = w1;
   }
 }
 
-template <bool CLAMP>
+template <int Q>
 __device__ __forceinline__ void dw_row_static_any(int grp_ch, const EpiTable& tab,
                                                   uint32_t taddr, int8_t* dst, bool valid,
                                                   bool border, int cls_off, const DwTcArgs& p) {
   switch (grp_ch) {
-    case 0: dw_row_static<0, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
-    case 1: dw_row_static<1, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
-    case 2: dw_row_static<2, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
-    default: dw_row_static<3, CLAMP>(tab, taddr, dst, valid, border, cls_off, p); break;
+    case 0: dw_row_static<0, Q>(tab, taddr, dst, valid, border, cls_off, p); break;
+    case 1: dw_row_static<1, Q>(tab, taddr, dst, valid, border, cls_off, p); break;
+    case 2: dw_row_static<2, Q>(tab, taddr, dst, valid, border, cls_off, p); break;
+    default: dw_row_static<3, Q>(tab, taddr, dst, valid, border, cls_off, p); break;
   }
 }
 
-template <int MODE, bool CLAMP>
+template <int MODE, int Q>
 __global__ void __launch_bounds__(kThreads, 1)
     k_dw_tc_s8(const __grid_constant__ CUtensorMap tmIn, const DwTcArgs p,
                const __grid_constant__ typename DwTabOf<MODE>::type tab) {
@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int cls = valid ? p.ycls[y] * p.n_xcls + p.xcls[x] : 0;
       const uint32_t tb = tlane + static_cast<uint32_t>(b * 32);
       if constexpr (MODE == kDwStatic) {
-        dw_row_static_any<CLAMP>(grp_ch, tab, tb, orow, valid, cls != p.base_cls, cls * p.C, p);
+        dw_row_static_any<Q>(grp_ch, tab, tb, orow, valid, cls != p.base_cls, cls * p.C, p);
       } else {
         const int32_t* brow = sbias + cls * 32;
 #pragma unroll
@@ -401,7 +401,7 @@ cudaError_t prepare_dw_tc(const pspml_op_desc& d, const int8_t* filter, const in
 
 namespace {
 
-template <int MODE, bool CLAMP>
+template <int MODE, int Q>
 cudaError_t launch_dw_variant(const CUtensorMap& m, const DwTcArgs& a,
                               const typename DwTabOf<MODE>::type& tab, int grid, int smem,
                               cudaStream_t s) {
@@ -411,11 +411,11 @@ cudaError_t launch_dw_variant(const CUtensorMap& m, const DwTcArgs& a,
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load() & bit) == 0) {
     const cudaError_t e = cudaFuncSetAttribute(
-        k_dw_tc_s8<MODE, CLAMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        k_dw_tc_s8<MODE, Q>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit);
   }
-  k_dw_tc_s8<MODE, CLAMP><<<grid, kThreads, smem, s>>>(m, a, tab);
+  k_dw_tc_s8<MODE, Q><<<grid, kThreads, smem, s>>>(m, a, tab);
   return cudaGetLastError();
 }
 
@@ -473,11 +473,15 @@ cudaError_t launch_dw_tc_once(const pspml_op_desc& d, const PreparedOp& pp, int6
   // smem-staged tables.
   if (pp.all_fast_known && pp.table != nullptr && a.n_groups <= kDwStaticGroups &&
       (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
-    return a.clamp ? launch_dw_variant<kDwStatic, true>(m, a, *pp.table, grid, smem, s)
-                   : launch_dw_variant<kDwStatic, false>(m, a, *pp.table, grid, smem, s);
+    switch (ep_flags(d.act_min, d.act_max, d.zp_out)) {
+      case 0: return launch_dw_variant<kDwStatic, 0>(m, a, *pp.table, grid, smem, s);
+      case 1: return launch_dw_variant<kDwStatic, 1>(m, a, *pp.table, grid, smem, s);
+      case 2: return launch_dw_variant<kDwStatic, 2>(m, a, *pp.table, grid, smem, s);
+      default: return launch_dw_variant<kDwStatic, 3>(m, a, *pp.table, grid, smem, s);
+    }
   }
-  if (pp.all_fast_known) return launch_dw_variant<kDwFast, false>(m, a, NoTab{0}, grid, smem, s);
-  return launch_dw_variant<kDwGeneral, false>(m, a, NoTab{0}, grid, smem, s);
+  if (pp.all_fast_known) return launch_dw_variant<kDwFast, 0>(m, a, NoTab{0}, grid, smem, s);
+  return launch_dw_variant<kDwGeneral, 0>(m, a, NoTab{0}, grid, smem, s);
 }
 
 }  // namespace

@@ -77,7 +77,7 @@ __device__ __forceinline__ void fence_async_smem() {
 }
 
 // 16 outputs of channels ch..ch+15 with the pair table's split constants.
-template <bool CLAMP>
+template <int Q>
 __device__ __forceinline__ uint4 requant16_pair(const uint32_t* v, const int2* mh, const int2* bs,
                                                 int ch, uint32_t lo4, uint32_t hi4) {
   uint32_t packed[4];
@@ -87,17 +87,16 @@ __device__ __forceinline__ uint4 requant16_pair(const uint32_t* v, const int2* m
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int c = ch + 4 * g + k;
-      const int2 b = bs[c];
-      r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]) + b.x, mh[c], b.y);
+      r[k] = rq_tab_q<Q>(v[4 * g + k], mh[c], bs[c]);
     }
     uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
-    if constexpr (CLAMP) w = clamp4(w, lo4, hi4);
+    if constexpr ((Q & kEpClamp) != 0) w = clamp4(w, lo4, hi4);
     packed[g] = w;
   }
   return make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
 
-template <int CG, int N, bool DWCLAMP, bool PWCLAMP>
+template <int CG, int N, int DWQ, int PWQ>
 __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
     k_dwpw_s8(const __grid_constant__ CUtensorMap tmIn, const DwPwArgs p,
               const __grid_constant__ DwPwTable tab) {
@@ -320,9 +319,9 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
           }
         }
         const uint4 w0 =
-            requant16_pair<DWCLAMP>(v0, tab.dw_mh, tab.dw_bs, g * 32, p.dw_lo4, p.dw_hi4);
+            requant16_pair<DWQ>(v0, tab.dw_mh, tab.dw_bs, g * 32, p.dw_lo4, p.dw_hi4);
         const uint4 w1 =
-            requant16_pair<DWCLAMP>(v1, tab.dw_mh, tab.dw_bs, g * 32 + 16, p.dw_lo4, p.dw_hi4);
+            requant16_pair<DWQ>(v1, tab.dw_mh, tab.dw_bs, g * 32 + 16, p.dw_lo4, p.dw_hi4);
         *reinterpret_cast<uint4*>(arow + (2 * g) * 2048) = w0;
         *reinterpret_cast<uint4*>(arow + (2 * g + 1) * 2048) = w1;
       }
@@ -348,13 +347,13 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
       for (int c = 0; c < N; c += 32) {
         tmem_wait_ld(u0);
         if (c + 16 < N) tmem_ld16_nowait(tp + static_cast<uint32_t>(c + 16), u1);
-        const uint4 o0 = requant16_pair<PWCLAMP>(u0, tab.pw_mh, tab.pw_bs, c, p.pw_lo4, p.pw_hi4);
+        const uint4 o0 = requant16_pair<PWQ>(u0, tab.pw_mh, tab.pw_bs, c, p.pw_lo4, p.pw_hi4);
         if (valid) *reinterpret_cast<uint4*>(orow + c) = o0;
         if (c + 16 < N) {
           tmem_wait_ld(u1);
           if (c + 32 < N) tmem_ld16_nowait(tp + static_cast<uint32_t>(c + 32), u0);
           const uint4 o1 =
-              requant16_pair<PWCLAMP>(u1, tab.pw_mh, tab.pw_bs, c + 16, p.pw_lo4, p.pw_hi4);
+              requant16_pair<PWQ>(u1, tab.pw_mh, tab.pw_bs, c + 16, p.pw_lo4, p.pw_hi4);
           if (valid) *reinterpret_cast<uint4*>(orow + c + 16) = o1;
         }
       }
@@ -388,7 +387,7 @@ __global__ void k_pack_pw_kmajor(const int8_t* __restrict__ f, int32_t N, int32_
   out[i] = static_cast<uint8_t>(f[static_cast<int64_t>(n) * C + kc * 16 + j]);
 }
 
-template <int CG, int N, bool DWC, bool PWC>
+template <int CG, int N, int DWC, int PWC>
 cudaError_t launch_pair(const CUtensorMap& m, const DwPwArgs& a, const DwPwTable& tab,
                         int grid, int smem, cudaStream_t s) {
   static std::atomic<uint64_t> done{0};
@@ -405,9 +404,20 @@ cudaError_t launch_pair(const CUtensorMap& m, const DwPwArgs& a, const DwPwTable
   return cudaGetLastError();
 }
 
+template <int CG, int N, int DWQ>
+cudaError_t launch_pair_pw(const CUtensorMap& m, const DwPwArgs& a, const DwPwTable& tab,
+                           int pwq, int grid, int smem, cudaStream_t s) {
+  switch (pwq) {
+    case 0: return launch_pair<CG, N, DWQ, 0>(m, a, tab, grid, smem, s);
+    case 1: return launch_pair<CG, N, DWQ, 1>(m, a, tab, grid, smem, s);
+    case 2: return launch_pair<CG, N, DWQ, 2>(m, a, tab, grid, smem, s);
+    default: return launch_pair<CG, N, DWQ, 3>(m, a, tab, grid, smem, s);
+  }
+}
+
 template <int CG, int N>
-cudaError_t launch_shape(const CUtensorMap& m, DwPwArgs a, const DwPwTable& tab, bool dwc,
-                         bool pwc, int num_sms, cudaStream_t s) {
+cudaError_t launch_shape(const CUtensorMap& m, DwPwArgs a, const DwPwTable& tab, int dwq,
+                         int pwq, int num_sms, cudaStream_t s) {
   using S = DwPwShape<CG, N>;
   const int overhead = 1024 + S::kFixed + 64 * 8 + 64;
   a.stages = std::min(4, (kSmemLimitF - overhead) / S::kStage);
@@ -415,11 +425,12 @@ cudaError_t launch_shape(const CUtensorMap& m, DwPwArgs a, const DwPwTable& tab,
   const int smem = std::max(overhead + a.stages * S::kStage, 120 * 1024);
   const int grid = static_cast<int>(std::min<int64_t>(a.tiles, num_sms));
   if (grid <= 0) return cudaSuccess;
-  if (dwc)
-    return pwc ? launch_pair<CG, N, true, true>(m, a, tab, grid, smem, s)
-               : launch_pair<CG, N, true, false>(m, a, tab, grid, smem, s);
-  return pwc ? launch_pair<CG, N, false, true>(m, a, tab, grid, smem, s)
-             : launch_pair<CG, N, false, false>(m, a, tab, grid, smem, s);
+  switch (dwq) {
+    case 0: return launch_pair_pw<CG, N, 0>(m, a, tab, pwq, grid, smem, s);
+    case 1: return launch_pair_pw<CG, N, 1>(m, a, tab, pwq, grid, smem, s);
+    case 2: return launch_pair_pw<CG, N, 2>(m, a, tab, pwq, grid, smem, s);
+    default: return launch_pair_pw<CG, N, 3>(m, a, tab, pwq, grid, smem, s);
+  }
 }
 
 }  // namespace
@@ -476,8 +487,8 @@ cudaError_t launch_dwpw_once(const pspml_op_desc& dw, const PreparedOp& pdw,
   a.pw_lo4 = splat4(pw.act_min);
   a.pw_hi4 = splat4(pw.act_max);
   a.err = dev_err;
-  const bool dwc = dw.act_min > -128 || dw.act_max < 127;
-  const bool pwc = pw.act_min > -128 || pw.act_max < 127;
+  const int dwq = ep_flags(dw.act_min, dw.act_max, dw.zp_out);
+  const int pwq = ep_flags(pw.act_min, pw.act_max, pw.zp_out);
 
   const int C = dw.in_c;
   CUtensorMap m;
@@ -491,8 +502,8 @@ cudaError_t launch_dwpw_once(const pspml_op_desc& dw, const PreparedOp& pdw,
       CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   const int N = pw.out_c;
-  if (C == 32 && N == 64) return launch_shape<1, 64>(m, a, tab, dwc, pwc, num_sms, s);
-  if (C == 64 && N == 64) return launch_shape<2, 64>(m, a, tab, dwc, pwc, num_sms, s);
+  if (C == 32 && N == 64) return launch_shape<1, 64>(m, a, tab, dwq, pwq, num_sms, s);
+  if (C == 64 && N == 64) return launch_shape<2, 64>(m, a, tab, dwq, pwq, num_sms, s);
   return cudaErrorInvalidValue;
 }
 

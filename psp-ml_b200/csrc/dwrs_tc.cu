@@ -166,7 +166,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
 }
 
-template <bool CLAMP>
+template <int Q>
 __device__ __forceinline__ uint4 rs_requant16(const uint32_t* v, const int2* mh, const int2* bs,
                                               int ch, uint32_t lo4, uint32_t hi4) {
   uint32_t packed[4];
@@ -176,11 +176,10 @@ __device__ __forceinline__ uint4 rs_requant16(const uint32_t* v, const int2* mh,
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int c = ch + 4 * g + k;
-      const int2 b = bs[c];
-      r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]) + b.x, mh[c], b.y);
+      r[k] = rq_tab_q<Q>(v[4 * g + k], mh[c], bs[c]);
     }
     uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
-    if constexpr (CLAMP) w = clamp4(w, lo4, hi4);
+    if constexpr ((Q & kEpClamp) != 0) w = clamp4(w, lo4, hi4);
     packed[g] = w;
   }
   return make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -215,7 +214,7 @@ __device__ __forceinline__ void rs_strip_range(int ncb, int k, int ns, int* firs
 // Epilogue of one warp: set `set` of slot `k`, lane quarter q, every
 // channel of the strip.  All epilogue warps of a kernel run this one code
 // path.
-template <int CG, int NPW, int S, int NCB, int P, int CB, bool DWCLAMP, bool PWCLAMP>
+template <int CG, int NPW, int S, int NCB, int P, int CB, int DWQ, int PWQ>
 __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& tab, RsBars& bars,
                                             uint8_t* sA, uint32_t tm_slot, int k, int set, int q,
                                             int lane, volatile int* abort_flag) {
@@ -313,7 +312,7 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
 #pragma unroll
         for (int h = 0; h < NV; ++h)
           *reinterpret_cast<uint4*>(atile + h * 2048) =
-              rs_requant16<DWCLAMP>(v[h], tab.dw_mh, tab.dw_bs, h * 16, p.dw_lo4, p.dw_hi4);
+              rs_requant16<DWQ>(v[h], tab.dw_mh, tab.dw_bs, h * 16, p.dw_lo4, p.dw_hi4);
         rs_fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars.apw_full[set]);
@@ -338,7 +337,7 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
 #pragma unroll
           for (int h = 0; h < NP; ++h)
             reinterpret_cast<uint4*>(o)[h] =
-                rs_requant16<PWCLAMP>(u[h], tab.pw_mh, tab.pw_bs, h * 16, p.pw_lo4, p.pw_hi4);
+                rs_requant16<PWQ>(u[h], tab.pw_mh, tab.pw_bs, h * 16, p.pw_lo4, p.pw_hi4);
         }
       } else {
         if (valid) {
@@ -357,14 +356,14 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
 #pragma unroll
           for (int h = 0; h < NV; ++h)
             reinterpret_cast<uint4*>(o)[h] =
-                rs_requant16<DWCLAMP>(v[h], mh, bs, h * 16, p.dw_lo4, p.dw_hi4);
+                rs_requant16<DWQ>(v[h], mh, bs, h * 16, p.dw_lo4, p.dw_hi4);
         }
       }
     }
   }
 }
 
-template <int CG, int NPW, int S, int NCB, int P, bool DWCLAMP, bool PWCLAMP>
+template <int CG, int NPW, int S, int NCB, int P, int DWQ, int PWQ>
 __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
     k_dwrs_s8(const __grid_constant__ CUtensorMap tmIn, const RsArgs p,
               const __grid_constant__ DwPwTable tab) {
@@ -686,18 +685,18 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
     // One code path per CTA: its channel block's table offsets are
     // compile-time constants.
     if (cb == 0) {
-      rs_epilogue<CG, NPW, S, NCB, P, 0, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q, lane,
+      rs_epilogue<CG, NPW, S, NCB, P, 0, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q, lane,
                                                         abort_flag);
     } else if constexpr (NCB >= 2) {
       if (cb == 1) {
-        rs_epilogue<CG, NPW, S, NCB, P, 1, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+        rs_epilogue<CG, NPW, S, NCB, P, 1, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
                                                           lane, abort_flag);
       } else if constexpr (NCB >= 4) {
         if (cb == 2)
-          rs_epilogue<CG, NPW, S, NCB, P, 2, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+          rs_epilogue<CG, NPW, S, NCB, P, 2, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
         else
-          rs_epilogue<CG, NPW, S, NCB, P, 3, DWCLAMP, PWCLAMP>(p, tab, bars[k], sA, tm, k, set, q,
+          rs_epilogue<CG, NPW, S, NCB, P, 3, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
       }
     }
@@ -711,7 +710,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
   }
 }
 
-template <int CG, int NPW, int S, int NCB, int P, bool DWC, bool PWC>
+template <int CG, int NPW, int S, int NCB, int P, int DWC, int PWC>
 cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int grid,
                       int smem, cudaStream_t s) {
   static std::atomic<uint64_t> done{0};
@@ -730,6 +729,22 @@ cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& ta
   return cudaGetLastError();
 }
 
+// The pointwise epilogue variant (ep_flags of the pointwise op).
+template <int CG, int NPW, int S, int NCB, int P, int DWQ>
+cudaError_t rs_launch_pw(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int pwq,
+                         int grid, int smem, cudaStream_t s) {
+  if constexpr (NPW == 0) {
+    return rs_launch<CG, NPW, S, NCB, P, DWQ, 0>(m, a, tab, grid, smem, s);
+  } else {
+    switch (pwq) {
+      case 0: return rs_launch<CG, NPW, S, NCB, P, DWQ, 0>(m, a, tab, grid, smem, s);
+      case 1: return rs_launch<CG, NPW, S, NCB, P, DWQ, 1>(m, a, tab, grid, smem, s);
+      case 2: return rs_launch<CG, NPW, S, NCB, P, DWQ, 2>(m, a, tab, grid, smem, s);
+      default: return rs_launch<CG, NPW, S, NCB, P, DWQ, 3>(m, a, tab, grid, smem, s);
+    }
+  }
+}
+
 // Shared memory of one launch (bytes) and its input stages.
 template <int CG, int NPW, int S, int NCB, int P>
 bool rs_smem(int* smem, int* stages) {
@@ -744,7 +759,7 @@ bool rs_smem(int* smem, int* stages) {
 }
 
 template <int CG, int NPW, int S, int NCB, int P>
-cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, bool dwc, bool pwc,
+cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, int dwq, int pwq,
                      int num_sms, cudaStream_t s) {
   using Sh = RsShape<CG, NPW, S, NCB, P>;
   int smem = 0;
@@ -754,15 +769,11 @@ cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, bool 
       (static_cast<int64_t>(a.strips) + Sh::NS - 1) / Sh::NS, std::max(1, num_sms / NCB)));
   const int grid = per_block * NCB;
   if (a.strips <= 0) return cudaSuccess;
-  if constexpr (NPW == 0) {
-    return dwc ? rs_launch<CG, NPW, S, NCB, P, true, false>(m, a, tab, grid, smem, s)
-               : rs_launch<CG, NPW, S, NCB, P, false, false>(m, a, tab, grid, smem, s);
-  } else {
-    if (dwc)
-      return pwc ? rs_launch<CG, NPW, S, NCB, P, true, true>(m, a, tab, grid, smem, s)
-                 : rs_launch<CG, NPW, S, NCB, P, true, false>(m, a, tab, grid, smem, s);
-    return pwc ? rs_launch<CG, NPW, S, NCB, P, false, true>(m, a, tab, grid, smem, s)
-               : rs_launch<CG, NPW, S, NCB, P, false, false>(m, a, tab, grid, smem, s);
+  switch (dwq) {
+    case 0: return rs_launch_pw<CG, NPW, S, NCB, P, 0>(m, a, tab, pwq, grid, smem, s);
+    case 1: return rs_launch_pw<CG, NPW, S, NCB, P, 1>(m, a, tab, pwq, grid, smem, s);
+    case 2: return rs_launch_pw<CG, NPW, S, NCB, P, 2>(m, a, tab, pwq, grid, smem, s);
+    default: return rs_launch_pw<CG, NPW, S, NCB, P, 3>(m, a, tab, pwq, grid, smem, s);
   }
 }
 
@@ -799,7 +810,7 @@ int rs_packing(const pspml_op_desc& d, int npw) {
 
 // One launch over `batch` samples (strip count below 2^31).
 cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
-                    const uint8_t* wpw_packed, const DwPwTable& tab, bool pwc, int32_t pw_min,
+                    const uint8_t* wpw_packed, const DwPwTable& tab, int pwq, int32_t pw_min,
                     int32_t pw_max, int64_t batch, const int8_t* in, int8_t* out,
                     unsigned* dev_err, int num_sms, cudaStream_t s) {
   const int C = dw.in_c;
@@ -829,7 +840,7 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
   a.pw_lo4 = splat4(pw_min);
   a.pw_hi4 = splat4(pw_max);
   a.err = dev_err;
-  const bool dwc = dw.act_min > -128 || dw.act_max < 127;
+  const int dwq = ep_flags(dw.act_min, dw.act_max, dw.zp_out);
 
   CUtensorMap m;
   if (S == 1) {
@@ -856,36 +867,36 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
       return cudaErrorInvalidValue;
   }
   if (npw == 64 && C == 64 && S == 1 && P == 1)
-    return rs_shape<2, 64, 1, 1, 1>(m, a, tab, dwc, pwc, num_sms, s);
+    return rs_shape<2, 64, 1, 1, 1>(m, a, tab, dwq, pwq, num_sms, s);
   if (npw != 0) return cudaErrorInvalidValue;
   if (P == 1) {
     if (S == 1) {
-      if (C == 32) return rs_shape<1, 0, 1, 1, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 64) return rs_shape<2, 0, 1, 1, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 128) return rs_shape<2, 0, 1, 2, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 256) return rs_shape<2, 0, 1, 4, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 32) return rs_shape<1, 0, 1, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 1, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 1, 2, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 1, 4, 1>(m, a, tab, dwq, 0, num_sms, s);
     } else {
-      if (C == 32) return rs_shape<1, 0, 2, 1, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 64) return rs_shape<2, 0, 2, 1, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 128) return rs_shape<2, 0, 2, 2, 1>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 256) return rs_shape<2, 0, 2, 4, 1>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 32) return rs_shape<1, 0, 2, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 2, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 2, 2, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 2, 4, 1>(m, a, tab, dwq, 0, num_sms, s);
     }
   } else if (S == 1) {
     if (P == 2) {
-      if (C == 64) return rs_shape<2, 0, 1, 1, 2>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 128) return rs_shape<2, 0, 1, 2, 2>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 256) return rs_shape<2, 0, 1, 4, 2>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 1, 1, 2>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 1, 2, 2>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 1, 4, 2>(m, a, tab, dwq, 0, num_sms, s);
     } else {
-      if (C == 64) return rs_shape<2, 0, 1, 1, 4>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 128) return rs_shape<2, 0, 1, 2, 4>(m, a, tab, dwc, false, num_sms, s);
-      if (C == 256) return rs_shape<2, 0, 1, 4, 4>(m, a, tab, dwc, false, num_sms, s);
+      if (C == 64) return rs_shape<2, 0, 1, 1, 4>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 1, 2, 4>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 1, 4, 4>(m, a, tab, dwq, 0, num_sms, s);
     }
   }
   return cudaErrorInvalidValue;
 }
 
 cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
-                   const uint8_t* wpw_packed, const DwPwTable& tab, bool pwc, int32_t pw_min,
+                   const uint8_t* wpw_packed, const DwPwTable& tab, int pwq, int32_t pw_min,
                    int32_t pw_max, int64_t out_per, int64_t batch, const int8_t* in, int8_t* out,
                    unsigned* dev_err, int num_sms, cudaStream_t s) {
   const int64_t per_sample = static_cast<int64_t>((dw.out_w + 127) / 128);
@@ -894,7 +905,7 @@ cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
   const int64_t in_per = static_cast<int64_t>(dw.in_h) * dw.in_w * dw.in_c;
   for (int64_t b0 = 0; b0 < batch; b0 += chunk) {
     const cudaError_t e =
-        rs_once(dw, pdw, npw, wpw_packed, tab, pwc, pw_min, pw_max, std::min(chunk, batch - b0),
+        rs_once(dw, pdw, npw, wpw_packed, tab, pwq, pw_min, pw_max, std::min(chunk, batch - b0),
                 in + b0 * in_per, out + b0 * out_per, dev_err, num_sms, s);
     if (e != cudaSuccess) return e;
   }
@@ -937,7 +948,7 @@ cudaError_t launch_dwrs_dw(const pspml_op_desc& d, const PreparedOp& p, int64_t 
   for (int k = 0; k < p.ncls; ++k)
     for (int c = 0; c < C; ++c) tab.dw_dbias[k * C + c] = p.table->dbias[k * C + c];
   const int64_t out_per = static_cast<int64_t>(d.out_h) * d.out_w * d.out_c;
-  return rs_run(d, p, 0, nullptr, tab, false, -128, 127, out_per, batch, in, out, dev_err,
+  return rs_run(d, p, 0, nullptr, tab, 0, -128, 127, out_per, batch, in, out, dev_err,
                 num_sms, s);
 }
 
@@ -945,9 +956,9 @@ cudaError_t launch_dwrs_pair(const pspml_op_desc& dw, const PreparedOp& pdw,
                              const pspml_op_desc& pw, const uint8_t* wpw_packed,
                              const DwPwTable& tab, int64_t batch, const int8_t* in, int8_t* out,
                              unsigned* dev_err, int num_sms, cudaStream_t s) {
-  const bool pwc = pw.act_min > -128 || pw.act_max < 127;
+  const int pwq = ep_flags(pw.act_min, pw.act_max, pw.zp_out);
   const int64_t out_per = static_cast<int64_t>(pw.out_h) * pw.out_w * pw.out_c;
-  return rs_run(dw, pdw, pw.out_c, wpw_packed, tab, pwc, pw.act_min, pw.act_max, out_per, batch,
+  return rs_run(dw, pdw, pw.out_c, wpw_packed, tab, pwq, pw.act_min, pw.act_max, out_per, batch,
                 in, out, dev_err, num_sms, s);
 }
 

@@ -52,8 +52,11 @@ bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc);
 constexpr int kTabRq = 512;
 constexpr int kTabDelta = 4096;
 struct EpiTable {
-  int2 mh[kTabRq];           // {M, high word of C - 2^32}
-  int2 bs[kTabRq];           // {folded bias of class base_cls, right shift - 1}
+  // Fast form: mh = {M, high word of C - 2^32}, bs = {folded bias of class
+  // base_cls, right shift - 1}; floor form (floor_entry): the bias folded
+  // into D, mh = {M, high word of D}, bs = {low word of D, right shift - 1}.
+  int2 mh[kTabRq];
+  int2 bs[kTabRq];
   int32_t dbias[kTabDelta];  // [ncls][N]: folded bias of the class - that of base_cls
 };
 
@@ -69,9 +72,51 @@ __device__ __forceinline__ int32_t rq_tab(int32_t a, const int2 mh, int32_t sr) 
   return (hi + static_cast<int32_t>((~static_cast<uint32_t>(a) | lo) >> 31)) >> sr;
 }
 
+// Epilogue variants of the table kernels: bit 0 clamps to the activation
+// range (narrower than int8), bit 1 takes the floor form.
+constexpr int kEpClamp = 1;
+constexpr int kEpFloor = 2;
+inline int ep_flags(int32_t act_min, int32_t act_max, int32_t zp_out) {
+  return ((act_min > -128 || act_max < 127) ? kEpClamp : 0) |
+         (act_min >= zp_out ? kEpFloor : 0);
+}
+
+// Floor-form table entry (ops with act_min >= zp_out, rq_fast_floor): the
+// folded bias moves into the 64-bit addend, D = bias * M + C with the full
+// C = 2^30 + 2^(30+r) + zp_out * 2^(31+r); the entry is
+// mh = {M, high word of D}, bs = {low word of D, r - 1}, and
+//   out + zp_out = high word of (acc * M + D) >> (r - 1).
+// One wide multiply-add and one shift per output.  The table builder makes
+// these entries for exactly the ops whose ep_flags have kEpFloor, so every
+// kernel reading an op's table agrees on its form.
+__host__ inline void floor_entry(int32_t m, uint32_t c_lo, int32_t c_hi, int32_t sr,
+                                 int32_t bias, int2* mh, int2* bs) {
+  const int64_t c =
+      static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(c_hi)) << 32) | c_lo) +
+      (int64_t{1} << 32);
+  const int64_t d = static_cast<int64_t>(bias) * m + c;
+  *mh = make_int2(m, static_cast<int32_t>(d >> 32));
+  *bs = make_int2(static_cast<int32_t>(static_cast<uint32_t>(static_cast<uint64_t>(d))), sr);
+}
+
+// Table requantisation of an accumulator (plus any border-class bias
+// difference) in the op's form.
+template <int Q>
+__device__ __forceinline__ int32_t rq_tab_q(uint32_t acc, const int2 mh, const int2 bs) {
+  if constexpr ((Q & kEpFloor) != 0) {
+    const int64_t d =
+        static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(mh.y)) << 32) |
+                             static_cast<uint32_t>(bs.x));
+    const int64_t t = static_cast<int64_t>(static_cast<int32_t>(acc)) * mh.x + d;
+    return static_cast<int32_t>(t >> 32) >> bs.y;
+  } else {
+    return rq_tab(static_cast<int32_t>(acc) + bs.x, mh, bs.y);
+  }
+}
+
 // Requantises 16 accumulators of channels ch .. ch+15 (table entries, bias
-// of the base class) into 16 packed bytes.
-template <bool CLAMP>
+// of the base class) into 16 packed bytes; Q: the op's ep_flags.
+template <int Q>
 __device__ __forceinline__ uint4 requant16_tab(const uint32_t* v, const EpiTable& tab, int ch,
                                                uint32_t lo4, uint32_t hi4) {
   uint32_t packed[4];
@@ -81,11 +126,10 @@ __device__ __forceinline__ uint4 requant16_tab(const uint32_t* v, const EpiTable
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int c = ch + 4 * g + k;
-      const int2 bs = tab.bs[c];
-      r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]) + bs.x, tab.mh[c], bs.y);
+      r[k] = rq_tab_q<Q>(v[4 * g + k], tab.mh[c], tab.bs[c]);
     }
     uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
-    if constexpr (CLAMP) w = clamp4(w, lo4, hi4);
+    if constexpr ((Q & kEpClamp) != 0) w = clamp4(w, lo4, hi4);
     packed[g] = w;
   }
   return make_uint4(packed[0], packed[1], packed[2], packed[3]);

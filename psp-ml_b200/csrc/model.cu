@@ -279,9 +279,16 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     auto t = std::make_unique<EpiTable>();
     std::memset(t.get(), 0, sizeof(EpiTable));
     const size_t base = static_cast<size_t>(p.base_cls) * n;
+    const pspml_op_desc& d = m->ops[i].d;
+    const bool floor_form = (ep_flags(d.act_min, d.act_max, d.zp_out) & kEpFloor) != 0;
     for (int c = 0; c < n; ++c) {
-      t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
-      t->bs[c] = make_int2(bias[base + c], rq[c].sr);
+      if (floor_form) {
+        floor_entry(rq[c].m, rq[c].c_lo, rq[c].c_hi, rq[c].sr, bias[base + c], &t->mh[c],
+                    &t->bs[c]);
+      } else {
+        t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
+        t->bs[c] = make_int2(bias[base + c], rq[c].sr);
+      }
     }
     if (p.ncls > 1)
       for (int k = 0; k < p.ncls; ++k)
@@ -317,9 +324,14 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     if (!low_word_fixed) continue;
     auto t = std::make_unique<SmallConvTable>();
     std::memset(t.get(), 0, sizeof(SmallConvTable));
+    const bool floor_form = (ep_flags(d.act_min, d.act_max, d.zp_out) & kEpFloor) != 0;
     for (int c = 0; c < 32; ++c) {
-      t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
-      t->bs[c] = make_int2(bias[c], rq[c].sr);
+      if (floor_form) {
+        floor_entry(rq[c].m, rq[c].c_lo, rq[c].c_hi, rq[c].sr, bias[c], &t->mh[c], &t->bs[c]);
+      } else {
+        t->mh[c] = make_int2(rq[c].m, rq[c].c_hi);
+        t->bs[c] = make_int2(bias[c], rq[c].sr);
+      }
       for (int j = 0; j < 4 && j < p.nw; ++j) t->w[c][j] = w[static_cast<size_t>(c) * p.nw + j];
     }
     p.sc_table = t.get();

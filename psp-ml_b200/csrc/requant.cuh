@@ -88,18 +88,46 @@ __device__ __forceinline__ int32_t rq_fast(int32_t a, const RqChannel& q) {
   return (hi + static_cast<int32_t>((~static_cast<uint32_t>(a) | lo) >> 31)) >> q.sr;
 }
 
+// Floor form, for ops whose activation clamp starts at or above the output
+// zero point (act_min >= zp_out: ReLU, ReLU6, ...): the [a < 0] correction
+// of the fast form is left out,
+//   out + zp_out = floor((p + C) / 2^(31 + r)) = (hi' + 1) >> (r - 1)
+// with hi' the high word of p + (C - 2^32) as the table stores it.  For
+// a >= 0 the correction is zero, so this is the fast form.  For a < 0 (so
+// p <= -M < 0) both this value and TFLite's are at most zp_out: TFLite's
+// high-mul and power-of-two division keep the sign of a, and here
+// p + 2^30 + 2^(30+r) < 2^(31+r).  After the clamp to [act_min, act_max]
+// both are act_min.  Two instructions fewer than the fast form.
+__device__ __forceinline__ int32_t rq_fast_floor(int32_t a, const RqChannel& q) {
+  const int64_t c =
+      static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi)) << 32) | q.c_lo);
+  const int64_t t = static_cast<int64_t>(a) * q.m + c;
+  return (static_cast<int32_t>(t >> 32) + 1) >> q.sr;
+}
+
 // requantised value + zp_out, before clamping; any channel.
 __device__ __forceinline__ int32_t rq_apply(int32_t a, const RqChannel& q) {
   if (q.sr >= 0) return rq_fast(a, q);
   return mbqm_dev(a, q.m, static_cast<int32_t>(q.c_lo)) + q.c_hi;
 }
 
-// Requantisation selected at compile time: FAST when every channel of the
-// op has a fast-form table entry (the op's all-fast flag).
-template <bool FAST>
+// Requantisation forms a kernel is compiled for.
+constexpr int kRqGeneral = 0;  // any channel: closed form or the literal steps
+constexpr int kRqFast = 1;     // every channel of the op has a fast-form entry
+constexpr int kRqFloor = 2;    // fast form and act_min >= zp_out (rq_fast_floor)
+
+// Requantisation selected at compile time.
+template <int RQ>
 __device__ __forceinline__ int32_t rq_sel(int32_t a, const RqChannel& q) {
-  if constexpr (FAST) return rq_fast(a, q);
+  if constexpr (RQ == kRqFloor) return rq_fast_floor(a, q);
+  if constexpr (RQ == kRqFast) return rq_fast(a, q);
   return rq_apply(a, q);
+}
+
+// The form of an op: `all_fast` when every channel has a fast-form entry.
+inline int rq_form(bool all_fast, int32_t act_min, int32_t zp_out) {
+  if (!all_fast) return kRqGeneral;
+  return act_min >= zp_out ? kRqFloor : kRqFast;
 }
 
 __device__ __forceinline__ RqChannel load_rq(const RqChannel* p) {

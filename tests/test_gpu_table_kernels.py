@@ -7,6 +7,8 @@ classes as bias differences, 256-row GEMM tiles for narrow outputs).  These
 tests run single ops through that path and compare every output byte with
 the oracle (the whole-network tests only see the logits, after global
 average pooling)."""
+import zlib
+
 import numpy as np
 import pytest
 
@@ -141,3 +143,79 @@ def test_stem_conv_static_table(ctx, oracle_mod, B, H, W, stride, zp_in, act):
     b, m, s = random_quant(r, 32)
     got = run_op_model(ctx, d, B, x, w, b, m, s)
     _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))
+
+
+def _dw(H, W, C, stride, zp_in, zp_out, act):
+    return conv_desc(capi.OP_DEPTHWISE_CONV2D, H, W, C, C, k=3, stride=stride, zp_in=zp_in,
+                     zp_out=zp_out, act=act)
+
+
+def _pw(H, W, K, N, zp_in, zp_out, act):
+    return make_desc(kind=capi.OP_CONV2D, in_h=H, in_w=W, in_c=K, out_h=H, out_w=W, out_c=N,
+                     zp_in=zp_in, zp_out=zp_out, act_min=act[0], act_max=act[1])
+
+
+def _fc(K, N, zp_in, zp_out, act):
+    return make_desc(kind=capi.OP_FULLY_CONNECTED, in_h=1, in_w=1, in_c=K, out_h=1, out_w=1,
+                     out_c=N, zp_in=zp_in, zp_out=zp_out, act_min=act[0], act_max=act[1])
+
+
+# Ops whose clamp starts at or above the output zero point (ReLU and the
+# like) take the floor form of the requantisation in every kernel: the
+# negative-accumulator rounding term is left out (those outputs clamp to
+# act_min either way) and the table holds the bias folded into the 64-bit
+# addend.  Each case: (label, batch, op descs of a chain).
+FLOOR_CASES = [
+    ("dw_tc static, clamp", 1, [_dw(6, 384, 96, 1, -3, -5, (-5, 127))]),
+    ("dw_tc static, zp -128", 2, [_dw(4, 200, 96, 1, 7, -128, (-128, 127))]),
+    ("row-streaming s1", 2, [_dw(5, 256, 64, 1, 3, -128, (-128, 127))]),
+    ("row-streaming s2 blocks, clamp", 2, [_dw(8, 256, 128, 2, -128, 10, (10, 127))]),
+    ("row-streaming packed rows", 3, [_dw(5, 32, 256, 1, -128, -128, (-128, 127))]),
+    ("cuda-core dw s2, clamp", 2, [_dw(6, 128, 128, 2, 0, -6, (-6, 127))]),
+    ("cuda-core dw s1, 36 channels", 2, [_dw(5, 40, 36, 1, 2, -128, (-128, 120))]),
+    ("gemm static 128", 2, [_pw(6, 40, 64, 128, -128, -128, (-128, 127))]),
+    ("gemm static 256-row tiles, clamp", 2, [_pw(8, 64, 32, 64, 5, 3, (3, 100))]),
+    ("gemm 3x3 table", 2, [conv_desc(capi.OP_CONV2D, 9, 20, 32, 64, k=3, stride=1, zp_in=-128,
+                                     zp_out=-128, act=(-128, 127))]),
+    ("gemm 3x3 table, clamp", 2, [conv_desc(capi.OP_CONV2D, 7, 12, 16, 48, k=3, stride=1,
+                                            zp_in=4, zp_out=5, act=(5, 127))]),
+    ("fc", 300, [_fc(256, 100, -3, -128, (-128, 127))]),
+    ("stem table", 2, [conv_desc(capi.OP_CONV2D, 20, 64, 1, 32, k=3, stride=2, zp_in=0,
+                                 zp_out=-100, act=(-100, 127))]),
+    ("small conv in_c 3", 2, [conv_desc(capi.OP_CONV2D, 16, 16, 3, 32, k=3, stride=1,
+                                        zp_in=-128, zp_out=-128, act=(-128, 127))]),
+    ("dw+pw pair 32->64", 2, [_dw(4, 256, 32, 1, -7, -128, (-128, 127)),
+                              _pw(4, 256, 32, 64, -128, 2, (2, 127))]),
+    ("dw+pw pair 64->64 (row-streaming)", 2, [_dw(3, 256, 64, 1, 5, 6, (6, 127)),
+                                              _pw(3, 256, 64, 64, 6, -128, (-128, 127))]),
+    ("dw+pw pair, pointwise not floor", 2, [_dw(3, 256, 64, 1, 5, -128, (-128, 127)),
+                                            _pw(3, 256, 64, 64, -128, 0, (-128, 127))]),
+]
+
+
+def _weights(r, d):
+    kind = int(d["kind"])
+    if kind == capi.OP_DEPTHWISE_CONV2D:
+        n = 9 * int(d["in_c"])
+    elif kind == capi.OP_FULLY_CONNECTED:
+        n = int(d["in_c"]) * int(d["out_c"])
+    else:
+        n = int(d["out_c"]) * int(d["kernel_h"]) * int(d["kernel_w"]) * int(d["in_c"])
+    return r.integers(-127, 128, n).astype(np.int8)
+
+
+@pytest.mark.parametrize("label,B,descs", FLOOR_CASES, ids=[c[0] for c in FLOOR_CASES])
+def test_floor_form_paths(ctx, oracle_mod, label, B, descs):
+    r = np.random.default_rng(zlib.crc32(label.encode()))
+    ops = []
+    for d in descs:
+        b, m, s = random_quant(r, int(d["out_c"]))
+        ops.append((d, _weights(r, d), b, m, s))
+    d0 = descs[0]
+    x = r.integers(-128, 128, B * int(d0["in_h"]) * int(d0["in_w"]) * int(d0["in_c"]))
+    x = x.astype(np.int8)
+    got = run_chain_model(ctx, ops, B, x)
+    want = x
+    for d, w, b, m, s in ops:
+        want = oracle_mod.op_s8(d, B, want, w, b, m, s)
+    _check(got, want)

@@ -370,7 +370,12 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
       for (int w = 0; w < NW; ++w)
         acc = __dp4a(static_cast<int>(x[w]), static_cast<int>(tab.w[co][w]), acc);
-      r[j] = rq_tab_q<Q>(static_cast<uint32_t>(acc), tab.mh[co], tab.bs[co]);
+      if constexpr ((Q & kEpFloor) != 0) {
+        r[j] = rq_tab_q<Q>(static_cast<uint32_t>(acc), tab.mh[co], tab.bs[co]);
+      } else {
+        const int2 bs = tab.bs[co];
+        r[j] = rq_tab(acc + bs.x, tab.mh[co], bs.y);
+      }
     }
     uint32_t w4 = pack_sat4(r[0], r[1], r[2], r[3]);
     if constexpr ((Q & kEpClamp) != 0) w4 = clamp4(w4, g.lo4, g.hi4);

@@ -87,7 +87,12 @@ __device__ __forceinline__ uint4 requant16_pair(const uint32_t* v, const int2* m
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int c = ch + 4 * g + k;
-      r[k] = rq_tab_q<Q>(v[4 * g + k], mh[c], bs[c]);
+      if constexpr ((Q & kEpFloor) != 0) {
+        r[k] = rq_tab_q<Q>(v[4 * g + k], mh[c], bs[c]);
+      } else {
+        const int2 b = bs[c];
+        r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]) + b.x, mh[c], b.y);
+      }
     }
     uint32_t w = pack_sat4(r[0], r[1], r[2], r[3]);
     if constexpr ((Q & kEpClamp) != 0) w = clamp4(w, lo4, hi4);

@@ -69,35 +69,6 @@ __device__ __forceinline__ uint32_t finish4(int32_t a0, int32_t a1, int32_t a2, 
   return w;
 }
 
-// Floor form with the bias folded into each channel's 64-bit addend
-// (d = bias * M + C, as floor_entry builds it), for threads that keep their
-// channels' constants in registers: one wide multiply-add and one shift per
-// output.
-struct FloorCh {
-  int64_t d;
-  int32_t m, sr;
-};
-__device__ __forceinline__ FloorCh floor_ch(int32_t bias, const RqChannel& q) {
-  FloorCh f;
-  const int64_t c =
-      static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi)) << 32) | q.c_lo) +
-      (int64_t{1} << 32);
-  f.d = static_cast<int64_t>(bias) * q.m + c;
-  f.m = q.m;
-  f.sr = q.sr;
-  return f;
-}
-__device__ __forceinline__ int32_t rq_floor_ch(int32_t acc, const FloorCh& f) {
-  return static_cast<int32_t>((static_cast<int64_t>(acc) * f.m + f.d) >> 32) >> f.sr;
-}
-__device__ __forceinline__ uint32_t finish4_floor(int32_t a0, int32_t a1, int32_t a2, int32_t a3,
-                                                  const FloorCh (&f)[4], const Geom& g) {
-  uint32_t w = pack_sat4(rq_floor_ch(a0, f[0]), rq_floor_ch(a1, f[1]), rq_floor_ch(a2, f[2]),
-                         rq_floor_ch(a3, f[3]));
-  if (g.clamp) w = clamp4(w, g.lo4, g.hi4);
-  return w;
-}
-
 __device__ __forceinline__ int8_t finish1(int32_t a, const RqChannel& q, const Geom& g) {
   int32_t r = rq_apply(a, q);
   r = max(r, -128);
@@ -141,13 +112,6 @@ __global__ void __launch_bounds__(128)
   const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff) + cw);
   const RqChannel q0 = load_rq(rq + 4 * cw), q1 = load_rq(rq + 4 * cw + 1),
                   q2 = load_rq(rq + 4 * cw + 2), q3 = load_rq(rq + 4 * cw + 3);
-  FloorCh fl[4];
-  if constexpr (RQ == kRqFloor) {
-    fl[0] = floor_ch(b.x, q0);
-    fl[1] = floor_ch(b.y, q1);
-    fl[2] = floor_ch(b.z, q2);
-    fl[3] = floor_ch(b.w, q3);
-  }
 
   const uint32_t zpw = splat4(g.zp_in);
   const int ix0 = ox0 * S - g.pl;
@@ -206,9 +170,7 @@ __global__ void __launch_bounds__(128)
     for (int p = 0; p < PX; ++p)
       if (ox0 + p < g.Wo)
         orow[static_cast<int64_t>(ox0 + p) * cwn] =
-            RQ == kRqFloor
-                ? finish4_floor(acc[p][0], acc[p][1], acc[p][2], acc[p][3], fl, g)
-                : finish4<RQ>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
+            finish4<RQ>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
 #pragma unroll
     for (int c = 0; c < NIN; ++c) {
       if (S == 1) {

@@ -2,6 +2,8 @@
 // requantisation fused in:
 //   k_dw3x3_s8       depthwise 3x3 (stride 1/2), dp4a with byte-masked weights
 //   k_small_conv_s8  conv with few input channels (K <= 128) over packed patches
+//   k_small_conv_tab_s8, k_stem_s2_s8  the 1 -> 32 channel 3x3 stem, constants
+//                    as kernel-parameter operands / in registers
 //   k_conv_direct_s8 any conv (fallback)
 //   k_dw_generic_s8  any depthwise conv (fallback)
 //   k_fc_warp_s8     FC with K % 16 != 0 (one warp per output)
@@ -348,6 +350,140 @@ __global__ void __launch_bounds__(128)
   op[1] = make_uint4(words[4], words[5], words[6], words[7]);
 }
 
+// Stride-2 variant of the constant-table stem for rows whose width is a
+// multiple of 8 and no left padding (the config-3 stem, 96x512 -> 48x256):
+// a thread keeps the weights and requant constants of 8 output channels in
+// registers and computes 4 consecutive pixels x 8 channels per output row,
+// for a strip of up to kStemRows rows.  Lane = pixel group (lane >> 2) x
+// channel group (lane & 3); a warp covers 32 consecutive pixels, a block
+// 128.  The block first copies the strip's 2 * rows + 1 input rows (257
+// bytes each, zero point outside the image) into shared memory with 8-byte
+// loads, so the row loop reads shared memory only; each pixel's patch words
+// come from its 9 bytes per row with funnel shifts and byte permutes.  The
+// weight words and per-channel constants are register operands, so an
+// output costs three dp4a, one wide multiply-add and a shift (floor form).
+constexpr int kStemRows = 16;
+constexpr int kStemRowBytes = 264;  // 257 used, 8-byte multiple
+
+template <int Q>
+__global__ void __launch_bounds__(128)
+    k_stem_s2_s8(const int8_t* __restrict__ in, int8_t* __restrict__ out, const Geom g,
+                 int64_t n_base, const __grid_constant__ SmallConvTable tab) {
+  __shared__ __align__(16) uint8_t srow[2 * kStemRows + 1][kStemRowBytes];
+  const int oy0 = blockIdx.y * kStemRows;
+  const int oy1 = min(oy0 + kStemRows, g.Ho);
+  const int64_t n = n_base + blockIdx.z;
+  const int xb = blockIdx.x * 256;  // first input column of the block
+  const int nrows = 2 * (oy1 - oy0) + 1;
+  const int iy0 = 2 * oy0 - g.pt;
+  const uint32_t zpw = splat4(g.zp_in);
+  {
+    const int8_t* img = in + n * static_cast<int64_t>(g.H) * g.W;
+    constexpr int kChunks = kStemRowBytes / 8;  // 33 chunks of 8 bytes per row
+    for (int c = threadIdx.x; c < nrows * kChunks; c += 128) {
+      const int rr = c / kChunks;
+      const int k = c - rr * kChunks;
+      const int iy = iy0 + rr;
+      const int x = xb + 8 * k;
+      uint2 v = make_uint2(zpw, zpw);
+      // W % 8 == 0: a chunk is wholly inside or outside the row.
+      if (iy >= 0 && iy < g.H && x < g.W)
+        v = __ldg(reinterpret_cast<const uint2*>(img + static_cast<int64_t>(iy) * g.W + x));
+      *reinterpret_cast<uint2*>(&srow[rr][8 * k]) = v;
+    }
+  }
+
+  const int lane = threadIdx.x & 31;
+  const int cg = lane & 3;
+  const int px = (threadIdx.x >> 5) * 32 + (lane >> 2) * 4;  // first pixel within the block
+  const int ox0 = blockIdx.x * 128 + px;
+  uint32_t w[8][3];
+  int32_t m[8], sr[8], cl[8], ch[8], bias[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int co = cg * 8 + k;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) w[k][j] = tab.w[co][j];
+    const int2 mh = tab.mh[co];
+    const int2 bs = tab.bs[co];
+    m[k] = mh.x;
+    sr[k] = bs.y;
+    if constexpr ((Q & kEpFloor) != 0) {
+      cl[k] = bs.x;  // low word of D (bias folded in)
+      ch[k] = mh.y;
+      bias[k] = 0;
+    } else {
+      cl[k] = 0x40000000;  // low word of C - 2^32
+      ch[k] = mh.y;
+      bias[k] = bs.x;
+    }
+  }
+  __syncthreads();
+  if (ox0 >= g.Wo) return;
+
+  // Bytes 2 * px .. 2 * px + 8 of shared row rr: {lo, hi, byte 8}.
+  auto row = [&](int rr, uint32_t& lo, uint32_t& hi, uint32_t& b8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(&srow[rr][2 * px]);
+    lo = v.x;
+    hi = v.y;
+    b8 = srow[rr][2 * px + 8];
+  };
+  uint32_t r0l, r0h, r0b, r1l, r1h, r1b, r2l, r2h, r2b;
+  row(0, r0l, r0h, r0b);
+  int8_t* obase = out + (n * g.Ho) * static_cast<int64_t>(g.Wo) * 32 + cg * 8;
+#pragma unroll 1
+  for (int oy = oy0; oy < oy1; ++oy) {
+    const int rr = 2 * (oy - oy0);
+    row(rr + 1, r1l, r1h, r1b);
+    row(rr + 2, r2l, r2h, r2b);
+    int8_t* orow = obase + (static_cast<int64_t>(oy) * g.Wo + ox0) * 32;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // Bytes 2j .. 2j+3 of each row.
+      const uint32_t s0 = j == 0 ? r0l : j == 1 ? __funnelshift_r(r0l, r0h, 16)
+                                       : j == 2 ? r0h : __funnelshift_r(r0h, r0b, 16);
+      const uint32_t s1 = j == 0 ? r1l : j == 1 ? __funnelshift_r(r1l, r1h, 16)
+                                       : j == 2 ? r1h : __funnelshift_r(r1h, r1b, 16);
+      const uint32_t s2 = j == 0 ? r2l : j == 1 ? __funnelshift_r(r2l, r2h, 16)
+                                       : j == 2 ? r2h : __funnelshift_r(r2h, r2b, 16);
+      // Patch words in filter order (ky, kx): taps 0-3, 4-7, 8.
+      const uint32_t p0 = __byte_perm(s0, s1, 0x4210);
+      const uint32_t p1 = __byte_perm(s1, s2, 0x5421);
+      const uint32_t p2 = s2 >> 16;
+      int32_t r[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        int32_t acc = __dp4a(static_cast<int>(p0), static_cast<int>(w[k][0]), 0);
+        acc = __dp4a(static_cast<int>(p1), static_cast<int>(w[k][1]), acc);
+        acc = __dp4a(static_cast<int>(p2), static_cast<int>(w[k][2]), acc);
+        const int64_t c = static_cast<int64_t>(
+            (static_cast<uint64_t>(static_cast<uint32_t>(ch[k])) << 32) |
+            static_cast<uint32_t>(cl[k]));
+        if constexpr ((Q & kEpFloor) != 0) {
+          const int64_t t = static_cast<int64_t>(acc) * m[k] + c;
+          r[k] = static_cast<int32_t>(t >> 32) >> sr[k];
+        } else {
+          const int32_t a = acc + bias[k];
+          const int64_t t = static_cast<int64_t>(a) * m[k] + c;
+          const uint32_t lo = static_cast<uint32_t>(t);
+          const int32_t hi = static_cast<int32_t>(t >> 32);
+          r[k] = (hi + static_cast<int32_t>((~static_cast<uint32_t>(a) | lo) >> 31)) >> sr[k];
+        }
+      }
+      uint32_t w0 = pack_sat4(r[0], r[1], r[2], r[3]);
+      uint32_t w1 = pack_sat4(r[4], r[5], r[6], r[7]);
+      if constexpr ((Q & kEpClamp) != 0) {
+        w0 = clamp4(w0, g.lo4, g.hi4);
+        w1 = clamp4(w1, g.lo4, g.hi4);
+      }
+      *reinterpret_cast<uint2*>(orow + j * 32) = make_uint2(w0, w1);
+    }
+    r0l = r2l;
+    r0h = r2h;
+    r0b = r2b;
+  }
+}
+
 // ------------------------------------------------------------- direct conv
 // Fallback for any conv: one thread per (sample, oy, ox) and COB output
 // channels; weights of the chunk in shared memory as int32 [K][COB].
@@ -609,12 +745,38 @@ cudaError_t small_conv_tab(const Geom& g, const PreparedOp& p, int64_t batch, co
   return cudaGetLastError();
 }
 
+// Shapes of k_stem_s2_s8: the table kernel's shapes with stride 2, no left
+// padding, rows of a multiple of 8 bytes and 4 | out_w <= in_w / 2.
+static bool stem_s2_ok(const pspml_op_desc& d, const int8_t* in, const int8_t* out) {
+  return d.stride_h == 2 && d.stride_w == 2 && d.pad_left == 0 && d.pad_top >= 0 &&
+         d.pad_top <= 2 && d.in_w % 8 == 0 && d.out_w % 4 == 0 && 2 * d.out_w <= d.in_w &&
+         (reinterpret_cast<uintptr_t>(in) & 7u) == 0 && (reinterpret_cast<uintptr_t>(out) & 7u) == 0;
+}
+
+static cudaError_t stem_s2(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
+                    int8_t* out, cudaStream_t s) {
+  for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
+    const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
+    const dim3 grid((g.Wo + 127) / 128, (g.Ho + kStemRows - 1) / kStemRows, nz);
+    const SmallConvTable& t = *p.sc_table;
+    switch (ep_flags(g.act_min, g.act_max, g.zp_out)) {
+      case 0: k_stem_s2_s8<0><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+      case 1: k_stem_s2_s8<1><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+      case 2: k_stem_s2_s8<2><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+      default: k_stem_s2_s8<3><<<grid, 128, 0, s>>>(in, out, g, n0, t); break;
+    }
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_small_conv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                               const int8_t* in, int8_t* out, cudaStream_t s) {
   const Geom g = geom_of(d);
   if (p.sc_table != nullptr && p.all_fast_known && d.out_c == 32 && d.in_c == 1 &&
-      d.kernel_h == 3 && d.kernel_w == 3 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0)
+      d.kernel_h == 3 && d.kernel_w == 3 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    if (stem_s2_ok(d, in, out)) return stem_s2(g, p, batch, in, out, s);
     return small_conv_tab<1>(g, p, batch, in, out, s);
+  }
   switch (d.in_c) {
     case 1: return small_conv_cob<3, 3, 1>(g, p, batch, in, out, s);
     case 2: return small_conv_cob<3, 3, 2>(g, p, batch, in, out, s);

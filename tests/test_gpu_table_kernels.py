@@ -219,3 +219,32 @@ def test_floor_form_paths(ctx, oracle_mod, label, B, descs):
     for d, w, b, m, s in ops:
         want = oracle_mod.op_s8(d, B, want, w, b, m, s)
     _check(got, want)
+
+
+@pytest.mark.parametrize("B,H,W,pads,zp_in,zp_out,act", [
+    (2, 96, 512, None, 0, -128, (-128, 127)),      # the config-3 stem (floor form)
+    (2, 20, 72, None, -9, 10, (-128, 127)),        # fast form, 36 px rows (partial warp)
+    (3, 11, 64, (1, 1, 0, 1), 5, 10, (-50, 100)),  # top padding, clamp, fast form
+    (2, 14, 256, (2, 0, 0, 1), -128, 7, (7, 90)),  # two rows of top padding, floor + clamp
+    (1, 7, 16, (0, 0, 0, 0), 3, -128, (-128, 127)),  # VALID: last input column unused
+])
+def test_stem_stride2_register_kernel(ctx, oracle_mod, B, H, W, pads, zp_in, zp_out, act):
+    """3x3 stride-2 conv with one input and 32 output channels on rows of a
+    multiple of 8 bytes: the register-resident stem kernel (four pixels x
+    eight channels per thread, strips of output rows)."""
+    r = np.random.default_rng(7800 + H * W + zp_out)
+    if pads is None:
+        d = conv_desc(capi.OP_CONV2D, H, W, 1, 32, k=3, stride=2, zp_in=zp_in, zp_out=zp_out,
+                      act=act)
+    else:
+        pt, pb, pl, pr = pads
+        d = make_desc(kind=capi.OP_CONV2D, in_h=H, in_w=W, in_c=1,
+                      out_h=(H + pt + pb - 3) // 2 + 1, out_w=(W + pl + pr - 3) // 2 + 1,
+                      out_c=32, kernel_h=3, kernel_w=3, stride_h=2, stride_w=2, pad_top=pt,
+                      pad_left=pl, pad_bottom=pb, pad_right=pr, zp_in=zp_in, zp_out=zp_out,
+                      act_min=act[0], act_max=act[1])
+    x = r.integers(-128, 128, B * H * W).astype(np.int8)
+    w = r.integers(-127, 128, 32 * 9).astype(np.int8)
+    b, m, s = random_quant(r, 32)
+    got = run_op_model(ctx, d, B, x, w, b, m, s)
+    _check(got, oracle_mod.op_s8(d, B, x, w, b, m, s))

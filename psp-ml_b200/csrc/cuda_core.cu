@@ -1,6 +1,6 @@
 // cuda_core.cu - int8 kernels on the CUDA cores, NHWC, with the TFLite
 // requantisation fused in:
-//   k_dw3x3_s8       depthwise 3x3 (stride 1/2), dp4a with byte-masked weights
+//   k_dw3x3_s8       depthwise 3x3 (stride 1/2), dp4a over the three taps of a filter row
 //   k_small_conv_s8  conv with few input channels (K <= 128) over packed patches
 //   k_small_conv_tab_s8, k_stem_s2_s8  the 1 -> 32 channel 3x3 stem, constants
 //                    as kernel-parameter operands / in registers
@@ -82,17 +82,23 @@ __device__ __forceinline__ int8_t finish1(int32_t a, const RqChannel& q, const G
 
 // ------------------------------------------------------ depthwise 3x3 (dp4a)
 // Thread: 4 channels (one word) x PX consecutive output pixels x a strip of
-// output rows (blockIdx.y).  It keeps the three input rows of the current
-// output row in registers and loads the S new rows of the next output row
-// while it computes, so the load latency overlaps the arithmetic.  Block:
-// 128 threads over (pixel group, channel word) pairs of one image
-// (blockIdx.z + n_base).  Weights [9][C]; out-of-image taps read zp_in.
+// output rows (blockIdx.y).  Each input row the thread needs (NIN pixels of
+// its 4 channels) is transposed once, with byte permutes, into per-channel
+// words of 4 consecutive pixels; a dp4a of such a word (funnel-shifted to
+// the output pixel's first tap) against the channel's packed row weights
+// [w(ky,0), w(ky,1), w(ky,2), 0] is the three taps of one filter row, so an
+// output costs three dp4a.  The thread keeps the three transposed rows of
+// the current output row in registers and loads the S new rows of the next
+// output row while it computes.  Block: 128 threads over (pixel group,
+// channel word) pairs of one image (blockIdx.z + n_base).  Weights [9][C];
+// out-of-image taps read zp_in.
 template <int S, int PX, int RQ>
 __global__ void __launch_bounds__(128)
     k_dw3x3_s8(const uint32_t* __restrict__ in, const uint32_t* __restrict__ f,
                const int32_t* __restrict__ bias_eff, const RqChannel* __restrict__ rq,
                uint32_t* __restrict__ out, const Geom g, int32_t rows_per, int64_t n_base) {
-  constexpr int NIN = (PX - 1) * S + 3;
+  constexpr int NIN = (PX - 1) * S + 3;  // input pixels of a row
+  constexpr int NT = (NIN + 3) / 4;      // transposed words per channel
   const int cwn = g.C >> 2;
   const int pair = blockIdx.x * 128 + threadIdx.x;
   const int groups = (g.Wo + PX - 1) / PX;
@@ -104,12 +110,19 @@ __global__ void __launch_bounds__(128)
   const int64_t n = n_base + blockIdx.z;
   const int ox0 = pg * PX;
 
-  uint32_t wm[9][4];
+  // wr[ky][c]: the three taps of filter row ky for channel c, byte kx.
+  uint32_t wr[3][4];
 #pragma unroll
-  for (int t = 0; t < 9; ++t) {
-    const uint32_t w = __ldg(f + t * cwn + cw);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) wm[t][j] = w & (0xFFu << (8 * j));
+  for (int ky = 0; ky < 3; ++ky) {
+    const uint32_t t0 = __ldg(f + (3 * ky) * cwn + cw);
+    const uint32_t t1 = __ldg(f + (3 * ky + 1) * cwn + cw);
+    const uint32_t t2 = __ldg(f + (3 * ky + 2) * cwn + cw);
+    const uint32_t lo01 = __byte_perm(t0, t1, 0x5140);  // t0.c0 t1.c0 t0.c1 t1.c1
+    const uint32_t hi01 = __byte_perm(t0, t1, 0x7362);  // t0.c2 t1.c2 t0.c3 t1.c3
+    wr[ky][0] = __byte_perm(lo01, t2, 0x0410) & 0x00FFFFFFu;
+    wr[ky][1] = __byte_perm(lo01, t2, 0x0532) & 0x00FFFFFFu;
+    wr[ky][2] = __byte_perm(hi01, t2, 0x0610) & 0x00FFFFFFu;
+    wr[ky][3] = __byte_perm(hi01, t2, 0x0732) & 0x00FFFFFFu;
   }
   const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff) + cw);
   const RqChannel q0 = load_rq(rq + 4 * cw), q1 = load_rq(rq + 4 * cw + 1),
@@ -127,11 +140,35 @@ __global__ void __launch_bounds__(128)
       x[c] = (row_ok && ix >= 0 && ix < g.W) ? __ldg(rowp + ix * cwn) : zpw;
     }
   };
-  uint32_t r0[NIN], r1[NIN], r2[NIN];
-  const int iy0 = oy0 * S - g.pt;
-  load_row(iy0, r0);
-  load_row(iy0 + 1, r1);
-  load_row(iy0 + 2, r2);
+  // Pixel-major words (4 channels each) -> channel-major words (4 pixels).
+  auto transpose = [&](const uint32_t (&x)[NIN], uint32_t (&t)[4][NT]) {
+#pragma unroll
+    for (int k = 0; k < NT; ++k) {
+      const uint32_t a = x[4 * k];
+      const uint32_t bb = 4 * k + 1 < NIN ? x[4 * k + 1] : zpw;
+      const uint32_t c = 4 * k + 2 < NIN ? x[4 * k + 2] : zpw;
+      const uint32_t d = 4 * k + 3 < NIN ? x[4 * k + 3] : zpw;
+      const uint32_t ab_lo = __byte_perm(a, bb, 0x5140);
+      const uint32_t ab_hi = __byte_perm(a, bb, 0x7362);
+      const uint32_t cd_lo = __byte_perm(c, d, 0x5140);
+      const uint32_t cd_hi = __byte_perm(c, d, 0x7362);
+      t[0][k] = __byte_perm(ab_lo, cd_lo, 0x5410);
+      t[1][k] = __byte_perm(ab_lo, cd_lo, 0x7632);
+      t[2][k] = __byte_perm(ab_hi, cd_hi, 0x5410);
+      t[3][k] = __byte_perm(ab_hi, cd_hi, 0x7632);
+    }
+  };
+  uint32_t t0[4][NT], t1[4][NT], t2[4][NT];
+  {
+    uint32_t x[NIN];
+    const int iy0 = oy0 * S - g.pt;
+    load_row(iy0, x);
+    transpose(x, t0);
+    load_row(iy0 + 1, x);
+    transpose(x, t1);
+    load_row(iy0 + 2, x);
+    transpose(x, t2);
+  }
   uint32_t* obase = out + (n * g.Ho) * static_cast<int64_t>(g.Wo) * cwn + cw;
 #pragma unroll 1
   for (int oy = oy0; oy < oy1; ++oy) {
@@ -149,41 +186,42 @@ __global__ void __launch_bounds__(128)
         load_row(niy + 2, p1);
       }
     }
-    int32_t acc[PX][4];
-#pragma unroll
-    for (int p = 0; p < PX; ++p)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[p][j] = 0;
-#pragma unroll
-    for (int p = 0; p < PX; ++p)
-#pragma unroll
-      for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc[p][j] = __dp4a(static_cast<int>(r0[p * S + kx]), static_cast<int>(wm[kx][j]),
-                             acc[p][j]);
-          acc[p][j] = __dp4a(static_cast<int>(r1[p * S + kx]),
-                             static_cast<int>(wm[3 + kx][j]), acc[p][j]);
-          acc[p][j] = __dp4a(static_cast<int>(r2[p * S + kx]),
-                             static_cast<int>(wm[6 + kx][j]), acc[p][j]);
-        }
     uint32_t* orow = obase + static_cast<int64_t>(oy) * g.Wo * cwn;
 #pragma unroll
-    for (int p = 0; p < PX; ++p)
+    for (int p = 0; p < PX; ++p) {
+      // Bytes S*p .. S*p+3 of a channel's transposed row.
+      auto tap = [&](const uint32_t (&t)[NT]) -> uint32_t {
+        const int off = S * p;
+        if (off % 4 == 0) return t[off / 4];
+        return __funnelshift_r(t[off / 4], t[off / 4 + 1], 8 * (off % 4));
+      };
+      int32_t acc[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        int32_t a = __dp4a(static_cast<int>(tap(t0[c])), static_cast<int>(wr[0][c]), 0);
+        a = __dp4a(static_cast<int>(tap(t1[c])), static_cast<int>(wr[1][c]), a);
+        acc[c] = __dp4a(static_cast<int>(tap(t2[c])), static_cast<int>(wr[2][c]), a);
+      }
       if (ox0 + p < g.Wo)
         orow[static_cast<int64_t>(ox0 + p) * cwn] =
-            finish4<RQ>(acc[p][0], acc[p][1], acc[p][2], acc[p][3], b, q0, q1, q2, q3, g);
+            finish4<RQ>(acc[0], acc[1], acc[2], acc[3], b, q0, q1, q2, q3, g);
+    }
+    if (S == 1) {
 #pragma unroll
-    for (int c = 0; c < NIN; ++c) {
-      if (S == 1) {
-        r0[c] = r1[c];
-        r1[c] = r2[c];
-        r2[c] = p0[c];
-      } else {
-        r0[c] = r2[c];
-        r1[c] = p0[c];
-        r2[c] = p1[c];
-      }
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int k = 0; k < NT; ++k) {
+          t0[c][k] = t1[c][k];
+          t1[c][k] = t2[c][k];
+        }
+      transpose(p0, t2);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int k = 0; k < NT; ++k) t0[c][k] = t2[c][k];
+      transpose(p0, t1);
+      transpose(p1, t2);
     }
   }
 }

@@ -213,7 +213,7 @@ def run_reference(args, wl, rank, world):
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ------------------------------------------------------------------ our arm
@@ -395,12 +395,28 @@ def run_ours(args, wl, rank, world, local_rank):
             "clocks": clocks,
             "layers": layers,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     model.close()
     ctx.close()
 
 
+_RESULT = None  # the process's original standard output: the JSON line only
+
+
+def emit(line) -> None:
+    out = _RESULT if _RESULT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _RESULT
+    # Everything else that reaches standard output (library banners such as
+    # NCCL's version line, stray prints) goes to standard error, so that the
+    # result line is the only line on standard output.
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)

@@ -93,7 +93,7 @@ __device__ __forceinline__ int8_t finish1(int32_t a, const RqChannel& q, const G
 // channel word) pairs of one image (blockIdx.z + n_base).  Weights [9][C];
 // out-of-image taps read zp_in.
 template <int S, int PX, int RQ>
-__global__ void __launch_bounds__(128, S == 1 ? 5 : 4)
+__global__ void __launch_bounds__(128)
     k_dw3x3_s8(const uint32_t* __restrict__ in, const uint32_t* __restrict__ f,
                const int32_t* __restrict__ bias_eff, const RqChannel* __restrict__ rq,
                uint32_t* __restrict__ out, const Geom g, int32_t rows_per, int64_t n_base) {

@@ -493,8 +493,10 @@ cudaError_t launch_dw_tc(const pspml_op_desc& d, const PreparedOp& pp, int64_t b
                          cudaStream_t s) {
   const bool aligned = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) &
                         15u) == 0;
-  if (aligned && dwrs_dw_supported(d) && pp.table != nullptr && pp.all_fast_known &&
-      pp.ncls <= 9)
+  // The row-streaming kernel stores 32-byte words.
+  const bool aligned32 = (reinterpret_cast<uintptr_t>(out) & 31u) == 0;
+  if (aligned && aligned32 && dwrs_dw_supported(d) && pp.table != nullptr &&
+      pp.all_fast_known && pp.ncls <= 9)
     return launch_dwrs_dw(d, pp, batch, in, out, dev_err, num_sms, s);
   // Shapes only the row-streaming kernel takes, without a constant table
   // (a channel outside the fast requant form): the generic kernel reads the

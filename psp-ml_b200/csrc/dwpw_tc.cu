@@ -353,19 +353,18 @@ __global__ void __launch_bounds__(DwPwShape<CG, N>::kThreads, 1)
       const uint32_t tp = tb + static_cast<uint32_t>(C);
       uint32_t u0[16], u1[16];
       tmem_ld16_nowait(tp, u0);
+      static_assert(N % 32 == 0, "32-byte stores");
 #pragma unroll
       for (int c = 0; c < N; c += 32) {
         tmem_wait_ld(u0);
-        if (c + 16 < N) tmem_ld16_nowait(tp + static_cast<uint32_t>(c + 16), u1);
+        tmem_ld16_nowait(tp + static_cast<uint32_t>(c + 16), u1);
         const uint4 o0 = requant16_pair<PWQ>(u0, tab.pw_mh, tab.pw_bs, c, p.pw_lo4, p.pw_hi4);
-        if (valid) *reinterpret_cast<uint4*>(orow + c) = o0;
-        if (c + 16 < N) {
-          tmem_wait_ld(u1);
-          if (c + 32 < N) tmem_ld16_nowait(tp + static_cast<uint32_t>(c + 32), u0);
-          const uint4 o1 =
-              requant16_pair<PWQ>(u1, tab.pw_mh, tab.pw_bs, c + 16, p.pw_lo4, p.pw_hi4);
-          if (valid) *reinterpret_cast<uint4*>(orow + c + 16) = o1;
-        }
+        tmem_wait_ld(u1);
+        if (c + 32 < N) tmem_ld16_nowait(tp + static_cast<uint32_t>(c + 32), u0);
+        const uint4 o1 =
+            requant16_pair<PWQ>(u1, tab.pw_mh, tab.pw_bs, c + 16, p.pw_lo4, p.pw_hi4);
+        // 32-byte aligned: rows of N bytes, arena or checked output base.
+        if (valid) st_global_v8(orow + c, o0, o1);
       }
       tc_fence_before();
       __syncwarp();

@@ -344,10 +344,13 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
         if (lane == 0) mbar_arrive(&bars.pw_empty);
         if (valid) {
           int8_t* o = p.out + pix * NPW;
+          static_assert(NP % 2 == 0, "32-byte stores");
 #pragma unroll
-          for (int h = 0; h < NP; ++h)
-            reinterpret_cast<uint4*>(o)[h] =
-                rs_requant16<PWQ>(u[h], tab.pw_mh, tab.pw_bs, h * 16, p.pw_lo4, p.pw_hi4);
+          for (int h = 0; h < NP; h += 2)
+            st_global_v8(o + 16 * h,
+                         rs_requant16<PWQ>(u[h], tab.pw_mh, tab.pw_bs, h * 16, p.pw_lo4, p.pw_hi4),
+                         rs_requant16<PWQ>(u[h + 1], tab.pw_mh, tab.pw_bs, h * 16 + 16,
+                                           p.pw_lo4, p.pw_hi4));
         }
       } else {
         if (valid) {
@@ -363,10 +366,11 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
           int8_t* o = p.out + pix * Cop + cbase;
           const int2* mh = tab.dw_mh + cbase;
           const int2* bs = tab.dw_bs + cbase;
+          static_assert(NV % 2 == 0, "32-byte stores");
 #pragma unroll
-          for (int h = 0; h < NV; ++h)
-            reinterpret_cast<uint4*>(o)[h] =
-                rs_requant16<DWQ>(v[h], mh, bs, h * 16, p.dw_lo4, p.dw_hi4);
+          for (int h = 0; h < NV; h += 2)
+            st_global_v8(o + 16 * h, rs_requant16<DWQ>(v[h], mh, bs, h * 16, p.dw_lo4, p.dw_hi4),
+                         rs_requant16<DWQ>(v[h + 1], mh, bs, h * 16 + 16, p.dw_lo4, p.dw_hi4));
         }
       }
     }

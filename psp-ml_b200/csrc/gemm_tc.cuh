@@ -256,8 +256,10 @@ __device__ __forceinline__ void epilogue_chunk_tab(uint32_t (&v)[16], int8_t* ds
 
 // One output row of BN channels with compile-time table offsets: every
 // per-channel constant is a constant-bank operand of the instruction using
-// it.  Tensor-memory loads run one 16-column chunk ahead of the arithmetic.
-// Q: the op's ep_flags.
+// it.  Tensor-memory loads run one 16-column chunk ahead of the arithmetic;
+// for tiles of up to 128 columns each 32-column pair of chunks leaves as one
+// 32-byte store (rows of N bytes, N a multiple of 32, 32-byte aligned
+// output).  Q: the op's ep_flags.
 template <int BN, int NOFF, int Q>
 __device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_t taddr,
                                                     int8_t* orow, bool valid,
@@ -265,17 +267,23 @@ __device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_
   orow += NOFF;
   uint32_t v0[16], v1[16];
   tmem_ld16_nowait(taddr, v0);
+  static_assert(BN % 32 == 0, "32-byte stores");
 #pragma unroll
   for (int c = 0; c < BN; c += 32) {
     tmem_wait_ld(v0);
-    if (c + 16 < BN) tmem_ld16_nowait(taddr + c + 16, v1);
+    tmem_ld16_nowait(taddr + c + 16, v1);
     const uint4 w0 = requant16_tab<Q>(v0, tab, NOFF + c, p.lo4, p.hi4);
-    if (valid) *reinterpret_cast<uint4*>(orow + c) = w0;
-    if (c + 16 < BN) {
-      tmem_wait_ld(v1);
-      if (c + 32 < BN) tmem_ld16_nowait(taddr + c + 32, v0);
-      const uint4 w1 = requant16_tab<Q>(v1, tab, NOFF + c + 16, p.lo4, p.hi4);
+    if constexpr (BN > 128) {
+      // (Measured: 256-column rows lose with the paired store.)
+      if (valid) *reinterpret_cast<uint4*>(orow + c) = w0;
+    }
+    tmem_wait_ld(v1);
+    if (c + 32 < BN) tmem_ld16_nowait(taddr + c + 32, v0);
+    const uint4 w1 = requant16_tab<Q>(v1, tab, NOFF + c + 16, p.lo4, p.hi4);
+    if constexpr (BN > 128) {
       if (valid) *reinterpret_cast<uint4*>(orow + c + 16) = w1;
+    } else {
+      if (valid) st_global_v8(orow + c, w0, w1);
     }
   }
 }
@@ -661,7 +669,7 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   }
   const bool is_static = !args.conv4d && fixed_n && args.tiles_n <= 4 &&
                          args.N == args.tiles_n * BN && args.ldo == args.N &&
-                         (reinterpret_cast<uintptr_t>(args.out) & 15u) == 0;
+                         (reinterpret_cast<uintptr_t>(args.out) & 31u) == 0;
   if (!is_static) {
     if (args.ep & kEpFloor)
       return launch_variant<BN, BK, MT, kEpiTable, kEpFloor>(ma, mb, args, *table, grid, smem, s);

@@ -82,7 +82,8 @@ int forward_chunk(pspml_model* m, const int8_t* in, int8_t* out, int64_t mb, cud
   for (size_t i = 0; i < m->ops.size(); ++i) {
     const ModelOp& op = m->ops[i];
     const int8_t* src = i == 0 ? in : ptrs[i - 1];
-    if (op.fuse == 1 && aligned(src) && aligned(ptrs[i + 1])) {
+    // The fused kernels store 32-byte words.
+    if (op.fuse == 1 && aligned(src) && (reinterpret_cast<uintptr_t>(ptrs[i + 1]) & 31u) == 0) {
       // Depthwise + pointwise in one kernel; the pair's time is the
       // depthwise op's, the pointwise op records none.
       const ModelOp& pw = m->ops[i + 1];

@@ -25,6 +25,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// 32-byte global store (sm_100): a lane writes one whole 32-byte sector,
+// so row-per-lane epilogues issue half the store instructions and L2 gets
+// full-sector writes.  `p` must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, const uint4 a, const uint4 b) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a.x),
+               "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w));
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

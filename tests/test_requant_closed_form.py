@@ -68,3 +68,54 @@ def test_predecremented_form_matches_tflite_definition():
         zp = rng.randint(-128, 127)
         a = rng.choice(edges) if it % 4 == 0 else rng.randint(-(1 << 31), (1 << 31) - 1)
         assert closed_form_predecremented(a, m, r, zp) == orc.mbqm(a, m, -r) + zp, (a, m, r, zp)
+
+
+def _clamp(v: int, lo: int, hi: int) -> int:
+    return max(lo, min(hi, v))
+
+
+def floor_form_folded(acc: int, bias: int, m: int, r: int, zp: int) -> int:
+    """The floor form with the bias folded into the 64-bit addend, as the
+    constant tables hold it (floor_entry in kernels.h): D = bias*M + C,
+    out + zp = hi(acc*M + D) >> (r - 1)."""
+    c = (1 << 30) + (1 << (30 + r)) + zp * (1 << (31 + r))
+    d = bias * m + c
+    t = acc * m + d
+    return (t >> 32) >> (r - 1)
+
+
+def test_floor_form_matches_tflite_after_the_clamp():
+    """For ops clamped at or above their output zero point the sign term of
+    the fast form can be dropped: both results clamp to the same byte."""
+    rng = random.Random(3)
+    for it in range(80000):
+        m = rng.choice([1 << 30, (1 << 31) - 1, rng.randint(1 << 30, (1 << 31) - 1)])
+        r = rng.randint(2, 23)
+        zp = rng.randint(-128, 127)
+        act_min = rng.randint(zp, 127)            # act_min >= zp_out (ReLU-like)
+        act_max = rng.randint(act_min, 127)
+        bias = rng.randint(-(1 << 21), 1 << 21)
+        if it % 4 == 0:
+            acc = -bias + rng.randint(-4, 4)       # a = acc + bias near zero
+        else:
+            acc = rng.randint(-(1 << 22), 1 << 22)
+        a = acc + bias
+        want = _clamp(_clamp(orc.mbqm(a, m, -r) + zp, -128, 127), act_min, act_max)
+        got = _clamp(_clamp(floor_form_folded(acc, bias, m, r, zp), -128, 127), act_min, act_max)
+        assert got == want, (acc, bias, m, r, zp, act_min, act_max)
+
+
+def test_floor_form_differs_without_the_clamp():
+    """Without a clamp at the zero point the floor form is not TFLite's (the
+    sign term matters for negative accumulators): the kernels use it only
+    when act_min >= zp_out."""
+    rng = random.Random(4)
+    diffs = 0
+    for _ in range(20000):
+        m = rng.randint(1 << 30, (1 << 31) - 1)
+        r = rng.randint(2, 12)
+        zp = rng.randint(-20, 20)
+        a = rng.randint(-(1 << 22), -1)
+        if floor_form_folded(a, 0, m, r, zp) != orc.mbqm(a, m, -r) + zp:
+            diffs += 1
+    assert diffs > 0

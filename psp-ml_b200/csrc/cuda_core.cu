@@ -127,6 +127,17 @@ __global__ void __launch_bounds__(128)
   const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff) + cw);
   const RqChannel q0 = load_rq(rq + 4 * cw), q1 = load_rq(rq + 4 * cw + 1),
                   q2 = load_rq(rq + 4 * cw + 2), q3 = load_rq(rq + 4 * cw + 3);
+  // Floor form with the bias and the rounding one folded into a 64-bit
+  // addend per channel (the same integer as (acc + bias) * M + C + 2^32):
+  // an output is one wide multiply-add and one shift, and the addend sits in
+  // an aligned register pair for the whole strip.
+  int64_t fd[4] = {0, 0, 0, 0};
+  if constexpr (RQ == kRqFloor) {
+    fd[0] = floor_addend(b.x, q0);
+    fd[1] = floor_addend(b.y, q1);
+    fd[2] = floor_addend(b.z, q2);
+    fd[3] = floor_addend(b.w, q3);
+  }
 
   const uint32_t zpw = splat4(g.zp_in);
   const int ix0 = ox0 * S - g.pl;
@@ -202,9 +213,19 @@ __global__ void __launch_bounds__(128)
         a = __dp4a(static_cast<int>(tap(t1[c])), static_cast<int>(wr[1][c]), a);
         acc[c] = __dp4a(static_cast<int>(tap(t2[c])), static_cast<int>(wr[2][c]), a);
       }
-      if (ox0 + p < g.Wo)
-        orow[static_cast<int64_t>(ox0 + p) * cwn] =
-            finish4<RQ>(acc[0], acc[1], acc[2], acc[3], b, q0, q1, q2, q3, g);
+      if (ox0 + p < g.Wo) {
+        uint32_t w;
+        if constexpr (RQ == kRqFloor) {
+          w = pack_sat4(rq_floor_folded(acc[0], q0.m, fd[0], q0.sr),
+                        rq_floor_folded(acc[1], q1.m, fd[1], q1.sr),
+                        rq_floor_folded(acc[2], q2.m, fd[2], q2.sr),
+                        rq_floor_folded(acc[3], q3.m, fd[3], q3.sr));
+          if (g.clamp) w = clamp4(w, g.lo4, g.hi4);
+        } else {
+          w = finish4<RQ>(acc[0], acc[1], acc[2], acc[3], b, q0, q1, q2, q3, g);
+        }
+        orow[static_cast<int64_t>(ox0 + p) * cwn] = w;
+      }
     }
     if (S == 1) {
 #pragma unroll
@@ -436,7 +457,10 @@ __global__ void __launch_bounds__(128)
   const int px = (threadIdx.x >> 5) * 32 + (lane >> 2) * 4;  // first pixel within the block
   const int ox0 = blockIdx.x * 128 + px;
   uint32_t w[8][3];
-  int32_t m[8], sr[8], cl[8], ch[8], bias[8];
+  // The 64-bit addend of each channel is held as one int64 (an aligned
+  // register pair) so the wide multiply-add of an output needs no moves.
+  int32_t m[8], sr[8], bias[8];
+  int64_t cd[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int co = cg * 8 + k;
@@ -446,15 +470,11 @@ __global__ void __launch_bounds__(128)
     const int2 bs = tab.bs[co];
     m[k] = mh.x;
     sr[k] = bs.y;
-    if constexpr ((Q & kEpFloor) != 0) {
-      cl[k] = bs.x;  // low word of D (bias folded in)
-      ch[k] = mh.y;
-      bias[k] = 0;
-    } else {
-      cl[k] = 0x40000000;  // low word of C - 2^32
-      ch[k] = mh.y;
-      bias[k] = bs.x;
-    }
+    // Floor form: D with the bias folded in ({mh.y, bs.x}); fast form: C - 2^32
+    // ({mh.y, 2^30}) and the bias added to the accumulator.
+    const uint32_t lo = (Q & kEpFloor) != 0 ? static_cast<uint32_t>(bs.x) : 0x40000000u;
+    cd[k] = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(mh.y)) << 32) | lo);
+    bias[k] = (Q & kEpFloor) != 0 ? 0 : bs.x;
   }
   __syncthreads();
   if (ox0 >= g.Wo) return;
@@ -494,9 +514,7 @@ __global__ void __launch_bounds__(128)
         int32_t acc = __dp4a(static_cast<int>(p0), static_cast<int>(w[k][0]), 0);
         acc = __dp4a(static_cast<int>(p1), static_cast<int>(w[k][1]), acc);
         acc = __dp4a(static_cast<int>(p2), static_cast<int>(w[k][2]), acc);
-        const int64_t c = static_cast<int64_t>(
-            (static_cast<uint64_t>(static_cast<uint32_t>(ch[k])) << 32) |
-            static_cast<uint32_t>(cl[k]));
+        const int64_t c = cd[k];
         if constexpr ((Q & kEpFloor) != 0) {
           const int64_t t = static_cast<int64_t>(acc) * m[k] + c;
           r[k] = static_cast<int32_t>(t >> 32) >> sr[k];

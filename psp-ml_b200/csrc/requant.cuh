@@ -105,6 +105,20 @@ __device__ __forceinline__ int32_t rq_fast_floor(int32_t a, const RqChannel& q) 
   return (static_cast<int32_t>(t >> 32) + 1) >> q.sr;
 }
 
+// Floor form with the bias folded in: for an accumulator `acc` whose bias is
+// `bias`, (acc + bias) * M + C + 2^32 = acc * M + D with D returned here, so
+// rq_floor_folded(acc, q.m, D, q.sr) == rq_fast_floor(acc + bias, q) for
+// every int32 acc (the same 64-bit integer, formed in another order).
+__device__ __forceinline__ int64_t floor_addend(int32_t bias, const RqChannel& q) {
+  const int64_t c =
+      static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(q.c_hi)) << 32) | q.c_lo);
+  return static_cast<int64_t>(bias) * q.m + c + (int64_t{1} << 32);
+}
+__device__ __forceinline__ int32_t rq_floor_folded(int32_t acc, int32_t m, int64_t d,
+                                                   int32_t sr) {
+  return static_cast<int32_t>((static_cast<int64_t>(acc) * m + d) >> 32) >> sr;
+}
+
 // requantised value + zp_out, before clamping; any channel.
 __device__ __forceinline__ int32_t rq_apply(int32_t a, const RqChannel& q) {
   if (q.sr >= 0) return rq_fast(a, q);

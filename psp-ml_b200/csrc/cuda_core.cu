@@ -468,13 +468,19 @@ __global__ void __launch_bounds__(128)
     for (int j = 0; j < 3; ++j) w[k][j] = tab.w[co][j];
     const int2 mh = tab.mh[co];
     const int2 bs = tab.bs[co];
-    m[k] = mh.x;
     sr[k] = bs.y;
-    // Floor form: D with the bias folded in ({mh.y, bs.x}); fast form: C - 2^32
-    // ({mh.y, 2^30}) and the bias added to the accumulator.
-    const uint32_t lo = (Q & kEpFloor) != 0 ? static_cast<uint32_t>(bs.x) : 0x40000000u;
-    cd[k] = static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(mh.y)) << 32) | lo);
-    bias[k] = (Q & kEpFloor) != 0 ? 0 : bs.x;
+    if constexpr ((Q & kEpFloor) != 0) {
+      // D with the bias folded in (floor_entry).
+      m[k] = bs.x;
+      cd[k] = floor_d(mh);
+      bias[k] = 0;
+    } else {
+      // C - 2^32 ({2^30, high word}); the bias goes onto the accumulator.
+      m[k] = mh.x;
+      cd[k] = static_cast<int64_t>(
+          (static_cast<uint64_t>(static_cast<uint32_t>(mh.y)) << 32) | 0x40000000u);
+      bias[k] = bs.x;
+    }
   }
   __syncthreads();
   if (ox0 >= g.Wo) return;

@@ -177,12 +177,7 @@ __device__ __forceinline__ uint4 rs_requant16(const uint32_t* v, const int2* mh,
     for (int k = 0; k < 4; ++k) {
       const int c = ch + 4 * g + k;
       if constexpr ((Q & kEpFloor) != 0) {
-        const int2 b = bs[c];
-        const int2 h = mh[c];
-        const int64_t t = static_cast<int64_t>(static_cast<int32_t>(v[4 * g + k])) * h.x +
-                          static_cast<int64_t>((static_cast<uint64_t>(static_cast<uint32_t>(h.y)) << 32) |
-                                               static_cast<uint32_t>(b.x));
-        r[k] = static_cast<int32_t>(t >> 32) >> b.y;
+        r[k] = rq_floor_entry(v[4 * g + k], mh[c], bs[c]);
       } else {
         const int2 b = bs[c];
         r[k] = rq_tab(static_cast<int32_t>(v[4 * g + k]) + b.x, mh[c], b.y);

@@ -149,10 +149,13 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU oracle
-def oracle_rate(net, descs, blob, target_s=12.0, probe=4):
+def oracle_rate(net, descs, blob, target_s=15.0, probe=4):
     """Oracle inferences/s on all host cores over a bounded sample."""
     from oracle import oracle as orc
     threads = host_threads()
+    # The probe keeps every thread busy (OpenMP splits the batch), so its
+    # rate predicts the sample's and the sample lasts about target_s.
+    probe = max(probe, 2 * threads)
     x = net.make_input(probe, tag="cpu-probe")
     t0 = time.perf_counter()
     orc.net_forward_s8(descs, blob, x, threads=threads)

@@ -143,30 +143,39 @@ __device__ __forceinline__ TileOrigin tile_origin(const TcGemmArgs& p, uint32_t 
 
 // Requantises 32 accumulators of one output row and stores them.  bias / rq
 // point into shared memory when the tables are staged there, else global.
+// Sixteen requantised, clamped outputs of channels bias[0..15] / rq[0..15]
+// as four packed words.
+template <bool FAST>
+__device__ __forceinline__ void requant_chunk16(const uint32_t (&v)[16], const int32_t* bias,
+                                                const RqChannel* rq, const TcGemmArgs& p,
+                                                uint32_t (&packed)[4]) {
+  const bool bvec = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    int4 b4;
+    if (bvec) {
+      b4 = reinterpret_cast<const int4*>(bias)[g];
+    } else {
+      b4 = make_int4(bias[4 * g], bias[4 * g + 1], bias[4 * g + 2], bias[4 * g + 3]);
+    }
+    const RqChannel q0 = rq[4 * g], q1 = rq[4 * g + 1], q2 = rq[4 * g + 2], q3 = rq[4 * g + 3];
+    const int32_t r0 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 0]) + b4.x, q0);
+    const int32_t r1 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 1]) + b4.y, q1);
+    const int32_t r2 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 2]) + b4.z, q2);
+    const int32_t r3 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 3]) + b4.w, q3);
+    uint32_t w = pack_sat4(r0, r1, r2, r3);
+    if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
+    packed[g] = w;
+  }
+}
+
 template <bool FAST>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int8_t* dst,
                                                const int32_t* bias, const RqChannel* rq, int cnt,
                                                const TcGemmArgs& p) {
   if (cnt == 16) {
-    const bool bvec = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
     uint32_t packed[4];
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      int4 b4;
-      if (bvec) {
-        b4 = reinterpret_cast<const int4*>(bias)[g];
-      } else {
-        b4 = make_int4(bias[4 * g], bias[4 * g + 1], bias[4 * g + 2], bias[4 * g + 3]);
-      }
-      const RqChannel q0 = rq[4 * g], q1 = rq[4 * g + 1], q2 = rq[4 * g + 2], q3 = rq[4 * g + 3];
-      const int32_t r0 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 0]) + b4.x, q0);
-      const int32_t r1 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 1]) + b4.y, q1);
-      const int32_t r2 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 2]) + b4.z, q2);
-      const int32_t r3 = rq_sel<FAST>(static_cast<int32_t>(v[4 * g + 3]) + b4.w, q3);
-      uint32_t w = pack_sat4(r0, r1, r2, r3);
-      if (p.clamp) w = clamp4(w, p.lo4, p.hi4);
-      packed[g] = w;
-    }
+    requant_chunk16<FAST>(v, bias, rq, p, packed);
     if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
       *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     } else if ((reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
@@ -560,6 +569,55 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
           orow = p.out + r * p.ldo;
         }
         const int32_t n0 = tn * BN;
+        // (256-column tiles only: the tile the host picks for odd N > 256
+        // without a constant table; narrower variants keep their registers.)
+        if constexpr (MODE == kEpiGeneral && BN == 256)
+        if (!p.conv4d && (p.ldo & 3) != 0 && n0 + BN <= p.N) {
+          // Rows whose starts are not 4-byte aligned (an odd row length such
+          // as 3337 logits), full N tile: this thread writes the row segment
+          // [n0, n0 + BN) in order, so each 16-byte chunk leaves as four
+          // 4-byte-aligned words, funnel-shifted against the previous
+          // chunk's last word; only the s = start % 4 head and tail bytes
+          // are single-byte stores.  (Sixteen byte stores per chunk, each
+          // touching 32 rows, had made this epilogue store-bound.)
+          int8_t* d0 = orow + n0;
+          const uint32_t sa = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(d0) & 3u);
+          uint32_t* aw = reinterpret_cast<uint32_t*>(d0 - sa);
+          const uint32_t sh = 8u * (4u - sa);
+          uint32_t carry = 0;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t v[16];
+            tmem_ld16(tb + static_cast<uint32_t>(c), v);
+            if (valid) {
+              uint32_t w[4];
+              if (fast)
+                requant_chunk16<true>(v, brow + n0 + c, rqb + n0 + c, p, w);
+              else
+                requant_chunk16<false>(v, brow + n0 + c, rqb + n0 + c, p, w);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int j = c / 4 + k;  // aligned word: segment bytes 4j - sa .. 4j + 3 - sa
+                if (j == 0 && sa != 0) {
+#pragma unroll
+                  for (int t = 0; t < 3; ++t)
+                    if (t < static_cast<int>(4u - sa)) d0[t] = static_cast<int8_t>(w[0] >> (8 * t));
+                } else {
+                  aw[j] = __funnelshift_rc(carry, w[k], sh);
+                }
+                carry = w[k];
+              }
+            }
+          }
+          if (valid && sa != 0) {
+#pragma unroll
+            for (int t = 0; t < 3; ++t)
+              if (t < static_cast<int>(sa))
+                d0[BN - static_cast<int>(sa) + t] =
+                    static_cast<int8_t>(carry >> (8 * (4 - static_cast<int>(sa) + t)));
+          }
+          continue;
+        }
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
           uint32_t v[16];

@@ -20,7 +20,10 @@ def _check(ctx, oracle_mod, d, batch, x, w=None, b=None, m=None, s=None):
 # ------------------------------------------------------------------ FC (tcgen05)
 @pytest.mark.parametrize("B,K,N", [
     (1, 512, 512), (7, 784, 10), (130, 256, 100), (257, 512, 3337), (64, 2048, 2048),
-    (3, 96, 33), (129, 64, 256), (300, 32, 48), (2, 8192, 40)])
+    (3, 96, 33), (129, 64, 256), (300, 32, 48), (2, 8192, 40),
+    # Row lengths of every residue mod 4 above one 256-column tile (rows
+    # not 4-byte aligned take the carried-word store path).
+    (300, 64, 1002), (129, 128, 515)])
 @pytest.mark.parametrize("mode", ["calibrated", "extreme"])
 def test_fc_tensor_core(ctx, oracle_mod, B, K, N, mode):
     r = np.random.default_rng(B * 7 + K + N)

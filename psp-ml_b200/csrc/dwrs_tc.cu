@@ -134,7 +134,7 @@ struct RsShape {
   static_assert(CG * R * 32 + NPW <= kSlotCols, "tensor memory per slot");
   static constexpr int kBdw = CG * 3 * kTap;           // resident weights of one block
   static_assert(NCB == 1 || NPW == 0, "channel blocks are for the depthwise conv alone");
-  static_assert(NCB == 1 || NCB == 2 || NCB == 4, "channel blocks");
+  static_assert(NCB == 1 || NCB == 2 || NCB == 4 || NCB == 8, "channel blocks");
   static_assert(P == 1 || P == 2 || P == 4, "packed samples");
   static_assert(P == 1 || (NPW == 0 && S == 1),
                 "packed samples are for a stride-1 depthwise conv alone");
@@ -701,12 +701,26 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
         rs_epilogue<CG, NPW, S, NCB, P, 1, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
                                                           lane, abort_flag);
       } else if constexpr (NCB >= 4) {
-        if (cb == 2)
+        if (cb == 2) {
           rs_epilogue<CG, NPW, S, NCB, P, 2, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
-        else
+        } else if (cb == 3) {
           rs_epilogue<CG, NPW, S, NCB, P, 3, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
+        } else if constexpr (NCB >= 8) {
+          if (cb == 4)
+            rs_epilogue<CG, NPW, S, NCB, P, 4, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+                                                              lane, abort_flag);
+          else if (cb == 5)
+            rs_epilogue<CG, NPW, S, NCB, P, 5, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+                                                              lane, abort_flag);
+          else if (cb == 6)
+            rs_epilogue<CG, NPW, S, NCB, P, 6, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+                                                              lane, abort_flag);
+          else
+            rs_epilogue<CG, NPW, S, NCB, P, 7, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+                                                              lane, abort_flag);
+        }
       }
     }
   }
@@ -788,7 +802,8 @@ cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, int d
 
 // Shapes the kernel takes: 3x3 depthwise, stride 1 or 2 (square), at most
 // one row/column of top/left padding, 64 or more output pixels per row; C
-// in {32, 64} or a multiple of 64 up to 256 (channel blocks); stride 2
+// in {32, 64} or a multiple of 64 up to 256 (channel blocks), or 512 for
+// stride-1 rows of at most 32 pixels (four samples per tile); stride 2
 // needs an even input width (the even/odd pixel view).
 bool rs_geometry_ok(const pspml_op_desc& d) {
   if (d.kind != PSPML_OP_DEPTHWISE_CONV2D || d.kernel_h != 3 || d.kernel_w != 3 ||
@@ -803,7 +818,10 @@ bool rs_geometry_ok(const pspml_op_desc& d) {
   if (S == 2 && (d.in_w % 2 != 0)) return false;
   if (d.out_w < 1 || d.out_w > 65535 || d.out_h > 4096 || d.in_h > 65535) return false;
   const int C = d.in_c;
-  if (!(C == 32 || C == 64 || C == 128 || C == 256)) return false;
+  if (!(C == 32 || C == 64 || C == 128 || C == 256 || C == 512)) return false;
+  // 512 channels (eight blocks) only with four samples per tile: stride 1,
+  // rows of at most 32 pixels.
+  if (C == 512 && (S != 1 || d.out_w > 32)) return false;
   // Every output row takes at least one input row: S*r - pad_top + 2 >= 0
   // and S*(out_h-1) - pad_top <= in_h - 1.
   if (S * (d.out_h - 1) - d.pad_top > d.in_h - 1) return false;
@@ -899,6 +917,7 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
       if (C == 64) return rs_shape<2, 0, 1, 1, 4>(m, a, tab, dwq, 0, num_sms, s);
       if (C == 128) return rs_shape<2, 0, 1, 2, 4>(m, a, tab, dwq, 0, num_sms, s);
       if (C == 256) return rs_shape<2, 0, 1, 4, 4>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 512) return rs_shape<2, 0, 1, 8, 4>(m, a, tab, dwq, 0, num_sms, s);
     }
   }
   return cudaErrorInvalidValue;

@@ -50,7 +50,7 @@ bool build_border_classes(const pspml_op_desc& d, BorderClasses* bc);
 // fixed, the table offsets are compile-time constants and the epilogue reads
 // the entries as constant-bank operands with no load instruction at all.
 constexpr int kTabRq = 512;
-constexpr int kTabDelta = 4096;
+constexpr int kTabDelta = 4608;  // 9 border classes x 512 channels
 struct EpiTable {
   // Fast form: mh = {M, high word of C - 2^32}, bs = {folded bias of class
   // base_cls, right shift - 1}; floor form (floor_entry): the bias folded
@@ -164,7 +164,7 @@ __device__ __forceinline__ void add_class_delta(uint32_t* v, const EpiTable& tab
 // (dwpw_tc.cu, dwrs_tc.cu): the depthwise op's split constants and
 // per-class bias differences (up to 9 border classes x 256 channels), the
 // pointwise op's split constants.
-constexpr int kDwTabC = 256;
+constexpr int kDwTabC = 512;
 struct DwPwTable {
   int2 dw_mh[kDwTabC];
   int2 dw_bs[kDwTabC];

@@ -56,6 +56,8 @@ def test_depthwise_static_table(ctx, oracle_mod, B, H, W, C, zp_in, act):
     (2, 12, 64, 256, 2, None, -128, (-128, 127)),        # stride 2, 32-px rows (CUDA cores)
     (3, 7, 50, 64, 1, None, 3, (-30, 100)),              # 50-px rows, clamp
     (2, 9, 40, 64, 2, (1, 1, 1, 1), -2, (-128, 127)),    # stride 2 top/left pad, narrow
+    (6, 6, 32, 512, 1, None, -128, (-128, 127)),         # eight channel blocks, four per tile
+    (3, 6, 24, 512, 1, None, 3, (-20, 110)),             # eight blocks, 24-px rows, clamp
 ])
 def test_depthwise_row_streaming_shapes(ctx, oracle_mod, B, H, W, C, stride, pads, zp_in, act):
     """Depthwise shapes of the row-streaming tensor-core kernel beyond the
@@ -171,6 +173,7 @@ FLOOR_CASES = [
     ("row-streaming s1", 2, [_dw(5, 256, 64, 1, 3, -128, (-128, 127))]),
     ("row-streaming s2 blocks, clamp", 2, [_dw(8, 256, 128, 2, -128, 10, (10, 127))]),
     ("row-streaming packed rows", 3, [_dw(5, 32, 256, 1, -128, -128, (-128, 127))]),
+    ("row-streaming 512 channels", 5, [_dw(6, 32, 512, 1, 2, -128, (-128, 127))]),
     ("cuda-core dw s2, clamp", 2, [_dw(6, 128, 128, 2, 0, -6, (-6, 127))]),
     ("cuda-core dw s1, 36 channels", 2, [_dw(5, 40, 36, 1, 2, -128, (-128, 120))]),
     ("gemm static 128", 2, [_pw(6, 40, 64, 128, -128, -128, (-128, 127))]),

@@ -952,7 +952,8 @@ bool dwrs_dw_supported(const pspml_op_desc& d) {
 }
 
 // The 32-channel pair measured faster on the tile-per-row kernel
-// (dwpw_tc.cu, 141 against 164 ms per config-4 step): with half the
+// (dwpw_tc.cu, 141 against 164 ms per config-4 step, and 129 against 150
+// with the later epilogues): with half the
 // depthwise channels a row carries less work and this kernel's per-row
 // chain (MMA, commit, block release) sets the pace, while that kernel
 // keeps four independent tiles in flight.

@@ -136,7 +136,8 @@ def test_maxpool(ctx, oracle_mod, B, H, W, C, act):
     _check(ctx, oracle_mod, d, B, x)
 
 
-@pytest.mark.parametrize("B,H,W,C", [(5, 6, 32, 512), (7, 4, 4, 256), (3, 3, 5, 7)])
+@pytest.mark.parametrize("B,H,W,C", [(5, 6, 32, 512), (7, 4, 4, 256), (3, 3, 5, 7), (4, 5, 3, 12),
+                                     (2, 7, 9, 48)])
 def test_global_avgpool(ctx, oracle_mod, B, H, W, C):
     r = np.random.default_rng(H * W + C)
     d = make_desc(kind=capi.OP_AVERAGE_POOL2D, in_h=H, in_w=W, in_c=C, out_h=1, out_w=1,

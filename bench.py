@@ -2,7 +2,8 @@
 """Benchmark: int8 inferences/sec of the psp-ml inference path on B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg4]
-                    [--impl ours|reference]
+                    [--impl ours|reference] [--batch B] [--point B,K]
+                    [--no-extras] [--no-e2e] [--no-cpu-baseline]
 
 One process per GPU (torchrun for N > 1).  Default workload: config 4 =
 config 3's depthwise-separable network ([96,512,1] int8 input, 3337 logits)
@@ -13,11 +14,16 @@ the rank's whole slice, micro-batched on the device.
 value    inferences/s of the whole job with inputs resident in HBM, from CUDA
          events around K steps, max over ranks.
 e2e      the same through pspml_forward with pinned host buffers: every step
-         copies its inputs in and its logits out.
+         copies its inputs in and its logits out; K steps between barriers,
+         max over ranks.
 roofline the dominant kernel's algorithmic bytes (or ops) per launch over its
          event-timed duration inside the timed region.
 cpu_baseline  the CPU oracle (int8 TFLite semantics, OpenMP) on a bounded
          sample, rank 0 at N=1 only.
+configs  (N = 1) the other benchmark configurations, each measured on its own
+         in the same run: config 0 (small CNN, batch 65536), config 2 (deep
+         CNN, batch 8192) and the nine points of config 1's FC sweep, each
+         with inferences/s, a per-layer roofline table and a CPU-oracle rate.
 
 --impl reference times the reference's CPU path on the host cores instead
 (the reference is Rust with no int8 kernels and cannot be built here, so its
@@ -47,6 +53,9 @@ from pspml import capi, netspec, shard  # noqa: E402
 METRIC = "int8 inferences/sec"
 UNIT = "inferences/s"
 
+# Config 1: one FullyConnected [B,K] x [K,K]^T per point.
+CFG1_POINTS = [(b, k) for b in (1, 256, 16384) for k in (512, 2048, 8192)]
+
 WORKLOADS = {
     # name: (config network, batch, batch kind, micro-batch)
     "cfg4": dict(cfg=3, batch=262144, kind="global", micro=8192,
@@ -56,9 +65,15 @@ WORKLOADS = {
                  desc="config 3: depthwise-separable CNN, batch 2048 per GPU"),
     "cfg2": dict(cfg=2, batch=8192, kind="per_gpu", micro=8192,
                  desc="config 2: 64x64x3 4-stage CNN, batch 8192 per GPU"),
+    "cfg1": dict(cfg=1, batch=16384, kind="per_gpu", micro=16384,
+                 desc="config 1: one int8 FullyConnected [B,K] x [K,K]^T, input zp -3, "
+                      "output zp 5 + ReLU"),
     "cfg0": dict(cfg=0, batch=65536, kind="per_gpu", micro=65536,
                  desc="config 0: 28x28x1 small CNN, batch 65536 per GPU"),
 }
+
+# Working sets below this are flushed from L2 (126 MB) before every step.
+L2_FLUSH_BYTES = 256 << 20
 
 
 def peaks():
@@ -67,6 +82,13 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), 2.0 * float(d["bf16_tflops"]), "measured"
     return 6650.0, 2.0 * 1590.0, "fallback"
+
+
+def build_net(cfg: int, point=None):
+    if cfg == 1:
+        b, k = point
+        return netspec.build_fc_sweep(b, k)
+    return netspec.BUILDERS[cfg]()
 
 
 # ------------------------------------------------------------ layer model
@@ -90,15 +112,61 @@ def layer_model(net, fused=None):
         if fused[i] == 1 and i + 1 < len(net.layers):
             nxt = net.layers[i + 1]
             a, b = out[i], out[i + 1]
-            a["name"] = f"{l.name}+pw"
+            suffix = "pool" if nxt.kind == capi.OP_MAX_POOL2D else "pw"
+            a["name"] = f"{l.name}+{suffix}"
             a["bytes_per_sample"] = int(np.prod(l.in_shape)) + int(np.prod(nxt.out_shape))
             a["weight_bytes"] += b["weight_bytes"]
             a["ops_per_sample"] += b["ops_per_sample"]
-            a["tensor"] = True
+            a["tensor"] = a["tensor"] or b["tensor"] or nxt.kind == capi.OP_CONV2D
             b["launches_per_chunk"] = 0
             b["bytes_per_sample"] = 0
             b["ops_per_sample"] = 0
     return out
+
+
+def layer_table(ops, op_ms, steps, chunks, n_local):
+    """Per-launch roofline of every op from its event-timed milliseconds
+    (summed over `steps` steps of `chunks` micro-batches each)."""
+    hbm_gbs, int8_tops, _ = peaks()
+    ridge = int8_tops * 1e12 / (hbm_gbs * 1e9)
+    layers = []
+    for o, ms in zip(ops, op_ms):
+        if o["launches_per_chunk"] == 0:
+            continue
+        launches = steps * chunks
+        avg_ms = max(ms / launches, 1e-6)
+        per_launch_samples = n_local / chunks
+        byts = o["bytes_per_sample"] * per_launch_samples + o["weight_bytes"]
+        flops = o["ops_per_sample"] * per_launch_samples
+        gbs = byts / (avg_ms * 1e-3) / 1e9
+        tops = flops / (avg_ms * 1e-3) / 1e12
+        tensor_bound = o["tensor"] and flops / max(byts, 1) > ridge
+        t_roof = max(flops / (int8_tops * 1e12), byts / (hbm_gbs * 1e9))
+        layers.append(dict(name=o["name"], ms_per_step=round(ms / steps, 4),
+                           share=None, bound="tensor" if tensor_bound else "hbm",
+                           gbs=round(gbs, 1), tops=round(tops, 2),
+                           frac=round(t_roof / (avg_ms * 1e-3), 4),
+                           bytes_per_launch=int(byts), ops_per_launch=int(flops),
+                           avg_launch_ms=round(avg_ms, 4)))
+    tot = sum(l["ms_per_step"] for l in layers) or 1.0
+    for l in layers:
+        l["share"] = round(l["ms_per_step"] / tot, 4)
+    return layers
+
+
+def roofline_of(layer, traffic=None):
+    """The roofline object of one layer-table entry."""
+    hbm_gbs, int8_tops, peak_src = peaks()
+    if layer["bound"] == "tensor":
+        roof = {"bound": "tensor", "achieved": layer["tops"], "peak": round(int8_tops, 1),
+                "unit": "TOPS", "frac": round(layer["tops"] / int8_tops, 4), "traffic": traffic}
+    else:
+        roof = {"bound": "hbm", "achieved": layer["gbs"], "peak": hbm_gbs, "unit": "GB/s",
+                "frac": round(layer["gbs"] / hbm_gbs, 4), "traffic": traffic}
+    roof["kernel"] = layer["name"]
+    roof["peak_source"] = (f"{peak_src}: HBM = MEASURED_PEAKS hbm_gbs; int8 tensor = 2 x "
+                           "bf16_tflops (no int8 measurement)")
+    return roof
 
 
 # ---------------------------------------------------------------- clocks
@@ -149,18 +217,18 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU oracle
-def oracle_rate(net, descs, blob, target_s=15.0, probe=4):
+def oracle_rate(net, descs, blob, target_s=15.0, probe=4, max_n=4096):
     """Oracle inferences/s on all host cores over a bounded sample."""
     from oracle import oracle as orc
     threads = host_threads()
     # The probe keeps every thread busy (OpenMP splits the batch), so its
     # rate predicts the sample's and the sample lasts about target_s.
-    probe = max(probe, 2 * threads)
+    probe = min(max(probe, 2 * threads), max_n)
     x = net.make_input(probe, tag="cpu-probe")
     t0 = time.perf_counter()
     orc.net_forward_s8(descs, blob, x, threads=threads)
     dt = max(time.perf_counter() - t0, 1e-6)
-    n = int(min(4096, max(probe, target_s * probe / dt)))
+    n = int(min(max_n, max(probe, target_s * probe / dt)))
     x = net.make_input(n, tag="cpu-sample")
     t0 = time.perf_counter()
     orc.net_forward_s8(descs, blob, x, threads=threads)
@@ -177,11 +245,19 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def parse_point(s):
+    b, k = (int(v) for v in s.split(","))
+    if (b, k) not in CFG1_POINTS:
+        raise SystemExit(f"--point {s}: not one of config 1's points {CFG1_POINTS}")
+    return b, k
+
+
 # ------------------------------------------------------------- reference arm
 def run_reference(args, wl, rank, world):
     if rank != 0:
         return
-    net = netspec.BUILDERS[wl["cfg"]]()
+    point = parse_point(args.point) if wl["cfg"] == 1 else None
+    net = build_net(wl["cfg"], point or (256, 2048))
     descs, blob = net.descs_and_blob()
     from oracle import oracle as orc
     orc.lib()
@@ -216,10 +292,121 @@ def run_reference(args, wl, rank, world):
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if point is not None:
+        line["config"]["point"] = {"B": point[0], "K": point[1]}
     emit(line)
 
 
 # ------------------------------------------------------------------ our arm
+def device_input(net, n, dev, seed):
+    """Seeded synthetic inputs generated on the device with the network's
+    input distribution (as Network.make_input), resident in HBM."""
+    import torch
+    in_e = net.in_elems
+    x = torch.empty(max(1, n) * in_e, dtype=torch.int8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    chunk = max(1, (1 << 27) // in_e)
+    for b0 in range(0, n, chunk):
+        b1 = min(n, b0 + chunk)
+        m = (b1 - b0) * in_e
+        if net.input_kind == "gaussian_spectrogram":
+            v = torch.randn(m, generator=gen, device=dev) * 25.0 - 40.0
+            v = v.round().clamp_(-128, 127)
+        elif net.input_kind == "uniform_int8":
+            v = torch.randint(-128, 128, (m,), generator=gen, device=dev).float()
+        else:
+            v = torch.randint(0, 256, (m,), generator=gen, device=dev).float() - 128.0
+        x[b0 * in_e:b1 * in_e] = v.to(torch.int8)
+        del v
+    return x
+
+
+def measure_net(ctx, net, n_local, micro, steps, warmup, dev, stream, seed, flush_buf=None):
+    """Device-resident forwards of one network: per-op CUDA events over
+    `steps` steps (L2 flushed before each when `flush_buf` is given).
+    Returns the layer table, the step time (sum of the op times) and the
+    rate."""
+    import torch
+    descs, blob = net.descs_and_blob()
+    model = capi.Model(ctx, descs, blob, micro)
+    try:
+        x_dev = device_input(net, n_local, dev, seed)
+        y_dev = torch.empty(max(1, n_local) * net.out_elems, dtype=torch.int8, device=dev)
+        for _ in range(warmup):
+            model.forward_device(x_dev.data_ptr(), y_dev.data_ptr(), n_local, stream)
+        torch.cuda.synchronize()
+        ctx.check_device()
+        op_ms = np.zeros(len(net.layers))
+        for _ in range(steps):
+            if flush_buf is not None:
+                flush_buf.add_(1)
+            op_ms += np.array(model.forward_timed(x_dev.data_ptr(), y_dev.data_ptr(), n_local,
+                                                  stream))
+        torch.cuda.synchronize()
+        ctx.check_device()
+        ops = layer_model(net, [model.op_fused(i) for i in range(len(net.layers))])
+        chunks = -(-n_local // micro)
+        layers = layer_table(ops, op_ms, steps, chunks, n_local)
+        ms = float(op_ms.sum()) / steps
+        launches = steps * chunks * sum(o["launches_per_chunk"] for o in ops)
+        del x_dev, y_dev
+    finally:
+        model.close()
+    return dict(layers=layers, ms_per_step=ms, value=n_local / (ms / 1000.0),
+                gpu_launches=int(launches), descs=descs, blob=blob)
+
+
+def run_extras(args, ctx, dev, stream):
+    """Configs 0, 2 and 1 measured on their own (N = 1): inferences/s, the
+    per-layer roofline table and the dominant kernel, plus a short CPU-oracle
+    rate for each."""
+    import torch
+    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    steps = max(3, min(args.steps, 5))
+    out = {}
+    for name in ("cfg0", "cfg2"):
+        wl = WORKLOADS[name]
+        net = build_net(wl["cfg"])
+        r = measure_net(ctx, net, wl["batch"], wl["micro"], steps, 2, dev, stream, seed=99)
+        dom = max(r["layers"], key=lambda l: l["ms_per_step"])
+        entry = {"value": round(r["value"], 1), "unit": UNIT, "batch": wl["batch"],
+                 "micro_batch": wl["micro"], "steps": steps,
+                 "ms_per_step": round(r["ms_per_step"], 3), "description": wl["desc"],
+                 "l2": "activations larger than L2 (no flush needed)",
+                 "roofline": roofline_of(dom), "layers": r["layers"]}
+        if not args.no_cpu_baseline:
+            rate, n, dt = oracle_rate(net, r["descs"], r["blob"], target_s=3.0)
+            entry["cpu_baseline"] = {"value": round(rate, 3), "unit": UNIT,
+                                     "cores": host_threads(), "kind": "port",
+                                     "sample": f"{n} samples in {dt:.1f} s"}
+        out[name] = entry
+        torch.cuda.empty_cache()
+    points = []
+    for b, k in CFG1_POINTS:
+        net = build_net(1, (b, k))
+        ws = b * k * 2 + k * k
+        r = measure_net(ctx, net, b, b, max(steps, 10), 2, dev, stream, seed=7,
+                        flush_buf=flush if ws < L2_FLUSH_BYTES else None)
+        l = r["layers"][0]
+        p = {"B": b, "K": k, "N": k, "value": round(r["value"], 1), "unit": UNIT,
+             "ms": round(r["ms_per_step"], 5), "bound": l["bound"], "gbs": l["gbs"],
+             "tops": l["tops"], "frac": l["frac"],
+             "l2": "L2 flushed before every step" if ws < L2_FLUSH_BYTES else
+                   "working set larger than L2"}
+        if not args.no_cpu_baseline:
+            rate, n, dt = oracle_rate(net, r["descs"], r["blob"], target_s=1.0, probe=4,
+                                      max_n=b)
+            p["cpu_baseline"] = {"value": round(rate, 3), "unit": UNIT,
+                                 "cores": host_threads(), "kind": "port",
+                                 "sample": f"{n} rows in {dt:.2f} s"}
+        points.append(p)
+        torch.cuda.empty_cache()
+    out["cfg1"] = {"description": WORKLOADS["cfg1"]["desc"], "points": points}
+    del flush
+    return out
+
+
 def run_ours(args, wl, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -238,40 +425,32 @@ def run_ours(args, wl, rank, world, local_rank):
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    net = netspec.BUILDERS[wl["cfg"]]()
+    point = parse_point(args.point) if wl["cfg"] == 1 else None
+    net = build_net(wl["cfg"], point)
     descs, blob = net.descs_and_blob()
-    if wl["kind"] == "global":
-        start, stop = shard.slice_for(wl["batch"], world, rank)
-        global_batch = wl["batch"]
+    if wl["cfg"] == 1:
+        start, stop = 0, point[0]
+        global_batch = point[0] * world
+    elif wl["kind"] == "global":
+        start, stop = shard.slice_for(args.batch or wl["batch"], world, rank)
+        global_batch = args.batch or wl["batch"]
     else:
-        start, stop = 0, wl["batch"]
-        global_batch = wl["batch"] * world
+        start, stop = 0, args.batch or wl["batch"]
+        global_batch = (args.batch or wl["batch"]) * world
     n_local = stop - start
-    micro = min(args.micro or wl["micro"], max(1, n_local))
+    micro = min(args.micro or (n_local if wl["cfg"] == 1 else wl["micro"]), max(1, n_local))
 
     ctx = capi.Context(local_rank)
     ctx.set_timeout_ms(600_000)
     model = capi.Model(ctx, descs, blob, micro)
     stream = torch.cuda.current_stream().cuda_stream
 
-    # Synthetic inputs generated on the device (same distributions as
-    # Network.make_input), resident in HBM; far larger than the 126 MB L2.
     in_e, out_e = net.in_elems, net.out_elems
-    x_dev = torch.empty(n_local * in_e, dtype=torch.int8, device=dev)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
-    chunk = 4096
-    for b0 in range(0, n_local, chunk):
-        b1 = min(n_local, b0 + chunk)
-        n = (b1 - b0) * in_e
-        if net.input_kind == "gaussian_spectrogram":
-            v = torch.randn(n, generator=gen, device=dev) * 25.0 - 40.0
-            v = v.round().clamp_(-128, 127)
-        else:
-            v = torch.randint(0, 256, (n,), generator=gen, device=dev).float() - 128.0
-        x_dev[b0 * in_e:b1 * in_e] = v.to(torch.int8)
-        del v
+    x_dev = device_input(net, n_local, dev, 1234 + rank)
     y_dev = torch.empty(max(1, n_local) * out_e, dtype=torch.int8, device=dev)
+    ws = n_local * (in_e + out_e) + blob.nbytes
+    flush = (torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+             if ws < L2_FLUSH_BYTES else None)
     torch.cuda.synchronize()
 
     ops = layer_model(net, [model.op_fused(i) for i in range(len(net.layers))])
@@ -283,7 +462,10 @@ def run_ours(args, wl, rank, world, local_rank):
     torch.cuda.synchronize()
     ctx.check_device()
 
-    # ---- timed region: K steps, per-op CUDA events on the launching stream
+    # ---- timed region: K steps, per-op CUDA events on the launching stream.
+    # A working set smaller than L2 is flushed (one 256 MB write) before
+    # every step; the step time is then the sum of the op times, which
+    # leaves the flush out.
     sampler = ClockSampler(local_rank)
     sampler.start()
     time.sleep(0.3)
@@ -294,6 +476,8 @@ def run_ours(args, wl, rank, world, local_rank):
     op_ms = np.zeros(n_ops)
     ev0.record()
     for _ in range(args.steps):
+        if flush is not None:
+            flush.add_(1)
         op_ms += np.array(model.forward_timed(x_dev.data_ptr(), y_dev.data_ptr(), n_local,
                                               stream))
     ev1.record()
@@ -301,35 +485,13 @@ def run_ours(args, wl, rank, world, local_rank):
     barrier()
     clocks = sampler.stop()
     ctx.check_device()
-    step_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    local_ms = (float(op_ms.sum()) if flush is not None else ev0.elapsed_time(ev1)) / args.steps
+    step_ms = max_over_ranks(local_ms)
     value = global_batch / (step_ms / 1000.0)
     gpu_launches = args.steps * chunks * sum(o["launches_per_chunk"] for o in ops)
 
     # ---- roofline of the dominant kernel (largest share of the timed region)
-    hbm_gbs, int8_tops, peak_src = peaks()
-    layers = []
-    for o, ms in zip(ops, op_ms):
-        if o["launches_per_chunk"] == 0:
-            continue
-        launches = args.steps * chunks
-        avg_ms = ms / launches
-        per_launch_samples = n_local / chunks
-        byts = o["bytes_per_sample"] * per_launch_samples + o["weight_bytes"]
-        flops = o["ops_per_sample"] * per_launch_samples
-        gbs = byts / (avg_ms * 1e-3) / 1e9
-        tops = flops / (avg_ms * 1e-3) / 1e12
-        ridge = int8_tops * 1e12 / (hbm_gbs * 1e9)
-        tensor_bound = o["tensor"] and flops / max(byts, 1) > ridge
-        t_roof = max(flops / (int8_tops * 1e12), byts / (hbm_gbs * 1e9))
-        layers.append(dict(name=o["name"], ms_per_step=round(ms / args.steps, 4),
-                           share=None, bound="tensor" if tensor_bound else "hbm",
-                           gbs=round(gbs, 1), tops=round(tops, 2),
-                           frac=round(t_roof / (avg_ms * 1e-3), 4),
-                           bytes_per_launch=int(byts), ops_per_launch=int(flops),
-                           avg_launch_ms=round(avg_ms, 4)))
-    tot = sum(l["ms_per_step"] for l in layers) or 1.0
-    for l in layers:
-        l["share"] = round(l["ms_per_step"] / tot, 4)
+    layers = layer_table(ops, op_ms, args.steps, chunks, n_local)
     dom = max(layers, key=lambda l: l["ms_per_step"])
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
@@ -341,56 +503,68 @@ def run_ours(args, wl, rank, world, local_rank):
                 traffic = int(per_sample * n_local / chunks)
         except Exception:
             traffic = None
-    if dom["bound"] == "tensor":
-        roof = {"bound": "tensor", "achieved": dom["tops"], "peak": round(int8_tops, 1),
-                "unit": "TOPS", "frac": round(dom["tops"] / int8_tops, 4), "traffic": traffic}
-    else:
-        roof = {"bound": "hbm", "achieved": dom["gbs"], "peak": hbm_gbs, "unit": "GB/s",
-                "frac": round(dom["gbs"] / hbm_gbs, 4), "traffic": traffic}
-    roof["kernel"] = dom["name"]
-    roof["peak_source"] = (f"{peak_src}: HBM = MEASURED_PEAKS hbm_gbs; int8 tensor = 2 x "
-                           "bf16_tflops (no int8 measurement)")
+    roof = roofline_of(dom, traffic)
 
-    # ---- end to end: pinned host buffers through pspml_forward
+    # ---- end to end: pinned host buffers through pspml_forward, the same
+    # K steps between barriers, max over ranks.
     e2e = None
     if not args.no_e2e:
-        hin = torch.empty(n_local * in_e, dtype=torch.int8).pin_memory()
+        hin = torch.empty(max(1, n_local) * in_e, dtype=torch.int8).pin_memory()
         hout = torch.empty(max(1, n_local) * out_e, dtype=torch.int8).pin_memory()
         hin.copy_(x_dev)
         torch.cuda.synchronize()
-        e2e_steps = max(1, min(args.steps, 3))
         model.forward(hin.data_ptr(), hout.data_ptr(), n_local)  # warm the pipeline
         barrier()
         t0 = time.perf_counter()
-        for _ in range(e2e_steps):
+        for _ in range(args.steps):
             model.forward(hin.data_ptr(), hout.data_ptr(), n_local)
-        e2e_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps)
+        local_s = (time.perf_counter() - t0) / args.steps
+        barrier()
+        e2e_s = max_over_ranks(local_s)
+        h2d_b = int(n_local * in_e)
         e2e = {"value": round(global_batch / e2e_s, 1), "unit": UNIT,
-               "h2d_bytes_per_step": int(n_local * in_e),
-               "d2h_bytes_per_step": int(n_local * out_e)}
+               "h2d_bytes_per_step": h2d_b, "d2h_bytes_per_step": int(n_local * out_e),
+               "steps": args.steps,
+               "h2d_gbs_all_ranks": round(h2d_b * world / e2e_s / 1e9, 2)}
+        del hin, hout
 
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as orc
         orc.lib()
-        rate, n, dt = oracle_rate(net, descs, blob)
+        rate, n, dt = oracle_rate(net, descs, blob, max_n=4096 if wl["cfg"] != 1 else n_local)
         cpu = {"value": round(rate, 3), "unit": UNIT, "cores": host_threads(), "kind": "port",
                "sample": f"{n} samples of the {args.workload} network in {dt:.1f} s (C oracle "
                          "of TFLite int8 semantics, OpenMP over the batch)"}
 
+    model.close()
+    flushed = flush is not None
+    del x_dev, y_dev, flush
+    torch.cuda.empty_cache()
+
+    # ---- the other configurations (N = 1)
+    extras = None
+    if world == 1 and not args.no_extras:
+        extras = run_extras(args, ctx, dev, stream)
+
     if rank == 0:
+        config = {"workload": args.workload, "description": wl["desc"],
+                  "global_batch": global_batch, "per_rank_batch": n_local,
+                  "micro_batch": micro, "parallelism": f"batch-slice x{world}, no collective",
+                  "l2": ("L2 flushed (256 MB write) before every step; step time = sum of "
+                         "the op times" if flushed else
+                         "inputs larger than L2 (no flush needed)"),
+                  "macs_per_inference": net.macs_per_sample()}
+        if point is not None:
+            config["point"] = {"B": point[0], "K": point[1]}
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
             "higher_is_better": True,
             "scaling": "strong" if wl["kind"] == "global" else "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": args.workload, "description": wl["desc"],
-                       "global_batch": global_batch, "per_rank_batch": n_local,
-                       "micro_batch": micro, "parallelism": f"batch-slice x{world}, no collective",
-                       "l2": "inputs larger than L2 (no flush needed)",
-                       "macs_per_inference": net.macs_per_sample()},
+            "config": config,
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -398,8 +572,9 @@ def run_ours(args, wl, rank, world, local_rank):
             "clocks": clocks,
             "layers": layers,
         }
+        if extras is not None:
+            line["configs"] = extras
         emit(line)
-    model.close()
     ctx.close()
 
 
@@ -427,9 +602,16 @@ def main():
     ap.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--micro", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="batch of the workload (global for cfg4, per GPU otherwise); small "
+                         "cases for profiling")
+    ap.add_argument("--point", default="16384,8192",
+                    help="config 1 point B,K when --workload cfg1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer pass (short profiling runs)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the other configurations (short profiling runs)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

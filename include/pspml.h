@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define PSPML_ABI_VERSION 1
+#define PSPML_ABI_VERSION 2
 
 typedef enum pspml_status {
   PSPML_OK = 0,
@@ -103,6 +103,8 @@ typedef struct pspml_timing {
   double d2h_bytes;       /* bytes copied device -> host                   */
   int32_t micro_batches;  /* micro-batches the call was split into         */
   int32_t devices;        /* devices used                                  */
+  int32_t rerun_shards;   /* pspml_forward_sharded: failed shards re-run on
+                             the other devices                             */
 } pspml_timing;
 
 /* ------------------------------------------------------------------ misc */
@@ -121,11 +123,24 @@ int pspml_device_count(int* count);
  * Replaces the reference's static scratch buffers (render.rs:153-180). */
 int pspml_ctx_create(int device, size_t workspace_bytes, pspml_ctx** out);
 int pspml_ctx_destroy(pspml_ctx* ctx);
-/* Host watchdog for synchronous calls (0 = no deadline). */
+/* Host watchdog for synchronous calls (0 = no deadline).  A call that
+ * passes the deadline returns PSPML_ERR_TIMEOUT while its device work may
+ * still run: the caller keeps the buffers it passed valid until that work
+ * ends (cudaDeviceSynchronize, or any later call on the same model, which
+ * is ordered after it), and treats the outputs as not written. */
 int pspml_ctx_set_timeout_ms(pspml_ctx* ctx, int64_t timeout_ms);
 /* Reads and clears the device-side error word that kernels set when a
- * bounded wait expires; returns PSPML_ERR_DEVICE_WAIT if it was set. */
+ * bounded wait expires; returns PSPML_ERR_DEVICE_WAIT if it was set.  The
+ * tensor-core kernels bound every wait at 4 s; on expiry they record a code
+ * here, stop, let issued copies land, free tensor memory and return. */
 int pspml_ctx_check_device(pspml_ctx* ctx);
+/* Diagnostic of the path above (no counterpart in the reference): one
+ * thread waits, with the kernels' bounded wait, on a barrier that it
+ * signals itself only when `signal` != 0; an unsignalled wait gives up after
+ * limit_us (1 us .. 10 s) and sets the error word, so the next
+ * pspml_ctx_check_device returns PSPML_ERR_DEVICE_WAIT.  Synchronous; the
+ * context stays usable. */
+int pspml_ctx_wait_selftest(pspml_ctx* ctx, int64_t limit_us, int32_t signal);
 
 /* Pinned host memory for full-speed host<->device copies. */
 int pspml_host_alloc(size_t bytes, void** out);
@@ -171,9 +186,11 @@ int pspml_fully_connected_s8(pspml_ctx* ctx, const pspml_op_desc* d,
  * every device that loads the library until the process exits.
  *  - Ops needing more scratch than that (more than about 13000 output
  *    channels) are rejected with PSPML_ERR_INVALID_ARG and a message.
- *  - The first call on a device looks up the array's device address and
- *    clears the error word (a synchronous memset); make that first call
- *    before any stream capture begins.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, which may load the library's device code);
+ *    make that first call before any stream capture begins.
+ *  - A kernel that gives up on a bounded wait sets an error word inside the
+ *    same array; pspml_noalloc_check_device reads and clears it.
  *  - All calls on a device share the one array: calls whose GPU work
  *    overlaps (different streams, or host threads without ordering) race
  *    and may produce wrong results.  Order them on one stream.
@@ -184,6 +201,12 @@ int pspml_fully_connected_s8_noalloc(const pspml_op_desc* d, int64_t batch,
                                      const int32_t* bias, const int32_t* mult,
                                      const int32_t* shift, int8_t* out,
                                      void* stream);
+/* Reads and clears the error word of pspml_fully_connected_s8_noalloc on
+ * the current device (the counterpart of pspml_ctx_check_device for that
+ * entry point, which has no context): PSPML_ERR_DEVICE_WAIT if one of its
+ * kernels gave up on a bounded wait since the last check.  Synchronous;
+ * allocates nothing.  No counterpart in the reference. */
+int pspml_noalloc_check_device(void);
 
 /* Replaces naive::max_pool2d (naive.rs:98-132); any window and stride. */
 int pspml_max_pool2d_s8(pspml_ctx* ctx, const pspml_op_desc* d, int64_t batch,
@@ -269,10 +292,19 @@ int pspml_forward(pspml_model* m, const int8_t* host_in, int8_t* host_out,
 
 /* Host-buffer forward sharded by contiguous batch slices over several
  * models (one per device, one host thread each), no collective: every
- * device writes its disjoint slice of host_out. */
+ * device writes its disjoint slice of host_out.  A device whose shard fails
+ * is dropped for the call and its slice re-run, split over the devices that
+ * succeeded (timing->rerun_shards counts them); the call fails only when
+ * no device succeeded, a re-run fails, or a shard timed out (its device may
+ * still be writing its slice, so it is not re-run). */
 int pspml_forward_sharded(pspml_model* const* models, int32_t n_models,
                           const int8_t* host_in, int8_t* host_out,
                           int64_t batch, pspml_timing* timing);
+
+/* Host-side failure injection for testing the error paths (no
+ * counterpart in the reference): the next `count` forward calls on `m`
+ * return `status` (a PSPML_ERR_* code) without touching the GPU. */
+int pspml_model_fail_next(pspml_model* m, int32_t count, int32_t status);
 
 /* Timed variant, replacing generated::forward_timed (generated.rs:139-294):
  * a device-resident forward of `batch` samples (micro-batched like

@@ -10,12 +10,27 @@
 #include <thread>
 
 #include "kernels.h"
+#include "ptx.cuh"
 #include "runtime.h"
 
 namespace pspml {
 
 namespace {
 thread_local std::string g_last_error;
+
+// One thread waits, with the bounded wait every tensor-core kernel uses, on
+// an mbarrier that it arrives on only when `signal` is set; an unsignalled
+// wait runs out after limit_ns and records kDevErrSelfTest in the error
+// word, exactly as a kernel whose TMA or MMA never completed would.
+__global__ void k_wait_selftest(unsigned* err, uint64_t limit_ns, int32_t signal) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (signal) mbar_arrive(&bar);
+    if (!mbar_wait(&bar, 0, nullptr, limit_ns)) atomicCAS(err, 0u, kDevErrSelfTest);
+  }
+}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
@@ -72,6 +87,11 @@ int validate_desc(const pspml_op_desc* d) {
     case PSPML_OP_AVERAGE_POOL2D:
       if (d->out_c != d->in_c || d->zp_out != d->zp_in)
         return set_error(PSPML_ERR_INVALID_ARG, "pooling keeps channels and quantisation");
+      // Padding narrower than the window on every side keeps at least one
+      // input element in every window (an average over none is undefined).
+      if (d->pad_top >= d->kernel_h || d->pad_bottom >= d->kernel_h ||
+          d->pad_left >= d->kernel_w || d->pad_right >= d->kernel_w)
+        return set_error(PSPML_ERR_INVALID_ARG, "pooling padding must be narrower than the window");
       break;
     case PSPML_OP_RESHAPE:
       if (static_cast<int64_t>(d->in_h) * d->in_w * d->in_c !=
@@ -253,6 +273,19 @@ int pspml_ctx_check_device(pspml_ctx* ctx) {
     return set_error(PSPML_ERR_DEVICE_WAIT, buf);
   }
   return PSPML_OK;
+}
+
+int pspml_ctx_wait_selftest(pspml_ctx* ctx, int64_t limit_us, int32_t signal) {
+  clear_error();
+  if (ctx == nullptr) return set_error(PSPML_ERR_INVALID_ARG, "null context");
+  if (limit_us < 1 || limit_us > 10000000)
+    return set_error(PSPML_ERR_INVALID_ARG, "wait limit must be 1 us .. 10 s");
+  int st = cuda_status(cudaSetDevice(ctx->device), "cudaSetDevice");
+  if (st) return st;
+  k_wait_selftest<<<1, 32, 0, ctx->stream>>>(ctx->dev_err, static_cast<uint64_t>(limit_us) * 1000u,
+                                             signal);
+  if ((st = cuda_status(cudaGetLastError(), "self-test launch"))) return st;
+  return cuda_status(cudaStreamSynchronize(ctx->stream), "self-test");
 }
 
 int pspml_host_alloc(size_t bytes, void** out) {

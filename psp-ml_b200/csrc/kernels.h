@@ -89,7 +89,8 @@ inline int ep_flags(int32_t act_min, int32_t act_max, int32_t zp_out) {
 // One wide multiply-add and one shift per output.  D is stored whole so the
 // multiply-add reads it as one 64-bit operand: assembling it from two
 // separate words cost two register moves per output (14.4 against 18.0
-// outputs per clock per SM on B200, microbench/requant_forms.cu).  The table builder makes
+// outputs per clock per SM on B200, measured in a requantisation
+// microbenchmark).  The table builder makes
 // these entries for exactly the ops whose ep_flags have kEpFloor, so every
 // kernel reading an op's table agrees on its form.
 __host__ inline void floor_entry(int32_t m, uint32_t c_lo, int32_t c_hi, int32_t sr,

@@ -479,6 +479,10 @@ int pspml_forward_device(pspml_model* m, const int8_t* dev_in, int8_t* dev_out, 
   if (m == nullptr || dev_in == nullptr || dev_out == nullptr || batch < 0)
     return set_error(PSPML_ERR_INVALID_ARG, "bad forward arguments");
   std::lock_guard<std::mutex> lock(m->mu);
+  if (m->fail_next > 0) {
+    --m->fail_next;
+    return set_error(m->fail_status, "injected failure (pspml_model_fail_next)");
+  }
   cudaSetDevice(m->ctx->device);
   auto s = static_cast<cudaStream_t>(stream);
   for (int64_t b0 = 0; b0 < batch; b0 += m->max_micro) {
@@ -541,6 +545,10 @@ int pspml_forward(pspml_model* m, const int8_t* host_in, int8_t* host_out, int64
     return set_error(PSPML_ERR_INVALID_ARG, "bad forward arguments");
   const auto t0 = std::chrono::steady_clock::now();
   std::lock_guard<std::mutex> lock(m->mu);
+  if (m->fail_next > 0) {
+    --m->fail_next;
+    return set_error(m->fail_status, "injected failure (pspml_model_fail_next)");
+  }
   int st = cuda_status(cudaSetDevice(m->ctx->device), "cudaSetDevice");
   if (st) return st;
   if ((st = ensure_pipeline(m))) return st;
@@ -577,6 +585,9 @@ int pspml_forward(pspml_model* m, const int8_t* host_in, int8_t* host_out, int64
   const int wst = wait_event(m->ctx, m->ev_done);
   if (!st) st = wst;
   if (!st) st = cuda_status(cudaGetLastError(), "forward");
+  // A kernel that gave up on a bounded wait left its output incomplete:
+  // report it here rather than return results that are not.
+  if (!st) st = pspml_ctx_check_device(m->ctx);
   if (timing) {
     timing->total_ms =
         std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -584,8 +595,19 @@ int pspml_forward(pspml_model* m, const int8_t* host_in, int8_t* host_out, int64
     timing->d2h_bytes = static_cast<double>(batch) * m->out_elems;
     timing->micro_batches = static_cast<int32_t>(chunks);
     timing->devices = 1;
+    timing->rerun_shards = 0;
   }
   return st;
+}
+
+int pspml_model_fail_next(pspml_model* m, int32_t count, int32_t status) {
+  clear_error();
+  if (m == nullptr || count < 0 || status <= PSPML_OK || status > PSPML_ERR_DEVICE_WAIT)
+    return set_error(PSPML_ERR_INVALID_ARG, "bad failure-injection arguments");
+  std::lock_guard<std::mutex> lock(m->mu);
+  m->fail_next = count;
+  m->fail_status = status;
+  return PSPML_OK;
 }
 
 int pspml_forward_sharded(pspml_model* const* models, int32_t n_models, const int8_t* host_in,
@@ -601,32 +623,83 @@ int pspml_forward_sharded(pspml_model* const* models, int32_t n_models, const in
       return set_error(PSPML_ERR_INVALID_ARG, "models disagree on input/output size");
   }
   const auto t0 = std::chrono::steady_clock::now();
+  const int64_t in_e = models[0]->in_elems, out_e = models[0]->out_elems;
   const int64_t per = (batch + n_models - 1) / n_models;
   std::vector<int> status(n_models, PSPML_OK);
   std::vector<std::string> msgs(n_models);
-  std::vector<std::thread> threads;
-  for (int i = 0; i < n_models; ++i) {
-    const int64_t b0 = std::min<int64_t>(batch, i * per);
-    const int64_t cnt = std::min<int64_t>(per, batch - b0);
-    threads.emplace_back([&, i, b0, cnt] {
-      if (cnt <= 0) return;
-      pspml_model* m = models[i];
-      status[i] = pspml_forward(m, host_in + b0 * m->in_elems, host_out + b0 * m->out_elems,
-                                cnt, nullptr);
-      if (status[i]) msgs[i] = pspml_last_error();
-    });
+  std::vector<int64_t> begin(n_models), count(n_models);
+  {
+    std::vector<std::thread> threads;
+    for (int i = 0; i < n_models; ++i) {
+      begin[i] = std::min<int64_t>(batch, i * per);
+      count[i] = std::max<int64_t>(0, std::min<int64_t>(per, batch - begin[i]));
+      threads.emplace_back([&, i] {
+        if (count[i] <= 0) return;
+        pspml_model* m = models[i];
+        status[i] = pspml_forward(m, host_in + begin[i] * in_e, host_out + begin[i] * out_e,
+                                  count[i], nullptr);
+        if (status[i]) msgs[i] = pspml_last_error();
+      });
+    }
+    for (auto& t : threads) t.join();
   }
-  for (auto& t : threads) t.join();
+  // A device whose shard failed is dropped and its slice re-run, split over
+  // the devices that succeeded.  A timed-out shard is not re-run: its
+  // device may still be writing into host_out.
+  std::vector<int> healthy, failed;
+  for (int i = 0; i < n_models; ++i) (status[i] ? failed : healthy).push_back(i);
   int st = PSPML_OK;
-  for (int i = 0; i < n_models && !st; ++i)
-    if (status[i]) st = set_error(status[i], "device " + std::to_string(i) + ": " + msgs[i]);
+  for (int i : failed)
+    if (status[i] == PSPML_ERR_TIMEOUT || healthy.empty()) {
+      st = set_error(status[i], "device " + std::to_string(i) + ": " + msgs[i]);
+      break;
+    }
+  int32_t rerun = 0;
+  if (!st && !failed.empty()) {
+    struct Part {
+      int model;
+      int64_t b0, cnt;
+      int status = PSPML_OK;
+      std::string msg;
+    };
+    std::vector<Part> parts;
+    for (int i : failed) {
+      const int64_t h = static_cast<int64_t>(healthy.size());
+      const int64_t sub = (count[i] + h - 1) / h;
+      for (int64_t k = 0; k < h; ++k) {
+        const int64_t b0 = begin[i] + k * sub;
+        const int64_t cnt = std::min<int64_t>(sub, begin[i] + count[i] - b0);
+        if (cnt > 0) parts.push_back(Part{healthy[static_cast<size_t>(k)], b0, cnt});
+      }
+      ++rerun;
+    }
+    // One host thread per healthy device runs its parts in order.
+    std::vector<std::thread> threads;
+    for (int hm : healthy)
+      threads.emplace_back([&, hm] {
+        for (Part& p : parts) {
+          if (p.model != hm) continue;
+          pspml_model* m = models[hm];
+          p.status = pspml_forward(m, host_in + p.b0 * in_e, host_out + p.b0 * out_e, p.cnt,
+                                   nullptr);
+          if (p.status) p.msg = pspml_last_error();
+        }
+      });
+    for (auto& t : threads) t.join();
+    for (const Part& p : parts)
+      if (p.status) {
+        st = set_error(p.status, "re-run on device " + std::to_string(p.model) + ": " + p.msg);
+        break;
+      }
+  }
   if (timing) {
     timing->total_ms =
         std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
-    timing->h2d_bytes = static_cast<double>(batch) * models[0]->in_elems;
-    timing->d2h_bytes = static_cast<double>(batch) * models[0]->out_elems;
+    timing->h2d_bytes = static_cast<double>(batch) * in_e;
+    timing->d2h_bytes = static_cast<double>(batch) * out_e;
     timing->micro_batches = 0;
     timing->devices = n_models;
+    timing->rerun_shards = rerun;
   }
   return st;
 }

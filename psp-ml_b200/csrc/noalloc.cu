@@ -40,7 +40,9 @@ std::mutex g_setup_mu;
 
 // Looks the arrays' device addresses up once per device (the host-side
 // names are only stand-ins, never device addresses).  Must run with `dev`
-// current; it issues no allocation.
+// current; it issues no allocation.  Nothing needs clearing here: a
+// __device__ array starts at zero when the module loads, and
+// pspml_noalloc_check_device clears the error word whenever it reads it.
 int setup_device(int dev, DeviceScratch** out) {
   if (dev < 0 || dev >= kMaxDevices) return set_error(PSPML_ERR_NO_DEVICE, "device index too large");
   std::lock_guard<std::mutex> lock(g_setup_mu);
@@ -54,8 +56,6 @@ int setup_device(int dev, DeviceScratch** out) {
     st = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_err), "cudaGetSymbolAddress(error word)");
     if (st) return st;
     d.err = static_cast<unsigned*>(p);
-    st = cuda_status(cudaMemset(d.err, 0, sizeof(g_noalloc_err)), "clear error word");
-    if (st) return st;
     st = cuda_status(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev),
                      "cudaDeviceGetAttribute");
     if (st) return st;
@@ -107,4 +107,20 @@ extern "C" int pspml_fully_connected_s8_noalloc(const pspml_op_desc* d, int64_t 
                    "op preparation");
   if (st) return st;
   return cuda_status(launch_op(*d, p, batch, in, out, ds->err, ds->num_sms, s), "op launch");
+}
+
+extern "C" int pspml_noalloc_check_device(void) {
+  clear_error();
+  unsigned v = 0;
+  int st = cuda_status(cudaMemcpyFromSymbol(&v, g_noalloc_err, sizeof(v)),
+                       "read no-allocation error word");
+  if (st) return st;
+  if (v == 0) return PSPML_OK;
+  const unsigned zero = 0;
+  st = cuda_status(cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(zero)),
+                   "clear no-allocation error word");
+  if (st) return st;
+  return set_error(PSPML_ERR_DEVICE_WAIT,
+                   "a no-allocation kernel gave up on a bounded wait (code " +
+                       std::to_string(v) + ")");
 }

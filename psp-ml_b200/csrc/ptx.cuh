@@ -19,6 +19,7 @@ enum DevErr : unsigned {
   kDevErrTmaWait = 1,   // producer: stage never released
   kDevErrMmaWait = 2,   // MMA: operands never arrived / accumulator busy
   kDevErrEpiWait = 3,   // epilogue: accumulator never completed
+  kDevErrSelfTest = 4,  // pspml_ctx_wait_selftest: its unsignalled wait ran out
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -74,10 +75,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with `parity` to complete.  Returns false if the
-// time limit passed or *abort became non-zero first.
+// Waits for the phase with `parity` to complete.  Returns false if
+// `limit_ns` passed or *abort became non-zero first.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          const volatile int* abort) {
+                                          const volatile int* abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
@@ -85,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (abort != nullptr && *abort) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 

@@ -71,5 +71,9 @@ struct pspml_model {
   std::vector<std::unique_ptr<pspml::DwPwTable>> pair_tables;
   std::vector<std::unique_ptr<pspml::SmallConvTable>> sc_tables;
   uint8_t* pair_weights = nullptr;  // device: packed pointwise weights of fused pairs
+  // Host-side failure injection (pspml_model_fail_next): the next
+  // `fail_next` forward calls return `fail_status` without touching the GPU.
+  int32_t fail_next = 0;
+  int32_t fail_status = 0;
   std::mutex mu;
 };

@@ -65,7 +65,7 @@ assert ctypes.sizeof(OpDesc) == OP_DESC_DTYPE.itemsize
 class Timing(ctypes.Structure):
     _fields_ = [("total_ms", ctypes.c_double), ("h2d_bytes", ctypes.c_double),
                 ("d2h_bytes", ctypes.c_double), ("micro_batches", ctypes.c_int32),
-                ("devices", ctypes.c_int32)]
+                ("devices", ctypes.c_int32), ("rerun_shards", ctypes.c_int32)]
 
 
 class PspmlError(RuntimeError):
@@ -88,6 +88,7 @@ _PROTOS = {
     "pspml_ctx_destroy": (ctypes.c_int, [_vp]),
     "pspml_ctx_set_timeout_ms": (ctypes.c_int, [_vp, _i64]),
     "pspml_ctx_check_device": (ctypes.c_int, [_vp]),
+    "pspml_ctx_wait_selftest": (ctypes.c_int, [_vp, _i64, _i32]),
     "pspml_host_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_vp)]),
     "pspml_host_free": (ctypes.c_int, [_vp]),
     "pspml_conv2d_s8": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -97,6 +98,7 @@ _PROTOS = {
                                  [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "pspml_fully_connected_s8_noalloc": (ctypes.c_int,
                                          [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "pspml_noalloc_check_device": (ctypes.c_int, []),
     "pspml_max_pool2d_s8": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
     "pspml_average_pool2d_s8": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
     "pspml_conv2d_f32": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),
@@ -107,6 +109,7 @@ _PROTOS = {
     "pspml_model_info": (ctypes.c_int, [_vp, ctypes.POINTER(_sz), ctypes.POINTER(_sz),
                                         ctypes.POINTER(_sz)]),
     "pspml_model_op_fused": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_i32)]),
+    "pspml_model_fail_next": (ctypes.c_int, [_vp, _i32, _i32]),
     "pspml_forward_device": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp]),
     "pspml_forward": (ctypes.c_int, [_vp, _vp, _vp, _i64, ctypes.POINTER(Timing)]),
     "pspml_forward_sharded": (ctypes.c_int, [ctypes.POINTER(_vp), _i32, _vp, _vp, _i64,
@@ -197,6 +200,9 @@ class Context:
     def check_device(self) -> None:
         call("pspml_ctx_check_device", self.handle)
 
+    def wait_selftest(self, limit_us: int, signal: bool) -> None:
+        call("pspml_ctx_wait_selftest", self.handle, limit_us, 1 if signal else 0)
+
 
 class Model:
     """A compiled op chain on one device (pspml_model)."""
@@ -231,6 +237,11 @@ class Model:
         f = ctypes.c_int32()
         call("pspml_model_op_fused", self.handle, op, ctypes.byref(f))
         return f.value
+
+    def fail_next(self, count: int, status: int) -> None:
+        """Host-side failure injection: the next `count` forward calls
+        return `status` without touching the GPU."""
+        call("pspml_model_fail_next", self.handle, count, status)
 
     def forward_device(self, dev_in: int, dev_out: int, batch: int, stream: int = 0) -> None:
         call("pspml_forward_device", self.handle, dev_in, dev_out, batch, stream)

@@ -40,7 +40,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_no_device_paths(lib):
-    assert lib.pspml_abi_version() == 1
+    assert lib.pspml_abi_version() == 2
     n = ctypes.c_int(-1)
     assert lib.pspml_device_count(ctypes.byref(n)) == capi.OK
     assert n.value >= 0
@@ -56,6 +56,33 @@ def test_errors_are_status_codes(lib):
                                None) == capi.ERR_INVALID_ARG
     assert lib.pspml_model_create(None, None, 0, None, 0, 1, None) == capi.ERR_INVALID_ARG
     assert lib.pspml_forward(None, None, None, 1, None) == capi.ERR_INVALID_ARG
+    assert lib.pspml_ctx_wait_selftest(None, 1000, 0) == capi.ERR_INVALID_ARG
+    assert lib.pspml_model_fail_next(None, 1, capi.ERR_CUDA) == capi.ERR_INVALID_ARG
+
+
+def test_timing_struct_layout():
+    # double x3, int32 x3 (padded to 8): must match struct pspml_timing
+    assert ctypes.sizeof(capi.Timing) == 40
+    assert capi.Timing.rerun_shards.offset == 32
+
+
+def test_pool_window_in_padding_rejected(lib):
+    # A pooling window that lies entirely in the padding would average over
+    # no input at all: rejected before any device work.
+    d = capi.OpDesc()
+    d.kind = capi.OP_AVERAGE_POOL2D
+    d.in_h = d.in_w = 4
+    d.in_c = d.out_c = 4
+    d.kernel_h = d.kernel_w = 2
+    d.stride_h = d.stride_w = 2
+    d.pad_top = 2
+    d.out_h = (4 + 2 - 2) // 2 + 1
+    d.out_w = 2
+    d.act_min, d.act_max = -128, 127
+    st = lib.pspml_average_pool2d_s8(ctypes.c_void_p(1), ctypes.byref(d), 1,
+                                     ctypes.c_void_p(16), ctypes.c_void_p(16), None)
+    assert st == capi.ERR_INVALID_ARG
+    assert b"padding" in lib.pspml_last_error()
 
 
 def test_bad_descriptor_rejected_before_device_work(lib):

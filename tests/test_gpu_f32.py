@@ -164,3 +164,41 @@ def test_mnist_cnn_f32_network(ctx, oracle_mod):
         h = oracle_mod.f32_fully_connected(o[i * 784:(i + 1) * 784], 784, w3, b3, 64, relu=True)
         logits = oracle_mod.f32_fully_connected(h, 64, w4, b4, 10)
         assert np.array_equal(g[i], logits)
+
+
+def test_reference_mnist_model_weights_f32(ctx, oracle_mod):
+    """The reference's own MNIST model (mnist_cnn.tflite's trained weights,
+    tests/golden/mnist_cnn_f32.npz made by make_mnist_f32_fixture.py) on the
+    GPU, op by op, bit-identical to the oracle chain.  Inputs are seeded
+    u8 pixels / 255, the reference's input conversion (main.rs:25-32)."""
+    from pathlib import Path
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "mnist_cnn_f32.npz")
+    r = np.random.default_rng(77)
+    B = 33
+    x = (r.integers(0, 256, B * 28 * 28).astype(np.float32) / np.float32(255.0))
+    w1, b1 = fx["conv1_w"].reshape(-1), fx["conv1_b"]
+    w2, b2 = fx["conv2_w"].reshape(-1), fx["conv2_b"]
+    w3, b3 = fx["fc1_w"].reshape(-1), fx["fc1_b"]
+    w4, b4 = fx["fc2_w"].reshape(-1), fx["fc2_b"]
+    assert fx["conv1_relu"] and fx["conv2_relu"] and fx["fc1_relu"] and not fx["fc2_relu"]
+    c1 = conv_f32_desc(28, 28, 1, 8, 5, F32_RELU | F32_GEMM)
+    p1 = pool_f32_desc(28, 28, 8)
+    c2 = conv_f32_desc(14, 14, 8, 16, 5, F32_RELU | F32_GEMM)
+    p2 = pool_f32_desc(14, 14, 16)
+    f1 = fc_f32_desc(784, 64, F32_RELU)
+    f2 = fc_f32_desc(64, 10, 0)
+    g = _gpu(ctx, "pspml_conv2d_f32", c1, B, x, w1, b1)
+    g = _gpu(ctx, "pspml_max_pool2d_f32", p1, B, g)
+    g = _gpu(ctx, "pspml_conv2d_f32", c2, B, g, w2, b2)
+    g = _gpu(ctx, "pspml_max_pool2d_f32", p2, B, g)
+    g = _gpu(ctx, "pspml_fully_connected_f32", f1, B, g, w3, b3)
+    g = _gpu(ctx, "pspml_fully_connected_f32", f2, B, g, w4, b4).reshape(B, 10)
+    o = oracle_conv(oracle_mod, c1, B, x, w1, b1)
+    o = oracle_mod.f32_max_pool2d(o, (B, 28, 28, 8), (2, 2), (2, 2), (B, 14, 14, 8))
+    o = oracle_conv(oracle_mod, c2, B, o, w2, b2)
+    o = oracle_mod.f32_max_pool2d(o, (B, 14, 14, 16), (2, 2), (2, 2), (B, 7, 7, 16))
+    for i in range(B):
+        h = oracle_mod.f32_fully_connected(o[i * 784:(i + 1) * 784], 784, w3, b3, 64, relu=True)
+        logits = oracle_mod.f32_fully_connected(h, 64, w4, b4, 10)
+        assert np.array_equal(g[i], logits)
+    assert np.all(np.isfinite(g))

@@ -12,6 +12,7 @@
   and those of the int8 path (graphs that are not chains, asymmetric
   weights)."""
 import math
+import os
 from pathlib import Path
 
 import numpy as np
@@ -20,8 +21,29 @@ import pytest
 from golden.ref_mnist_tflite_offsets import MNIST_CONSTANTS, MNIST_FILE_BYTES
 from pspml import capi, flatbuf, netspec, tflite
 
-REF_MNIST = Path("/root/reference/examples/mnist-bench/mnist_cnn.tflite")
+# The reference checkout: PSPML_REFERENCE_ROOT, else a `reference` directory
+# beside this repository.
+REF_ROOT = Path(os.environ.get("PSPML_REFERENCE_ROOT",
+                               Path(__file__).resolve().parents[2] / "reference"))
+REF_MNIST = REF_ROOT / "examples" / "mnist-bench" / "mnist_cnn.tflite"
 needs_ref = pytest.mark.skipif(not REF_MNIST.exists(), reason="reference tree not present")
+FIXTURE = Path(__file__).resolve().parent / "golden" / "mnist_cnn_f32.npz"
+
+
+@needs_ref
+def test_mnist_fixture_holds_the_reference_weights():
+    """tests/golden/mnist_cnn_f32.npz (used by the GPU f32 test) holds exactly
+    the reference model's constants at the reference parser's offsets."""
+    m = tflite.load(REF_MNIST)
+    raw = np.frombuffer(m.data, np.float32)
+    fx = np.load(FIXTURE)
+    # tensor indices of conv1/conv2/fc1/fc2 weights and biases in the file
+    plan = tflite.to_f32_plan(m)
+    for name, p in (("conv1", plan[0]), ("conv2", plan[2]), ("fc1", plan[5]), ("fc2", plan[6])):
+        np.testing.assert_array_equal(fx[f"{name}_w"], p.weights)
+        np.testing.assert_array_equal(fx[f"{name}_b"], p.bias)
+    foff, flen = MNIST_CONSTANTS[8]
+    np.testing.assert_array_equal(fx["conv1_w"].reshape(-1), raw[foff:foff + flen])
 
 
 @needs_ref

@@ -1,12 +1,16 @@
-"""The no-allocation fully-connected entry point against the regular one.
+"""The no-allocation fully-connected entry point against the regular one and
+the oracle.
 
 pspml_fully_connected_s8_noalloc serves callers that cannot allocate device
-memory (CUDA graph capture, fixed memory budgets, caller-owned buffers): it
-takes no context and keeps its scratch in a fixed array inside the library.
-Its output must equal pspml_fully_connected_s8's, bit for bit (integer
-arithmetic), on consecutive calls that reuse that shared scratch.  This file
-is collected last so that a run stopping at the first failure has already
-run every other test; it also passes when run alone in a fresh process.
+memory (code running under CUDA graph capture, hosts whose device memory
+budget is fixed at start-up, callers that pass only buffers they already
+own): it takes no context and keeps its scratch in a fixed array inside the
+library.  Its output must equal pspml_fully_connected_s8's and the oracle's,
+bit for bit (integer arithmetic), on consecutive calls that reuse that
+shared scratch, and a call after the first must leave the device's free
+memory unchanged.  This file is collected last so that a run stopping at the
+first failure has already run every other test; it also passes when run
+alone in a fresh process.
 """
 import ctypes
 
@@ -24,23 +28,37 @@ def _fc_desc(K, N, zp_in=-3, zp_out=5, act=(5, 127)):
                      out_c=N, zp_in=zp_in, zp_out=zp_out, act_min=act[0], act_max=act[1])
 
 
-def _run_both(ctx, d, B, seed, mode="calibrated"):
-    import torch
-    r = np.random.default_rng(seed)
-    K, N = int(d["in_c"]), int(d["out_c"])
-    x = torch.from_numpy(r.integers(-128, 128, (B, K)).astype(np.int8).reshape(-1)).cuda()
-    w = torch.from_numpy(r.integers(-127, 128, (N, K)).astype(np.int8).reshape(-1)).cuda()
-    b, m, s = (torch.from_numpy(a).cuda() for a in random_quant(r, N, mode))
-    stream = torch.cuda.current_stream().cuda_stream
-    ds = capi.desc_struct(d)
-    ref = torch.empty(B * N, dtype=torch.int8, device="cuda")
-    capi.call("pspml_fully_connected_s8", ctx.handle, ctypes.byref(ds), B, x.data_ptr(),
-              w.data_ptr(), b.data_ptr(), m.data_ptr(), s.data_ptr(), ref.data_ptr(), stream)
-    got = torch.full((B * N,), 99, dtype=torch.int8, device="cuda")
-    capi.call("pspml_fully_connected_s8_noalloc", ctypes.byref(ds), B, x.data_ptr(),
-              w.data_ptr(), b.data_ptr(), m.data_ptr(), s.data_ptr(), got.data_ptr(), stream)
-    torch.cuda.synchronize()
-    return ref.cpu().numpy(), got.cpu().numpy()
+class _Case:
+    """One FC op's tensors on the device, allocated before any measured call."""
+
+    def __init__(self, d, B, seed, mode="calibrated"):
+        import torch
+        r = np.random.default_rng(seed)
+        K, N = int(d["in_c"]), int(d["out_c"])
+        self.d, self.B, self.N = d, B, N
+        self.x_h = r.integers(-128, 128, (B, K)).astype(np.int8)
+        self.w_h = r.integers(-127, 128, (N, K)).astype(np.int8)
+        self.q_h = random_quant(r, N, mode)
+        self.x = torch.from_numpy(self.x_h.reshape(-1)).cuda()
+        self.w = torch.from_numpy(self.w_h.reshape(-1)).cuda()
+        self.b, self.m, self.s = (torch.from_numpy(a).cuda() for a in self.q_h)
+        self.ref = torch.empty(B * N, dtype=torch.int8, device="cuda")
+        self.got = torch.full((B * N,), 99, dtype=torch.int8, device="cuda")
+        self.ds = capi.desc_struct(d)
+
+    def args(self, out):
+        return (ctypes.byref(self.ds), self.B, self.x.data_ptr(), self.w.data_ptr(),
+                self.b.data_ptr(), self.m.data_ptr(), self.s.data_ptr(), out.data_ptr())
+
+    def run_noalloc(self, stream):
+        capi.call("pspml_fully_connected_s8_noalloc", *self.args(self.got), stream)
+
+    def run_regular(self, ctx, stream):
+        capi.call("pspml_fully_connected_s8", ctx.handle, *self.args(self.ref), stream)
+
+    def oracle(self, orc):
+        b, m, s = self.q_h
+        return orc.op_s8(self.d, self.B, self.x_h, self.w_h, b, m, s)
 
 
 @pytest.fixture(scope="module")
@@ -52,22 +70,58 @@ def fc_ctx():
     c.close()
 
 
-def test_noalloc_matches_regular_entry_point_on_consecutive_calls(fc_ctx):
+def _check(case, orc):
+    import torch
+    torch.cuda.synchronize()
+    capi.call("pspml_noalloc_check_device")
+    got = case.got.cpu().numpy()
+    assert np.array_equal(got, case.ref.cpu().numpy()), \
+        f"{np.count_nonzero(got != case.ref.cpu().numpy())} outputs differ from the regular call"
+    assert np.array_equal(got, case.oracle(orc)), "outputs differ from the oracle"
+
+
+def test_noalloc_matches_regular_entry_point_and_oracle_on_consecutive_calls(fc_ctx, oracle_mod):
+    import torch
+    stream = torch.cuda.current_stream().cuda_stream
     # Two calls in a row with different shapes and quantisation: the second
     # reuses the scratch the first one filled.
-    cases = [(_fc_desc(512, 3337), 257, 1, "calibrated"),
-             (_fc_desc(784, 10, zp_in=-128, zp_out=0, act=(-128, 127)), 33, 2, "extreme")]
-    for d, B, seed, mode in cases:
-        ref, got = _run_both(fc_ctx, d, B, seed, mode)
-        assert np.array_equal(ref, got), f"{np.count_nonzero(ref != got)} outputs differ"
+    cases = [_Case(_fc_desc(512, 3337), 257, 1, "calibrated"),
+             _Case(_fc_desc(784, 10, zp_in=-128, zp_out=0, act=(-128, 127)), 33, 2, "extreme")]
+    for c in cases:
+        c.run_regular(fc_ctx, stream)
+        c.run_noalloc(stream)
+        _check(c, oracle_mod)
 
 
-def test_noalloc_cuda_core_path_twice(fc_ctx):
+def test_noalloc_cuda_core_path_twice(fc_ctx, oracle_mod):
+    import torch
+    stream = torch.cuda.current_stream().cuda_stream
     # K % 16 != 0 takes the CUDA-core FC kernel; run it twice in a row.
-    d = _fc_desc(100, 7)
     for seed in (3, 4):
-        ref, got = _run_both(fc_ctx, d, 5, seed)
-        assert np.array_equal(ref, got)
+        c = _Case(_fc_desc(100, 7), 5, seed)
+        c.run_regular(fc_ctx, stream)
+        c.run_noalloc(stream)
+        _check(c, oracle_mod)
+
+
+def test_noalloc_calls_leave_device_free_memory_unchanged(oracle_mod):
+    import torch
+    stream = torch.cuda.current_stream().cuda_stream
+    cases = [_Case(_fc_desc(512, 1024), 300, 5), _Case(_fc_desc(256, 64), 17, 6)]
+    cases[0].run_noalloc(stream)  # the first call on the device does its set-up
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        for c in cases:
+            c.run_noalloc(stream)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"device free memory moved by {free0 - free1} bytes"
+    capi.call("pspml_noalloc_check_device")
+    for c in cases:
+        b, m, s = c.q_h
+        want = oracle_mod.op_s8(c.d, c.B, c.x_h, c.w_h, b, m, s)
+        assert np.array_equal(c.got.cpu().numpy(), want)
 
 
 def test_noalloc_rejects_ops_beyond_its_scratch():

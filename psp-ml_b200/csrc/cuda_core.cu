@@ -346,6 +346,103 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// Conv + ReLU + 2x2 / stride-2 max pool (TFLite CONV_2D then MAX_POOL_2D):
+// a thread computes the four conv pixels of one pooled output pixel for COB
+// output channels as k_small_conv_s8 does, requantises each and keeps the
+// byte-wise signed max, so only the pooled tensor reaches memory.  TFLite
+// pools the requantised int8 outputs, so the result is exact.  Needs 4 | Co
+// (whole words) and even Ho, Wo; the pooled output is [Ho/2][Wo/2][Co].
+template <int KH, int KW, int CI, int COB, int RQ>
+__global__ void __launch_bounds__(128)
+    k_small_conv_pool_s8(const int8_t* __restrict__ in, const uint32_t* __restrict__ wpack,
+                         int32_t nw_stride, const int32_t* __restrict__ bias_eff,
+                         const RqChannel* __restrict__ rq, int8_t* __restrict__ out,
+                         const Geom g, int64_t n_base) {
+  constexpr int K = KH * KW * CI;
+  constexpr int NW = (K + 3) / 4;
+  constexpr int NW4 = (NW + 3) / 4;
+  __shared__ uint4 sw[COB][NW4];
+  const int co0 = blockIdx.y * COB;
+  for (int i = threadIdx.x; i < COB * NW4; i += blockDim.x) {
+    const int co = i / NW4, w4 = i - (i / NW4) * NW4;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (co0 + co < g.Co)
+      v = __ldg(reinterpret_cast<const uint4*>(wpack + static_cast<int64_t>(co0 + co) * nw_stride) +
+                w4);
+    sw[co][w4] = v;
+  }
+  __syncthreads();
+  const int Hp = g.Ho >> 1, Wp = g.Wo >> 1;
+  const int pix = blockIdx.x * 128 + threadIdx.x;
+  if (pix >= Hp * Wp) return;
+  const int py = pix / Wp, px = pix - (pix / Wp) * Wp;
+  const int64_t n = n_base + blockIdx.z;
+  const int8_t* img = in + n * static_cast<int64_t>(g.H) * g.W * CI;
+  const uint32_t zpb = static_cast<uint32_t>(g.zp_in) & 0xFFu;
+  const int cnt = min(COB, g.Co - co0);
+  uint32_t best[COB / 4];
+#pragma unroll 1
+  for (int sub = 0; sub < 4; ++sub) {
+    const int oy = 2 * py + (sub >> 1), ox = 2 * px + (sub & 1);
+    uint32_t x[NW4 * 4];
+#pragma unroll
+    for (int i = 0; i < NW4 * 4; ++i) x[i] = 0;
+#pragma unroll
+    for (int ky = 0; ky < KH; ++ky) {
+      const int iy = oy * g.sh - g.pt + ky;
+#pragma unroll
+      for (int kx = 0; kx < KW; ++kx) {
+        const int ix = ox * g.sw - g.pl + kx;
+        const bool ok = iy >= 0 && iy < g.H && ix >= 0 && ix < g.W;
+        const int8_t* pxp = img + (static_cast<int64_t>(ok ? iy : 0) * g.W + (ok ? ix : 0)) * CI;
+        if constexpr (CI % 4 == 0) {
+#pragma unroll
+          for (int c4 = 0; c4 < CI / 4; ++c4)
+            x[((ky * KW + kx) * CI) / 4 + c4] =
+                ok ? __ldg(reinterpret_cast<const uint32_t*>(pxp) + c4) : zpb * 0x01010101u;
+        } else {
+#pragma unroll
+          for (int ci = 0; ci < CI; ++ci) {
+            const int k = (ky * KW + kx) * CI + ci;
+            const uint32_t b =
+                ok ? static_cast<uint32_t>(static_cast<uint8_t>(__ldg(pxp + ci))) : zpb;
+            x[k >> 2] |= b << (8 * (k & 3));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int c4 = 0; c4 < COB / 4; ++c4) {
+      int32_t a[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int co = c4 * 4 + j;
+        int32_t acc = 0;
+#pragma unroll
+        for (int w4 = 0; w4 < NW4; ++w4) {
+          const uint4 wv = sw[co][w4];
+          acc = __dp4a(static_cast<int>(x[4 * w4 + 0]), static_cast<int>(wv.x), acc);
+          acc = __dp4a(static_cast<int>(x[4 * w4 + 1]), static_cast<int>(wv.y), acc);
+          acc = __dp4a(static_cast<int>(x[4 * w4 + 2]), static_cast<int>(wv.z), acc);
+          acc = __dp4a(static_cast<int>(x[4 * w4 + 3]), static_cast<int>(wv.w), acc);
+        }
+        a[j] = acc;
+      }
+      const int cb = min(co0 + 4 * c4, g.Co - 4);  // channels past Co are never stored
+      const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff + cb));
+      const uint32_t w = finish4<RQ>(a[0], a[1], a[2], a[3], b, load_rq(rq + cb),
+                                     load_rq(rq + cb + 1), load_rq(rq + cb + 2),
+                                     load_rq(rq + cb + 3), g);
+      best[c4] = sub == 0 ? w : __vmaxs4(best[c4], w);
+    }
+  }
+  uint32_t* op = reinterpret_cast<uint32_t*>(
+      out + ((n * Hp + py) * static_cast<int64_t>(Wp) + px) * g.Co + co0);
+#pragma unroll
+  for (int c4 = 0; c4 < COB / 4; ++c4)
+    if (4 * c4 < cnt) op[c4] = best[c4];
+}
+
 // Constant-table variant for 32 output channels and a patch of at most 16
 // bytes (the stem conv): weights and requant constants are kernel-parameter
 // operands at compile-time offsets, so the only loads are the input patch
@@ -765,12 +862,24 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 template <int KH, int KW, int CI, int RQ>
 cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
-                           int8_t* out, cudaStream_t s) {
+                           int8_t* out, cudaStream_t s, bool pool) {
   const int cob = g.Co <= 8 ? 8 : g.Co <= 16 ? 16 : 32;
-  const int pix = g.Ho * g.Wo;
+  const int pix = pool ? (g.Ho / 2) * (g.Wo / 2) : g.Ho * g.Wo;
   for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
     const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
     const dim3 grid((pix + 127) / 128, (g.Co + cob - 1) / cob, nz);
+    if (pool) {
+      if (cob == 8)
+        k_small_conv_pool_s8<KH, KW, CI, 8, RQ><<<grid, 128, 0, s>>>(
+            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0);
+      else if (cob == 16)
+        k_small_conv_pool_s8<KH, KW, CI, 16, RQ><<<grid, 128, 0, s>>>(
+            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0);
+      else
+        k_small_conv_pool_s8<KH, KW, CI, 32, RQ><<<grid, 128, 0, s>>>(
+            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0);
+      continue;
+    }
     if (cob == 8)
       k_small_conv_s8<KH, KW, CI, 8, RQ><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
                                                               p.rq, out, g, n0);
@@ -786,11 +895,11 @@ cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, co
 
 template <int KH, int KW, int CI>
 cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
-                           int8_t* out, cudaStream_t s) {
+                           int8_t* out, cudaStream_t s, bool pool) {
   switch (rq_form(p.all_fast_known, g.act_min, g.zp_out)) {
-    case kRqFloor: return small_conv_cob<KH, KW, CI, kRqFloor>(g, p, batch, in, out, s);
-    case kRqFast: return small_conv_cob<KH, KW, CI, kRqFast>(g, p, batch, in, out, s);
-    default: return small_conv_cob<KH, KW, CI, kRqGeneral>(g, p, batch, in, out, s);
+    case kRqFloor: return small_conv_cob<KH, KW, CI, kRqFloor>(g, p, batch, in, out, s, pool);
+    case kRqFast: return small_conv_cob<KH, KW, CI, kRqFast>(g, p, batch, in, out, s, pool);
+    default: return small_conv_cob<KH, KW, CI, kRqGeneral>(g, p, batch, in, out, s, pool);
   }
 }
 
@@ -843,19 +952,32 @@ static cudaError_t stem_s2(const Geom& g, const PreparedOp& p, int64_t batch, co
 }
 
 cudaError_t launch_small_conv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
-                              const int8_t* in, int8_t* out, cudaStream_t s) {
+                              const int8_t* in, int8_t* out, cudaStream_t s, bool pool) {
   const Geom g = geom_of(d);
+  if (pool) {
+    if (d.out_c % 4 != 0 || d.out_h % 2 != 0 || d.out_w % 2 != 0 ||
+        (reinterpret_cast<uintptr_t>(out) & 3u) != 0)
+      return cudaErrorInvalidValue;
+    switch (d.in_c) {
+      case 1: return small_conv_cob<3, 3, 1>(g, p, batch, in, out, s, true);
+      case 2: return small_conv_cob<3, 3, 2>(g, p, batch, in, out, s, true);
+      case 3: return small_conv_cob<3, 3, 3>(g, p, batch, in, out, s, true);
+      case 4: return small_conv_cob<3, 3, 4>(g, p, batch, in, out, s, true);
+      case 8: return small_conv_cob<3, 3, 8>(g, p, batch, in, out, s, true);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (p.sc_table != nullptr && p.all_fast_known && d.out_c == 32 && d.in_c == 1 &&
       d.kernel_h == 3 && d.kernel_w == 3 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
     if (stem_s2_ok(d, in, out)) return stem_s2(g, p, batch, in, out, s);
     return small_conv_tab<1>(g, p, batch, in, out, s);
   }
   switch (d.in_c) {
-    case 1: return small_conv_cob<3, 3, 1>(g, p, batch, in, out, s);
-    case 2: return small_conv_cob<3, 3, 2>(g, p, batch, in, out, s);
-    case 3: return small_conv_cob<3, 3, 3>(g, p, batch, in, out, s);
-    case 4: return small_conv_cob<3, 3, 4>(g, p, batch, in, out, s);
-    case 8: return small_conv_cob<3, 3, 8>(g, p, batch, in, out, s);
+    case 1: return small_conv_cob<3, 3, 1>(g, p, batch, in, out, s, false);
+    case 2: return small_conv_cob<3, 3, 2>(g, p, batch, in, out, s, false);
+    case 3: return small_conv_cob<3, 3, 3>(g, p, batch, in, out, s, false);
+    case 4: return small_conv_cob<3, 3, 4>(g, p, batch, in, out, s, false);
+    case 8: return small_conv_cob<3, 3, 8>(g, p, batch, in, out, s, false);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -41,7 +41,7 @@ extern template cudaError_t run_tc_bn<128>(int, int, const CUtensorMap&, const C
 
 cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
                                 const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
-                                cudaStream_t s) {
+                                cudaStream_t s, bool pool) {
   const int N = d.out_c;
   const bool is_fc = d.kind == PSPML_OP_FULLY_CONNECTED;
   const int Kc = is_fc ? d.in_h * d.in_w * d.in_c : d.in_c;
@@ -85,8 +85,16 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
                                             : CU_TENSOR_MAP_SWIZZLE_32B;
   CUtensorMap ma, mb;
   const uint32_t estr[4] = {1, 1, 1, 1};
+  if (pool && (pp.path != OpPath::kTc4d || !pp.all_fast_known || pp.table == nullptr ||
+               N % 16 != 0 || d.out_h % 2 != 0 || d.out_w % 2 != 0))
+    return cudaErrorInvalidValue;
+  a.pool = pool ? 1 : 0;
+  a.Hp = d.out_h / 2;
+  a.Wp = d.out_w / 2;
   if (pp.path == OpPath::kTc4d) {
-    const int bw = std::min(pow2_ceil(d.out_w), 128);
+    // A pooled epilogue needs a window's pixels in one warp: tiles of at
+    // most 16 pixels per row.
+    const int bw = std::min(pow2_ceil(d.out_w), pool ? 16 : 128);
     const int bh = std::min(pow2_ceil(d.out_h), 128 / bw);
     const int bi = 128 / (bw * bh);
     a.conv4d = 1;
@@ -151,7 +159,7 @@ using tcg::launch_tc_gemm_once;
 // (or A rows) run as several launches over batch slices.
 cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t batch,
                            const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
-                           cudaStream_t s) {
+                           cudaStream_t s, bool pool) {
   const bool is_fc = d.kind == PSPML_OP_FULLY_CONNECTED;
   const int64_t rows_per = is_fc ? 1 : static_cast<int64_t>(d.out_h) * d.out_w;
   // Rows bound the 2D tile count; a 4D tile holds at least one output row
@@ -159,11 +167,12 @@ cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& pp, int64_t
   const int64_t max_rows = ((1ll << 31) - 4096) / std::max(1, (d.out_c + 31) / 32);
   const int64_t chunk = std::max<int64_t>(1, max_rows / rows_per);
   const int64_t in_per = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
-  const int64_t out_per = static_cast<int64_t>(d.out_h) * d.out_w * d.out_c;
+  const int64_t out_per = pool ? static_cast<int64_t>(d.out_h / 2) * (d.out_w / 2) * d.out_c
+                              : static_cast<int64_t>(d.out_h) * d.out_w * d.out_c;
   for (int64_t b0 = 0; b0 < batch; b0 += chunk) {
     const cudaError_t e =
         launch_tc_gemm_once(d, pp, std::min(chunk, batch - b0), in + b0 * in_per,
-                            out + b0 * out_per, dev_err, num_sms, s);
+                            out + b0 * out_per, dev_err, num_sms, s, pool);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -79,7 +79,21 @@ struct TcGemmArgs {
   int32_t stages;
   int32_t b_res;  // the CTA's N tile of B stays in smem, loaded once (the grid is a
                   // multiple of tiles_n, so CTA b always works on N tile b % tiles_n)
+  // 2x2 / stride-2 max pool fused into the 4D epilogue: `out` is the pooled
+  // [nimg][Hp][Wp][N] tensor (Hp = Ho / 2, Wp = Wo / 2).  Tiles are at most
+  // 16 pixels wide, so a window's four pixels are lanes l, l ^ 1, l ^ bw,
+  // l ^ bw ^ 1 of one epilogue warp.
+  int32_t pool;
+  int32_t Hp, Wp;
 };
+
+// Signed byte-wise max of a 16-byte chunk with the same chunk of lane ^ m.
+__device__ __forceinline__ uint4 vmax_xor(const uint4 w, int m) {
+  return make_uint4(__vmaxs4(w.x, __shfl_xor_sync(0xFFFFFFFFu, w.x, m)),
+                    __vmaxs4(w.y, __shfl_xor_sync(0xFFFFFFFFu, w.y, m)),
+                    __vmaxs4(w.z, __shfl_xor_sync(0xFFFFFFFFu, w.z, m)),
+                    __vmaxs4(w.w, __shfl_xor_sync(0xFFFFFFFFu, w.w, m)));
+}
 
 constexpr int kParamSmemMax = 32 * 1024;
 
@@ -562,6 +576,37 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
             cls_off = cls * p.N;
             border = cls != p.base_cls;
             brow = bb + cls_off;
+          }
+          if constexpr (MODE == kEpiTable) {
+            if (p.pool) {
+              // Conv + ReLU + 2x2 max pool: requantise this pixel's 16
+              // channels, take the max with the window's other three lanes
+              // (horizontal neighbour lane ^ 1, vertical lane ^ bw) and let
+              // the window's top-left lane store the pooled chunk.  TFLite
+              // pools the requantised int8 outputs, so this is exact.  The
+              // host fuses only N % 16 == 0 and even Ho, Wo: a window's
+              // lanes are all valid or all invalid, and every lane joins
+              // the shuffles.
+              int8_t* prow =
+                  p.out + ((n * p.Hp + (y >> 1)) * p.Wp + (x >> 1)) * static_cast<int64_t>(p.N);
+              const bool store = valid && ((x | y) & 1) == 0;
+              const int vert = 1 << p.bw_log2;
+#pragma unroll 1
+              for (int c = 0; c < BN; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(tb + static_cast<uint32_t>(c), v);
+                const int32_t nc = tn * BN + c;
+                if (nc < p.N) {
+                  if (border) add_class_delta(v, tab, cls_off + nc, 16);
+                  uint4 w = p.clamp
+                                ? requant16_tab<(Q & kEpFloor) | kEpClamp>(v, tab, nc, p.lo4, p.hi4)
+                                : requant16_tab<Q & kEpFloor>(v, tab, nc, p.lo4, p.hi4);
+                  w = vmax_xor(vmax_xor(w, 1), vert);
+                  if (store) store16(prow + nc, w);
+                }
+              }
+              continue;
+            }
           }
         } else {
           const int64_t r = static_cast<int64_t>(tm) * TM + mt * kBM + row;

@@ -284,11 +284,25 @@ cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch
                       cudaStream_t s);
 
 // ---- individual launchers (gemm_tc.cu, cuda_core.cu)
+// pool: a 2x2 / stride-2 max pool after the conv is fused into its
+// epilogue and `out` is the pooled tensor (conv_pool_supported).
 cudaError_t launch_tc_gemm(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                            const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
-                           cudaStream_t s);
+                           cudaStream_t s, bool pool = false);
 cudaError_t launch_small_conv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
-                              const int8_t* in, int8_t* out, cudaStream_t s);
+                              const int8_t* in, int8_t* out, cudaStream_t s, bool pool = false);
+
+// Whether conv `conv` (prepared as `p`) can run with the max pool `pool`
+// after it fused into its epilogue: a 2x2 / stride-2 unpadded pool over the
+// whole conv output, a pool clamp no narrower than the conv's, and a conv
+// path with a pooled epilogue (tensor-core implicit GEMM with a constant
+// table and N % 16 == 0, or the small-channel conv with 4 | N).
+bool conv_pool_supported(const pspml_op_desc& conv, const PreparedOp& p,
+                         const pspml_op_desc& pool);
+// Launches the conv with the pool fused; `out` is the pool's output.
+cudaError_t launch_conv_pool(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                             const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                             cudaStream_t s);
 cudaError_t launch_conv_direct(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                                const int8_t* in, int8_t* out, cudaStream_t s);
 cudaError_t launch_fc_warp(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,

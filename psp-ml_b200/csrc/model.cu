@@ -82,8 +82,22 @@ int forward_chunk(pspml_model* m, const int8_t* in, int8_t* out, int64_t mb, cud
   for (size_t i = 0; i < m->ops.size(); ++i) {
     const ModelOp& op = m->ops[i];
     const int8_t* src = i == 0 ? in : ptrs[i - 1];
-    // The fused kernels store 32-byte words.
-    if (op.fuse == 1 && aligned(src) && (reinterpret_cast<uintptr_t>(ptrs[i + 1]) & 31u) == 0) {
+    if (op.fuse == 1 && op.pool_pair && aligned(src) && aligned(ptrs[i + 1])) {
+      // Conv + max pool in one kernel; the pair's time is the conv's.
+      const int st = cuda_status(launch_conv_pool(op.d, op.prep, mb, src, ptrs[i + 1],
+                                                  m->ctx->dev_err, m->ctx->num_sms, s),
+                                 "fused conv + max pool");
+      if (st) return st;
+      if (events) {
+        cudaEventRecord((*events)[i + 1], s);
+        cudaEventRecord((*events)[i + 2], s);
+      }
+      ++i;
+      continue;
+    }
+    // The fused depthwise + pointwise kernels store 32-byte words.
+    if (op.fuse == 1 && !op.pool_pair && aligned(src) &&
+        (reinterpret_cast<uintptr_t>(ptrs[i + 1]) & 31u) == 0) {
       // Depthwise + pointwise in one kernel; the pair's time is the
       // depthwise op's, the pointwise op records none.
       const ModelOp& pw = m->ops[i + 1];
@@ -103,6 +117,30 @@ int forward_chunk(pspml_model* m, const int8_t* in, int8_t* out, int64_t mb, cud
     if (events) cudaEventRecord((*events)[i + 1], s);
   }
   return PSPML_OK;
+}
+
+// Chunk sizes of the host-buffer pipeline.  Only the first chunk's input
+// copy and the last chunk's output copy run with no compute to hide them
+// under, so a long batch starts with a ramp of 1/8, 1/4 and 1/2 micro-batch
+// (each chunk's compute then covers the next, twice as large, chunk's copy)
+// before full micro-batches: the exposed copy shrinks eightfold.
+std::vector<int64_t> pipeline_chunks(int64_t batch, int64_t micro) {
+  std::vector<int64_t> sizes;
+  int64_t left = batch;
+  if (batch >= 2 * micro)
+    for (int64_t f : {8, 4, 2}) {
+      const int64_t sz = micro / f;
+      if (sz >= 64) {
+        sizes.push_back(sz);
+        left -= sz;
+      }
+    }
+  while (left > 0) {
+    const int64_t sz = std::min(micro, left);
+    sizes.push_back(sz);
+    left -= sz;
+  }
+  return sizes;
 }
 
 int ensure_pipeline(pspml_model* m) {
@@ -390,6 +428,17 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     }
   }
 
+  // Conv + max pool pairs that run as one kernel (the conv's epilogue
+  // pools its requantised outputs).
+  for (int i = 0; i + 1 < n_ops && !st; ++i) {
+    ModelOp& a = m->ops[i];
+    ModelOp& b = m->ops[i + 1];
+    if (a.fuse || b.fuse || !conv_pool_supported(a.d, a.prep, b.d)) continue;
+    a.fuse = 1;
+    a.pool_pair = true;
+    b.fuse = 2;
+  }
+
   // Arena: op i's output lives from op i until the last op reading it
   // (reshapes alias their input, extending its life).  Greedy first fit by
   // descending size over the time-overlapping buffers.
@@ -552,13 +601,14 @@ int pspml_forward(pspml_model* m, const int8_t* host_in, int8_t* host_out, int64
   int st = cuda_status(cudaSetDevice(m->ctx->device), "cudaSetDevice");
   if (st) return st;
   if ((st = ensure_pipeline(m))) return st;
-  const int64_t chunks = (batch + m->max_micro - 1) / m->max_micro;
+  const std::vector<int64_t> sizes = pipeline_chunks(batch, m->max_micro);
+  const int64_t chunks = static_cast<int64_t>(sizes.size());
   // Three streams: H2D of chunk c+1 and D2H of chunk c-1 run under the
   // compute of chunk c; two staging slots per direction.
-  for (int64_t c = 0; c < chunks && !st; ++c) {
+  int64_t b0 = 0;
+  for (int64_t c = 0; c < chunks && !st; b0 += sizes[static_cast<size_t>(c)], ++c) {
     const int k = static_cast<int>(c & 1);
-    const int64_t b0 = c * m->max_micro;
-    const int64_t mb = std::min<int64_t>(m->max_micro, batch - b0);
+    const int64_t mb = sizes[static_cast<size_t>(c)];
     const size_t in_b = static_cast<size_t>(mb * m->in_elems);
     const size_t out_b = static_cast<size_t>(mb * m->out_elems);
     if (c >= 2) cudaStreamWaitEvent(m->s_h2d, m->ev_in_free[k], 0);

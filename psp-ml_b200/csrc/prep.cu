@@ -338,6 +338,34 @@ bool host_all_fast(const int32_t* mult, const int32_t* shift, int32_t n) {
   return true;
 }
 
+bool conv_pool_supported(const pspml_op_desc& conv, const PreparedOp& p,
+                         const pspml_op_desc& pool) {
+  if (conv.kind != PSPML_OP_CONV2D || pool.kind != PSPML_OP_MAX_POOL2D) return false;
+  if (pool.kernel_h != 2 || pool.kernel_w != 2 || pool.stride_h != 2 || pool.stride_w != 2 ||
+      pool.pad_top != 0 || pool.pad_left != 0 || pool.pad_bottom != 0 || pool.pad_right != 0)
+    return false;
+  if (pool.in_h != conv.out_h || pool.in_w != conv.out_w || pool.in_c != conv.out_c ||
+      conv.out_h % 2 != 0 || conv.out_w % 2 != 0)
+    return false;
+  // The pool clamps to its own activation range; a range no narrower than
+  // the conv's makes that clamp a no-op on the conv's outputs.
+  if (pool.act_min > conv.act_min || pool.act_max < conv.act_max) return false;
+  if (p.path == OpPath::kTc4d)
+    return p.all_fast_known && p.table != nullptr && conv.out_c % 16 == 0;
+  if (p.path == OpPath::kSmallConv) return conv.out_c % 4 == 0 && small_conv_supported(conv);
+  return false;
+}
+
+cudaError_t launch_conv_pool(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                             const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                             cudaStream_t s) {
+  if (batch <= 0) return cudaSuccess;
+  if (p.path == OpPath::kTc4d)
+    return launch_tc_gemm(d, p, batch, in, out, dev_err, num_sms, s, true);
+  if (p.path == OpPath::kSmallConv) return launch_small_conv(d, p, batch, in, out, s, true);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                       const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
                       cudaStream_t s) {

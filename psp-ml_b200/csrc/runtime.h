@@ -43,9 +43,12 @@ struct ModelOp {
   int64_t out_elems = 0;      // per sample
   int64_t in_elems = 0;
   bool alias_input = false;   // reshape: output is the input buffer
-  // Fused depthwise + pointwise pair: 1 on the depthwise op (which then
-  // runs both ops in one kernel), 2 on the pointwise op (skipped).
+  // Fused pair: 1 on the first op (which then runs both ops in one
+  // kernel), 2 on the second (skipped).  The pairs are a depthwise conv
+  // with the 1x1 conv after it, and (pool_pair) a conv with the 2x2 max
+  // pool after it.
   int fuse = 0;
+  bool pool_pair = false;
   const pspml::DwPwTable* pair_table = nullptr;
   const uint8_t* wpw = nullptr;  // packed pointwise weights of the pair
 };

@@ -741,6 +741,82 @@ __global__ void k_fc_warp_s8(const int8_t* __restrict__ in, const int8_t* __rest
   if (lane == 0) out[b * N + o] = finish1(s + (bias != nullptr ? bias[o] : 0), load_rq(rq + o), g);
 }
 
+// ------------------------------------------------ small-batch FC (GEMV)
+// FC over B <= 4 samples with K % 16 == 0: a GEMV, bound by reading the
+// weights once.  A warp takes one output channel at a time (grid-stride
+// over channels, every SM busy); each lane streams 16-byte chunks of the
+// weight row, four in flight, and dots them with the same chunks of every
+// sample (the B x K activations stay in L1 / L2).  The sums start from the
+// folded bias (bias - zp_in * sum(w)), so sum(x * w) + bias_eff is TFLite's
+// sum((x - zp_in) * w) + bias; any requantisation form.
+// Read-only streaming load (no L1 allocation).  Not volatile: the compiler
+// may issue a warp's loads back to back, ahead of the dot products.
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ int32_t dot16(const uint4 a, const uint4 b, int32_t s) {
+  s = __dp4a(static_cast<int>(a.x), static_cast<int>(b.x), s);
+  s = __dp4a(static_cast<int>(a.y), static_cast<int>(b.y), s);
+  s = __dp4a(static_cast<int>(a.z), static_cast<int>(b.z), s);
+  return __dp4a(static_cast<int>(a.w), static_cast<int>(b.w), s);
+}
+
+template <int B>
+__global__ void __launch_bounds__(256)
+    k_fc_gemv_s8(const int8_t* __restrict__ in, const int8_t* __restrict__ f,
+                 const int32_t* __restrict__ bias_eff, const RqChannel* __restrict__ rq,
+                 int8_t* __restrict__ out, int32_t K, int32_t N, const Geom g) {
+  const int lane = threadIdx.x & 31;
+  const int32_t warps = static_cast<int32_t>(gridDim.x * (blockDim.x >> 5));
+  const int32_t chunks = K >> 4;
+  for (int32_t o = static_cast<int32_t>(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5));
+       o < N; o += warps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(f + static_cast<int64_t>(o) * K);
+    int32_t acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0;
+    int32_t c = lane;
+    // Eight 16-byte weight loads per lane in flight (4 KB per warp).
+    for (; c + 224 < chunks; c += 256) {
+      uint4 w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) w[u] = ld_stream16(wr + c + 32 * u);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4* xr = reinterpret_cast<const uint4*>(in + static_cast<int64_t>(b) * K);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[b] = dot16(w[u], __ldg(xr + c + 32 * u), acc[b]);
+      }
+    }
+#pragma unroll 4
+    for (; c < chunks; c += 32) {
+      const uint4 w0 = ld_stream16(wr + c);
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        acc[b] = dot16(w0, __ldg(reinterpret_cast<const uint4*>(in + static_cast<int64_t>(b) * K) + c),
+                       acc[b]);
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc[b] += __shfl_xor_sync(0xFFFFFFFFu, acc[b], off);
+    if (lane < B) {
+      int32_t a = acc[0];
+#pragma unroll
+      for (int b = 1; b < B; ++b)
+        if (lane == b) a = acc[b];
+      int32_t r = rq_apply(a + __ldg(bias_eff + o), load_rq(rq + o));
+      r = min(max(r, g.act_min), g.act_max);
+      out[static_cast<int64_t>(lane) * N + o] = static_cast<int8_t>(r);
+    }
+  }
+}
+
 // ----------------------------------------------------------------- pooling
 // Max pool: one thread per (sample, oy, ox, VEC channels); the window is
 // clipped to the image; the max starts at -128 and is then clamped.
@@ -1060,6 +1136,26 @@ cudaError_t launch_fc_warp(const pspml_op_desc& d, const PreparedOp& p, int64_t 
   const int64_t total = batch * d.out_c;
   k_fc_warp_s8<<<grid_for(total * 32), kBlock, 0, s>>>(in, p.filter, p.bias, p.rq, out, K,
                                                        d.out_c, total, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fc_gemv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                           const int8_t* in, int8_t* out, int num_sms, cudaStream_t s) {
+  const Geom g = geom_of(d);
+  const int64_t K = static_cast<int64_t>(d.in_h) * d.in_w * d.in_c;
+  if (batch < 1 || batch > kGemvMaxBatch || K % 16 != 0 || K >= (1ll << 31) ||
+      (reinterpret_cast<uintptr_t>(in) & 15u) != 0 ||
+      (reinterpret_cast<uintptr_t>(p.filter) & 15u) != 0)
+    return cudaErrorInvalidValue;
+  const int64_t warps = std::min<int64_t>(d.out_c, static_cast<int64_t>(num_sms) * 64);
+  const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
+  const int32_t k32 = static_cast<int32_t>(K);
+  switch (batch) {
+    case 1: k_fc_gemv_s8<1><<<grid, 256, 0, s>>>(in, p.filter, p.bias_eff, p.rq, out, k32, d.out_c, g); break;
+    case 2: k_fc_gemv_s8<2><<<grid, 256, 0, s>>>(in, p.filter, p.bias_eff, p.rq, out, k32, d.out_c, g); break;
+    case 3: k_fc_gemv_s8<3><<<grid, 256, 0, s>>>(in, p.filter, p.bias_eff, p.rq, out, k32, d.out_c, g); break;
+    default: k_fc_gemv_s8<4><<<grid, 256, 0, s>>>(in, p.filter, p.bias_eff, p.rq, out, k32, d.out_c, g); break;
+  }
   return cudaGetLastError();
 }
 

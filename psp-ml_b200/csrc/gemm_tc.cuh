@@ -77,6 +77,8 @@ struct TcGemmArgs {
   int32_t ep;           // ep_flags of the op (table epilogues)
   unsigned* err;
   int32_t stages;
+  int32_t group;  // k-iterations per pipeline stage (divides taps * kblocks): one
+                  // TMA barrier and one MMA commit cover `group` filter taps
   int32_t b_res;  // the CTA's N tile of B stays in smem, loaded once (the grid is a
                   // multiple of tiles_n, so CTA b always works on N tile b % tiles_n)
   // 2x2 / stride-2 max pool fused into the 4D epilogue: `out` is the pooled
@@ -330,9 +332,10 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const int stages = p.stages;
   const int kiters = p.taps * p.kblocks;
+  const int grp = p.group;  // k-iterations per stage
   uint8_t* sA = smem;
-  uint8_t* sB = smem + stages * A_BYTES;  // B ring, or all of B when b_res
-  uint8_t* sP = sB + (p.b_res ? kiters : stages) * B_BYTES;  // staged requant + bias tables
+  uint8_t* sB = smem + stages * grp * A_BYTES;  // B ring, or all of B when b_res
+  uint8_t* sP = sB + (p.b_res ? kiters : stages * grp) * B_BYTES;  // staged requant + bias tables
   RqChannel* srq = reinterpret_cast<RqChannel*>(sP);
   int32_t* sbias = reinterpret_cast<int32_t*>(sP + static_cast<size_t>(p.N) * sizeof(RqChannel));
   uint64_t* full = reinterpret_cast<uint64_t*>(sP + p.param_smem);
@@ -388,7 +391,7 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
       uint32_t ph = 0;
       int64_t issued = 0;
       bool ok = true;
-      const uint32_t a_tx = p.b_res ? A_BYTES : A_BYTES + B_BYTES;
+      const uint32_t a_tx = static_cast<uint32_t>(grp) * (p.b_res ? A_BYTES : A_BYTES + B_BYTES);
       if (p.b_res) {
         // Every SM would otherwise fetch the same few KB of weights from the
         // same L2 slices for every tile.
@@ -411,32 +414,35 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
         TileOrigin o{0, 0, 0};
         if (p.conv4d) o = tile_origin(p, static_cast<uint32_t>(tm));
         int tap = 0, kb = 0, ky = 0, kx = 0;
-        for (int it = 0; it < kiters; ++it) {
+        for (int it = 0; it < kiters; it += grp) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
             record_error(p.err, abort_flag, kDevErrTmaWait);
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[s], a_tx);
-          if (p.conv4d)
-            tma_load_4d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
-                        o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
-          else
-            tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, tm * TM);
-          if (!p.b_res)
-            tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
+          for (int g = 0; g < grp; ++g) {
+            const int slot = s * grp + g;
+            if (p.conv4d)
+              tma_load_4d(sA + slot * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
+                          o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
+            else
+              tma_load_2d(sA + slot * A_BYTES, &tmA, &full[s], kb * BK, tm * TM);
+            if (!p.b_res)
+              tma_load_2d(sB + slot * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
+            if (++kb == kblocks) {
+              kb = 0;
+              ++tap;
+              if (++kx == p.kw) {
+                kx = 0;
+                ++ky;
+              }
+            }
+          }
           ++issued;
           if (++s == stages) {
             s = 0;
             ph ^= 1u;
-          }
-          if (++kb == kblocks) {
-            kb = 0;
-            ++tap;
-            if (++kx == p.kw) {
-              kx = 0;
-              ++ky;
-            }
           }
         }
         if (!ok) break;
@@ -477,22 +483,26 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kCols);
-        for (int it = 0; it < kiters; ++it) {
+        for (int it = 0; it < kiters; it += grp) {
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             record_error(p.err, abort_flag, kDevErrMmaWait);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = a_base + static_cast<uint32_t>(s * A_BYTES);
-          const uint32_t b0 = b_base + static_cast<uint32_t>((p.b_res ? it : s) * B_BYTES);
+          for (int g = 0; g < grp; ++g) {
+            const int slot = s * grp + g;
+            const uint32_t a0 = a_base + static_cast<uint32_t>(slot * A_BYTES);
+            const uint32_t b0 =
+                b_base + static_cast<uint32_t>((p.b_res ? it + g : slot) * B_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < BK / 32; ++kk) {
-            const uint64_t bd = make_sdesc(b0 + kk * 32, 16, kSbo, kLayout);
+            for (int kk = 0; kk < BK / 32; ++kk) {
+              const uint64_t bd = make_sdesc(b0 + kk * 32, 16, kSbo, kLayout);
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-              const uint64_t ad = make_sdesc(a0 + mt * kBM * BK + kk * 32, 16, kSbo, kLayout);
-              umma_i8(d_tmem + mt * BN, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+              for (int mt = 0; mt < MT; ++mt) {
+                const uint64_t ad = make_sdesc(a0 + mt * kBM * BK + kk * 32, 16, kSbo, kLayout);
+                umma_i8(d_tmem + mt * BN, ad, bd, idesc, (it + g > 0 || kk > 0) ? 1u : 0u);
+              }
             }
           }
           umma_commit(&empty[s]);
@@ -750,17 +760,30 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   if (grid < args.tiles_total && args.tiles_n > 1 && num_sms >= args.tiles_n)
     grid = num_sms / args.tiles_n * args.tiles_n;
   const bool fixed_n = grid % args.tiles_n == 0 || grid == args.tiles_total;
-  const int bres_bytes = args.taps * args.kblocks * BN * BK;
+  const int kiters = args.taps * args.kblocks;
+  const int bres_bytes = kiters * BN * BK;
   const int base_overhead = 1024 + 64 * 8 + 64 + args.param_smem;
   args.b_res = fixed_n && base_overhead + bres_bytes + 4 * A_BYTES <= kSmemLimit;
-  const int stage_bytes = args.b_res ? A_BYTES : A_BYTES + BN * BK;
+  const int iter_bytes = args.b_res ? A_BYTES : A_BYTES + BN * BK;
   const int overhead = base_overhead + (args.b_res ? bres_bytes : 0);
+  // Stages of `group` k-iterations: the largest divisor of the tile's
+  // k-iterations (at most 9) that still leaves three stages.  Small-channel
+  // convs (9 taps of one K block each) then take one or three barrier
+  // hand-offs per tile instead of nine.
+  int group = 1;
+  for (int g = std::min(kiters, 9); g > 1; --g)
+    if (kiters % g == 0 && 3 * g * iter_bytes <= kSmemLimit - overhead) {
+      group = g;
+      break;
+    }
+  const int stage_bytes = group * iter_bytes;
   int stages = (kSmemLimit - overhead) / stage_bytes;
   stages = std::min(stages, kMaxStages);
   // At least 120 KB so that a second CTA never shares the SM: the grid is
   // one persistent CTA per SM.
   const int smem = std::max(overhead + stages * stage_bytes, 120 * 1024);
   args.stages = stages;
+  args.group = group;
   if (grid <= 0) return cudaSuccess;
   if (table == nullptr) {
     // 256-row tiles only run with a constant table (the host picks MT).

@@ -307,6 +307,13 @@ cudaError_t launch_conv_direct(const pspml_op_desc& d, const PreparedOp& p, int6
                                const int8_t* in, int8_t* out, cudaStream_t s);
 cudaError_t launch_fc_warp(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                            const int8_t* in, int8_t* out, cudaStream_t s);
+// FC over at most kGemvMaxBatch samples on a kTc2d-prepared op (folded bias
+// and requant tables), K % 16 == 0, 16-byte aligned input and filter: a
+// weight-streaming GEMV on the CUDA cores (the tensor-core tiles would hold
+// one valid row of 128).
+constexpr int64_t kGemvMaxBatch = 4;
+cudaError_t launch_fc_gemv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                           const int8_t* in, int8_t* out, int num_sms, cudaStream_t s);
 cudaError_t launch_dw3x3(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
                          const int8_t* in, int8_t* out, cudaStream_t s);
 cudaError_t launch_dw_generic(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,

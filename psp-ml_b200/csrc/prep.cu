@@ -372,6 +372,10 @@ cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch
   if (batch <= 0) return cudaSuccess;
   switch (p.path) {
     case OpPath::kTc2d:
+      if (d.kind == PSPML_OP_FULLY_CONNECTED && batch <= kGemvMaxBatch &&
+          (reinterpret_cast<uintptr_t>(in) & 15u) == 0)
+        return launch_fc_gemv(d, p, batch, in, out, num_sms, s);
+      return launch_tc_gemm(d, p, batch, in, out, dev_err, num_sms, s);
     case OpPath::kTc4d:
       return launch_tc_gemm(d, p, batch, in, out, dev_err, num_sms, s);
     case OpPath::kSmallConv:

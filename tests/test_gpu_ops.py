@@ -23,7 +23,9 @@ def _check(ctx, oracle_mod, d, batch, x, w=None, b=None, m=None, s=None):
     (3, 96, 33), (129, 64, 256), (300, 32, 48), (2, 8192, 40),
     # Row lengths of every residue mod 4 above one 256-column tile (rows
     # not 4-byte aligned take the carried-word store path).
-    (300, 64, 1002), (129, 128, 515)])
+    (300, 64, 1002), (129, 128, 515),
+    # Batches of 1-4 take the weight-streaming GEMV kernel.
+    (4, 1024, 777), (1, 16, 3), (2, 4096, 4099)])
 @pytest.mark.parametrize("mode", ["calibrated", "extreme"])
 def test_fc_tensor_core(ctx, oracle_mod, B, K, N, mode):
     r = np.random.default_rng(B * 7 + K + N)

@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(128)
     k_small_conv_s8(const int8_t* __restrict__ in, const uint32_t* __restrict__ wpack,
                     int32_t nw_stride, const int32_t* __restrict__ bias_eff,
                     const RqChannel* __restrict__ rq, int8_t* __restrict__ out, const Geom g,
-                    int64_t n_base) {
+                    int64_t n_base, uint32_t total, const FastDiv per_img) {
   constexpr int K = KH * KW * CI;
   constexpr int NW = (K + 3) / 4;
   constexpr int NW4 = (NW + 3) / 4;
@@ -272,10 +272,13 @@ __global__ void __launch_bounds__(128)
     sw[co][w4] = v;
   }
   __syncthreads();
-  const int pix = blockIdx.x * 128 + threadIdx.x;
-  if (pix >= g.Ho * g.Wo) return;
+  // Flat loop over (image, pixel): a block loads its weights once and no
+  // thread idles on a partial last block of an image.
+  for (uint32_t idx = blockIdx.x * 128 + threadIdx.x; idx < total; idx += gridDim.x * 128) {
+  const uint32_t nl = per_img.div(idx);
+  const int pix = static_cast<int>(idx - nl * per_img.d);
   const int oy = pix / g.Wo, ox = pix - (pix / g.Wo) * g.Wo;
-  const int64_t n = n_base + blockIdx.z;
+  const int64_t n = n_base + nl;
   const int8_t* img = in + n * static_cast<int64_t>(g.H) * g.W * CI;
 
   uint32_t x[NW4 * 4];
@@ -345,6 +348,7 @@ __global__ void __launch_bounds__(128)
     }
   }
 }
+}
 
 // Conv + ReLU + 2x2 / stride-2 max pool (TFLite CONV_2D then MAX_POOL_2D):
 // a thread computes the four conv pixels of one pooled output pixel for COB
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(128)
     k_small_conv_pool_s8(const int8_t* __restrict__ in, const uint32_t* __restrict__ wpack,
                          int32_t nw_stride, const int32_t* __restrict__ bias_eff,
                          const RqChannel* __restrict__ rq, int8_t* __restrict__ out,
-                         const Geom g, int64_t n_base) {
+                         const Geom g, int64_t n_base, uint32_t total, const FastDiv per_img) {
   constexpr int K = KH * KW * CI;
   constexpr int NW = (K + 3) / 4;
   constexpr int NW4 = (NW + 3) / 4;
@@ -373,10 +377,11 @@ __global__ void __launch_bounds__(128)
   }
   __syncthreads();
   const int Hp = g.Ho >> 1, Wp = g.Wo >> 1;
-  const int pix = blockIdx.x * 128 + threadIdx.x;
-  if (pix >= Hp * Wp) return;
+  for (uint32_t idx = blockIdx.x * 128 + threadIdx.x; idx < total; idx += gridDim.x * 128) {
+  const uint32_t nl = per_img.div(idx);
+  const int pix = static_cast<int>(idx - nl * per_img.d);
   const int py = pix / Wp, px = pix - (pix / Wp) * Wp;
-  const int64_t n = n_base + blockIdx.z;
+  const int64_t n = n_base + nl;
   const int8_t* img = in + n * static_cast<int64_t>(g.H) * g.W * CI;
   const uint32_t zpb = static_cast<uint32_t>(g.zp_in) & 0xFFu;
   const int cnt = min(COB, g.Co - co0);
@@ -441,6 +446,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
   for (int c4 = 0; c4 < COB / 4; ++c4)
     if (4 * c4 < cnt) op[c4] = best[c4];
+}
 }
 
 // Constant-table variant for 32 output channels and a patch of at most 16
@@ -940,31 +946,39 @@ template <int KH, int KW, int CI, int RQ>
 cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s, bool pool) {
   const int cob = g.Co <= 8 ? 8 : g.Co <= 16 ? 16 : 32;
-  const int pix = pool ? (g.Ho / 2) * (g.Wo / 2) : g.Ho * g.Wo;
-  for (int64_t n0 = 0; n0 < batch; n0 += kMaxGridZ) {
-    const unsigned nz = static_cast<unsigned>(std::min<int64_t>(kMaxGridZ, batch - n0));
-    const dim3 grid((pix + 127) / 128, (g.Co + cob - 1) / cob, nz);
+  const int64_t pix = pool ? static_cast<int64_t>(g.Ho / 2) * (g.Wo / 2)
+                           : static_cast<int64_t>(g.Ho) * g.Wo;
+  // Launches over batch slices of fewer than 2^31 (image, pixel) pairs;
+  // each block loops over the pairs (at most 16 blocks of 128 threads per
+  // SM per channel chunk).
+  const int64_t per_launch = std::max<int64_t>(1, ((1ll << 31) - 1) / pix);
+  const FastDiv fd(static_cast<uint32_t>(pix));
+  for (int64_t n0 = 0; n0 < batch; n0 += per_launch) {
+    const int64_t nimg = std::min<int64_t>(per_launch, batch - n0);
+    const uint32_t total = static_cast<uint32_t>(nimg * pix);
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>((total + 127) / 128, 148 * 16)),
+                    (g.Co + cob - 1) / cob, 1);
     if (pool) {
       if (cob == 8)
         k_small_conv_pool_s8<KH, KW, CI, 8, RQ><<<grid, 128, 0, s>>>(
-            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0);
+            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0, total, fd);
       else if (cob == 16)
         k_small_conv_pool_s8<KH, KW, CI, 16, RQ><<<grid, 128, 0, s>>>(
-            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0);
+            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0, total, fd);
       else
         k_small_conv_pool_s8<KH, KW, CI, 32, RQ><<<grid, 128, 0, s>>>(
-            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0);
+            in, p.wpack, p.nw, p.bias_eff, p.rq, out, g, n0, total, fd);
       continue;
     }
     if (cob == 8)
       k_small_conv_s8<KH, KW, CI, 8, RQ><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
-                                                              p.rq, out, g, n0);
+                                                              p.rq, out, g, n0, total, fd);
     else if (cob == 16)
       k_small_conv_s8<KH, KW, CI, 16, RQ><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
-                                                               p.rq, out, g, n0);
+                                                               p.rq, out, g, n0, total, fd);
     else
       k_small_conv_s8<KH, KW, CI, 32, RQ><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff,
-                                                               p.rq, out, g, n0);
+                                                               p.rq, out, g, n0, total, fd);
   }
   return cudaGetLastError();
 }

@@ -227,9 +227,12 @@ struct NoTable {
 enum : int {
   kEpiGeneral = 0,  // tables in smem or global, runtime fast/general requant
   kEpiTable = 1,    // fast requant, tables a kernel parameter, runtime offsets
-  kEpiStatic = 2    // as kEpiTable with every offset a compile-time constant:
+  kEpiStatic = 2,   // as kEpiTable with every offset a compile-time constant:
                     // 2D A, up to four N tiles (N == tiles_n * BN) with a
                     // fixed N tile per CTA, 16-byte aligned rows
+  kEpiConvStatic = 3  // 4D (implicit-GEMM conv) A with N == BN (one N tile):
+                      // compile-time table offsets, border-class bias
+                      // differences and the fused max pool as in kEpiTable
 };
 template <int MODE>
 struct TabOf {
@@ -310,6 +313,38 @@ __device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_
     } else {
       if (valid) st_global_v8(orow + c, w0, w1);
     }
+  }
+}
+
+// One output pixel of a conv tile whose N is the tile width, every
+// requantisation constant at a compile-time table offset (a constant-bank
+// operand, no load): the run-time-offset loop of kEpiTable loads two table
+// words per output.  Tensor-memory loads run one 16-column chunk ahead.
+// `border`: the pixel's class is not the table's base class (its bias
+// difference is added from dbias[cls_off + channel]).  POOL: the 2x2 max
+// over lanes l, l ^ 1, l ^ vert (see the pooled branch of the kernel); the
+// window's top-left lane stores the pooled chunk at `orow`.  Q: the op's
+// ep_flags.
+template <int BN, int Q, bool POOL>
+__device__ __forceinline__ void epilogue_row_conv(const EpiTable& tab, uint32_t taddr,
+                                                  int8_t* orow, bool store, bool border,
+                                                  int cls_off, int vert, const TcGemmArgs& p) {
+  uint32_t v0[16], v1[16];
+  tmem_ld16_nowait(taddr, v0);
+#pragma unroll
+  for (int c = 0; c < BN; c += 32) {
+    tmem_wait_ld(v0);
+    tmem_ld16_nowait(taddr + c + 16, v1);
+    if (border) add_class_delta(v0, tab, cls_off + c, 16);
+    uint4 w0 = requant16_tab<Q>(v0, tab, c, p.lo4, p.hi4);
+    if constexpr (POOL) w0 = vmax_xor(vmax_xor(w0, 1), vert);
+    if (store) store16(orow + c, w0);
+    tmem_wait_ld(v1);
+    if (c + 32 < BN) tmem_ld16_nowait(taddr + c + 32, v0);
+    if (border) add_class_delta(v1, tab, cls_off + c + 16, 16);
+    uint4 w1 = requant16_tab<Q>(v1, tab, c + 16, p.lo4, p.hi4);
+    if constexpr (POOL) w1 = vmax_xor(vmax_xor(w1, 1), vert);
+    if (store) store16(orow + c + 16, w1);
   }
 }
 
@@ -414,6 +449,40 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
         TileOrigin o{0, 0, 0};
         if (p.conv4d) o = tile_origin(p, static_cast<uint32_t>(tm));
         int tap = 0, kb = 0, ky = 0, kx = 0;
+        // (The static 2D epilogue only runs 1x1 GEMMs, whose stages are one
+        // k-block: those kernels carry only this loop.)
+        if (MODE == kEpiStatic || grp == 1) {
+        // One k-block per stage (the loop of the 1x1 GEMMs, whose tiles are
+        // short enough that this thread's own instructions set the pace).
+        for (int it = 0; it < kiters; ++it) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+            record_error(p.err, abort_flag, kDevErrTmaWait);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], a_tx);
+          if (p.conv4d)
+            tma_load_4d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, o.x0 + kx - p.pad_l,
+                        o.y0 + ky - p.pad_t, static_cast<int32_t>(o.n0));
+          else
+            tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * BK, tm * TM);
+          if (!p.b_res)
+            tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], tap * p.Kc + kb * BK, tn * BN);
+          ++issued;
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+          if (++kb == kblocks) {
+            kb = 0;
+            ++tap;
+            if (++kx == p.kw) {
+              kx = 0;
+              ++ky;
+            }
+          }
+        }
+        } else if constexpr (MODE != kEpiStatic)
         for (int it = 0; it < kiters; it += grp) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
             record_error(p.err, abort_flag, kDevErrTmaWait);
@@ -483,6 +552,32 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kCols);
+        if (MODE == kEpiStatic || grp == 1) {
+        for (int it = 0; it < kiters; ++it) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            record_error(p.err, abort_flag, kDevErrMmaWait);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = a_base + static_cast<uint32_t>(s * A_BYTES);
+          const uint32_t b0 = b_base + static_cast<uint32_t>((p.b_res ? it : s) * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t bd = make_sdesc(b0 + kk * 32, 16, kSbo, kLayout);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              const uint64_t ad = make_sdesc(a0 + mt * kBM * BK + kk * 32, 16, kSbo, kLayout);
+              umma_i8(d_tmem + mt * BN, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        } else if constexpr (MODE != kEpiStatic)
         for (int it = 0; it < kiters; it += grp) {
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             record_error(p.err, abort_flag, kDevErrMmaWait);
@@ -562,6 +657,30 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
             case 2: epilogue_row_static<BN, 2 * BN, Q>(tab, ta, orow, ok, p); break;
             default: epilogue_row_static<BN, 3 * BN, Q>(tab, ta, orow, ok, p); break;
           }
+        }
+      } else if constexpr (MODE == kEpiConvStatic) {
+        // Implicit-GEMM conv, one N tile: pixel (x, y) of image n.
+        const uint32_t tm = static_cast<uint32_t>(t);
+        const TileOrigin o = tile_origin(p, tm);
+        const int32_t x = o.x0 + (row & ((1 << p.bw_log2) - 1));
+        const int32_t y = o.y0 + ((row >> p.bw_log2) & ((1 << p.bh_log2) - 1));
+        const int64_t n = o.n0 + (row >> (p.bw_log2 + p.bh_log2));
+        const bool valid = x < p.Wo && y < p.Ho && n < p.nimg;
+        int cls_off = 0;
+        bool border = false;
+        if (valid && p.ycls != nullptr) {
+          const int cls = p.ycls[y] * p.n_xcls + p.xcls[x];
+          cls_off = cls * BN;
+          border = cls != p.base_cls;
+        }
+        if (p.pool) {
+          int8_t* prow =
+              p.out + ((n * p.Hp + (y >> 1)) * p.Wp + (x >> 1)) * static_cast<int64_t>(BN);
+          epilogue_row_conv<BN, Q, true>(tab, tb0, prow, valid && ((x | y) & 1) == 0, border,
+                                         cls_off, 1 << p.bw_log2, p);
+        } else {
+          int8_t* orow = p.out + ((n * p.Ho + y) * p.Wo + x) * static_cast<int64_t>(BN);
+          epilogue_row_conv<BN, Q, false>(tab, tb0, orow, valid, border, cls_off, 0, p);
         }
       } else {
 #pragma unroll 1
@@ -766,12 +885,14 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   args.b_res = fixed_n && base_overhead + bres_bytes + 4 * A_BYTES <= kSmemLimit;
   const int iter_bytes = args.b_res ? A_BYTES : A_BYTES + BN * BK;
   const int overhead = base_overhead + (args.b_res ? bres_bytes : 0);
-  // Stages of `group` k-iterations: the largest divisor of the tile's
-  // k-iterations (at most 9) that still leaves three stages.  Small-channel
-  // convs (9 taps of one K block each) then take one or three barrier
-  // hand-offs per tile instead of nine.
+  // Stages of `group` k-iterations for convs with several filter taps: the
+  // largest divisor of the tile's k-iterations (at most 9) that still
+  // leaves three stages.  Small-channel 3x3 convs (9 taps of one K block
+  // each) then take one or three barrier hand-offs per tile instead of nine.
+  // (1x1 GEMMs keep one k-block per stage: grouping their 2-4 K blocks
+  // measured slower.)
   int group = 1;
-  for (int g = std::min(kiters, 9); g > 1; --g)
+  for (int g = std::min(kiters, 9); args.taps > 1 && g > 1; --g)
     if (kiters % g == 0 && 3 * g * iter_bytes <= kSmemLimit - overhead) {
       group = g;
       break;
@@ -792,6 +913,16 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
                                                         s);
     else
       return cudaErrorInvalidValue;
+  }
+  if constexpr (MT == 1) {
+    if (args.conv4d && args.tiles_n == 1 && args.N == BN) {
+      switch (args.ep) {
+        case 0: return launch_variant<BN, BK, 1, kEpiConvStatic, 0>(ma, mb, args, *table, grid, smem, s);
+        case 1: return launch_variant<BN, BK, 1, kEpiConvStatic, 1>(ma, mb, args, *table, grid, smem, s);
+        case 2: return launch_variant<BN, BK, 1, kEpiConvStatic, 2>(ma, mb, args, *table, grid, smem, s);
+        default: return launch_variant<BN, BK, 1, kEpiConvStatic, 3>(ma, mb, args, *table, grid, smem, s);
+      }
+    }
   }
   const bool is_static = !args.conv4d && fixed_n && args.tiles_n <= 4 &&
                          args.N == args.tiles_n * BN && args.ldo == args.N &&

@@ -88,6 +88,8 @@ struct RsArgs {
   uint32_t dw_lo4, dw_hi4, pw_lo4, pw_hi4;
   unsigned* err;
   int32_t stages;
+  int32_t borders;  // 0: every border class has the base class's folded bias (an
+                    // input zero point of 0), so no pixel needs a difference
 };
 
 // Barriers of one slot.  Rows are numbered per slot across its strips; row
@@ -266,8 +268,8 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
     const bool valid = x < p.Wo && (P == 1 || static_cast<int>(n) < p.batch);
     const bool any_valid = __any_sync(0xFFFFFFFFu, valid);
     // Border classes: the first, the last and the interior output rows.
-    int cls_top = 0, cls_mid = 0, cls_bot = 0;
-    if (valid) {
+    int cls_top = p.base_cls, cls_mid = p.base_cls, cls_bot = p.base_cls;
+    if (valid && p.borders) {
       const int xc = p.xcls[x];
       cls_top = p.ycls[0] * p.n_xcls + xc;
       cls_mid = p.ycls[Ho > 1 ? 1 : 0] * p.n_xcls + xc;
@@ -862,6 +864,10 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
   a.xcls = pdw.xcls;
   a.n_xcls = pdw.n_xcls;
   a.base_cls = pdw.base_cls;
+  // With an input zero point of 0 the zero fill at the borders is the real
+  // zero: every class's bias difference is 0 and the epilogue skips them.
+  a.borders = 0;
+  for (int i = 0; i < pdw.ncls * C && !a.borders; ++i) a.borders = tab.dw_dbias[i] != 0;
   a.dw_lo4 = splat4(dw.act_min);
   a.dw_hi4 = splat4(dw.act_max);
   a.pw_lo4 = splat4(pw_min);

@@ -51,7 +51,19 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
   // tile, and B stays resident.  (For N <= 256 one 256-column tile is
   // faster: splitting it makes every CTA pair read A twice.)
   const bool tab = pp.all_fast_known && pp.table != nullptr;
-  const int bn = N <= 32 ? 32 : N <= 64 ? 64 : (N <= 128 || (tab && N > 256 && N <= 512)) ? 128 : 256;
+  int bn = N <= 32 ? 32 : N <= 64 ? 64 : (N <= 128 || (tab && N > 256 && N <= 512)) ? 128 : 256;
+  // A 2D GEMM with few row tiles (an FC over a small batch) would leave
+  // most SMs idle with wide N tiles: narrow them until the grid covers the
+  // SMs (each CTA then streams a narrower slice of the weights).
+  bool narrowed = false;
+  if (pp.path == OpPath::kTc2d) {
+    const int64_t rows2d = is_fc ? batch : batch * d.out_h * d.out_w;
+    const int64_t tiles_m = (rows2d + kBM - 1) / kBM;
+    while (bn > 32 && tiles_m * ((N + bn - 1) / bn) < num_sms) {
+      bn /= 2;
+      narrowed = true;
+    }
+  }
   const int bk = Kc >= 128 ? 128 : (Kc > 32 ? 64 : 32);
 
   TcGemmArgs a{};
@@ -123,7 +135,7 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
   } else {
     const int64_t rows = is_fc ? batch : batch * d.out_h * d.out_w;
     if (rows >= (1ll << 31) - 2 * kBM) return cudaErrorInvalidValue;
-    mt = bn <= 64 && rows > kBM && pp.all_fast_known && pp.table != nullptr ? 2 : 1;
+    mt = bn <= 64 && !narrowed && rows > kBM && pp.all_fast_known && pp.table != nullptr ? 2 : 1;
     a.conv4d = 0;
     a.rows = rows;
     a.ldo = N;

@@ -449,6 +449,156 @@ __global__ void __launch_bounds__(128)
 }
 }
 
+// 3x3 stride-1 conv with few input channels (CI in {1, 2, 3, 4, 8}): a
+// thread computes a 2x2 block of output pixels x COB channels from the 4x4
+// input window it loads once (zero point outside the image), so every
+// weight word read from shared memory and every requantisation constant
+// serves four pixels (one pixel per thread re-read each weight per pixel
+// and loaded its nine taps separately).  For CI % 4 == 0 the patch words
+// are the window's pixel words themselves; for CI < 4 they are assembled
+// from the window bytes.  POOL: the block is the 2x2 window of the max pool
+// after the conv and only its max is stored ([Ho/2][Wo/2][Co]); otherwise
+// the block's pixels inside the image are stored.  Needs 4 | Co.
+template <int CI, int COB, int RQ, bool POOL>
+__global__ void __launch_bounds__(128)
+    k_small_conv_2x2_s8(const int8_t* __restrict__ in, const uint32_t* __restrict__ wpack,
+                        int32_t nw_stride, const int32_t* __restrict__ bias_eff,
+                        const RqChannel* __restrict__ rq, int8_t* __restrict__ out,
+                        const Geom g, int64_t n_base, uint32_t total, const FastDiv per_img,
+                        const FastDiv per_row) {
+  constexpr int K = 9 * CI;
+  constexpr int NW = (K + 3) / 4;
+  constexpr int NW4 = (NW + 3) / 4;
+  constexpr int CW = CI % 4 == 0 ? CI / 4 : 0;  // words per pixel when whole words
+  __shared__ uint4 sw[COB][NW4];
+  const int co0 = blockIdx.y * COB;
+  for (int i = threadIdx.x; i < COB * NW4; i += blockDim.x) {
+    const int co = i / NW4, w4 = i - (i / NW4) * NW4;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (co0 + co < g.Co)
+      v = __ldg(reinterpret_cast<const uint4*>(wpack + static_cast<int64_t>(co0 + co) * nw_stride) +
+                w4);
+    sw[co][w4] = v;
+  }
+  __syncthreads();
+  const int Bw = static_cast<int>(per_row.d);
+  const uint32_t zp4 = (static_cast<uint32_t>(g.zp_in) & 0xFFu) * 0x01010101u;
+  const int Hp = g.Ho >> 1, Wp = g.Wo >> 1;
+  for (uint32_t idx = blockIdx.x * 128 + threadIdx.x; idx < total; idx += gridDim.x * 128) {
+    const uint32_t nl = per_img.div(idx);
+    const uint32_t blk = idx - nl * per_img.d;
+    const int by = static_cast<int>(per_row.div(blk));
+    const int bx = static_cast<int>(blk) - by * Bw;
+    const int oy0 = 2 * by, ox0 = 2 * bx;
+    const int64_t n = n_base + nl;
+    const int8_t* img = in + n * static_cast<int64_t>(g.H) * g.W * CI;
+    const int iy0 = oy0 - g.pt, ix0 = ox0 - g.pl;
+
+    // The 4x4 window: words of CI % 4 == 0 pixels, or bytes.
+    uint32_t win[4][4][CW > 0 ? CW : CI];
+#pragma unroll
+    for (int wy = 0; wy < 4; ++wy) {
+      const int iy = iy0 + wy;
+#pragma unroll
+      for (int wx = 0; wx < 4; ++wx) {
+        const int ix = ix0 + wx;
+        const bool ok = iy >= 0 && iy < g.H && ix >= 0 && ix < g.W;
+        const int8_t* pxp = img + (static_cast<int64_t>(ok ? iy : 0) * g.W + (ok ? ix : 0)) * CI;
+        if constexpr (CW == 2) {
+          const uint2 v = ok ? __ldg(reinterpret_cast<const uint2*>(pxp)) : make_uint2(zp4, zp4);
+          win[wy][wx][0] = v.x;
+          win[wy][wx][1] = v.y;
+        } else if constexpr (CW == 1) {
+          win[wy][wx][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(pxp)) : zp4;
+        } else {
+#pragma unroll
+          for (int ci = 0; ci < CI; ++ci)
+            win[wy][wx][ci] = ok ? static_cast<uint32_t>(static_cast<uint8_t>(__ldg(pxp + ci)))
+                                 : (zp4 & 0xFFu);
+        }
+      }
+    }
+    // Patch words of the four pixels (sub = dy * 2 + dx), filter order
+    // (ky, kx, ci), zero beyond the K bytes.
+    uint32_t x[4][NW4 * 4];
+#pragma unroll
+    for (int sub = 0; sub < 4; ++sub) {
+      const int dy = sub >> 1, dx = sub & 1;
+#pragma unroll
+      for (int wi = 0; wi < NW4 * 4; ++wi) x[sub][wi] = 0;
+      if constexpr (CW > 0) {
+#pragma unroll
+        for (int t = 0; t < 9; ++t)
+#pragma unroll
+          for (int c = 0; c < CW; ++c) x[sub][t * CW + c] = win[dy + t / 3][dx + t % 3][c];
+      } else {
+#pragma unroll
+        for (int t = 0; t < 9; ++t)
+#pragma unroll
+          for (int ci = 0; ci < CI; ++ci) {
+            const int k = t * CI + ci;
+            x[sub][k >> 2] |= win[dy + t / 3][dx + t % 3][ci] << (8 * (k & 3));
+          }
+      }
+    }
+    const int cnt = min(COB, g.Co - co0);
+    uint32_t* prow = nullptr;  // pooled output word row
+    uint32_t* orow[4];         // the block's output word rows (null outside the image)
+    if constexpr (POOL) {
+      prow = reinterpret_cast<uint32_t*>(
+          out + ((n * Hp + by) * static_cast<int64_t>(Wp) + bx) * g.Co + co0);
+    } else {
+#pragma unroll
+      for (int sub = 0; sub < 4; ++sub) {
+        const int oy = oy0 + (sub >> 1), ox = ox0 + (sub & 1);
+        orow[sub] = (oy < g.Ho && ox < g.Wo)
+                        ? reinterpret_cast<uint32_t*>(
+                              out + ((n * g.Ho + oy) * static_cast<int64_t>(g.Wo) + ox) * g.Co + co0)
+                        : nullptr;
+      }
+    }
+#pragma unroll
+    for (int c4 = 0; c4 < COB / 4; ++c4) {
+      int32_t a[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) a[sub][j] = 0;
+#pragma unroll
+        for (int w4 = 0; w4 < NW4; ++w4) {
+          const uint4 wv = sw[c4 * 4 + j][w4];
+#pragma unroll
+          for (int sub = 0; sub < 4; ++sub) {
+            int32_t acc = a[sub][j];
+            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 0]), static_cast<int>(wv.x), acc);
+            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 1]), static_cast<int>(wv.y), acc);
+            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 2]), static_cast<int>(wv.z), acc);
+            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 3]), static_cast<int>(wv.w), acc);
+            a[sub][j] = acc;
+          }
+        }
+      }
+      const int cb = min(co0 + 4 * c4, g.Co - 4);  // channels past Co are never stored
+      const int4 b = __ldg(reinterpret_cast<const int4*>(bias_eff + cb));
+      const RqChannel q0 = load_rq(rq + cb), q1 = load_rq(rq + cb + 1),
+                      q2 = load_rq(rq + cb + 2), q3 = load_rq(rq + cb + 3);
+      uint32_t r4[4];
+#pragma unroll
+      for (int sub = 0; sub < 4; ++sub)
+        r4[sub] = finish4<RQ>(a[sub][0], a[sub][1], a[sub][2], a[sub][3], b, q0, q1, q2, q3, g);
+      if (4 * c4 < cnt) {
+        if constexpr (POOL) {
+          prow[c4] = __vmaxs4(__vmaxs4(r4[0], r4[1]), __vmaxs4(r4[2], r4[3]));
+        } else {
+#pragma unroll
+          for (int sub = 0; sub < 4; ++sub)
+            if (orow[sub] != nullptr) orow[sub][c4] = r4[sub];
+        }
+      }
+    }
+  }
+}
+
 // Constant-table variant for 32 output channels and a patch of at most 16
 // bytes (the stem conv): weights and requant constants are kernel-parameter
 // operands at compile-time offsets, so the only loads are the input patch
@@ -755,15 +905,11 @@ __global__ void k_fc_warp_s8(const int8_t* __restrict__ in, const int8_t* __rest
 // sample (the B x K activations stay in L1 / L2).  The sums start from the
 // folded bias (bias - zp_in * sum(w)), so sum(x * w) + bias_eff is TFLite's
 // sum((x - zp_in) * w) + bias; any requantisation form.
-// Read-only streaming load (no L1 allocation).  Not volatile: the compiler
-// may issue a warp's loads back to back, ahead of the dot products.
-__device__ __forceinline__ uint4 ld_stream16(const void* p) {
-  uint4 v;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "l"(p));
-  return v;
-}
+// Streaming (evict-first) 16-byte load through the intrinsic, which the
+// compiler schedules freely: a lane's eight weight loads issue back to back,
+// ahead of the dot products (inline assembly was kept in order and left
+// one load in flight).
+__device__ __forceinline__ uint4 ld_stream16(const uint4* p) { return __ldcs(p); }
 
 __device__ __forceinline__ int32_t dot16(const uint4 a, const uint4 b, int32_t s) {
   s = __dp4a(static_cast<int>(a.x), static_cast<int>(b.x), s);
@@ -983,9 +1129,50 @@ cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, co
   return cudaGetLastError();
 }
 
+// The 2x2-block kernel (3x3, stride 1, 4 | Co, 4-byte aligned output).
+template <int CI, int RQ>
+cudaError_t small_conv_2x2(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
+                           int8_t* out, cudaStream_t s, bool pool) {
+  const int cob = g.Co <= 8 ? 8 : g.Co <= 16 ? 16 : 32;
+  const int bh = pool ? g.Ho / 2 : (g.Ho + 1) / 2;
+  const int bw = pool ? g.Wo / 2 : (g.Wo + 1) / 2;
+  const int64_t per = static_cast<int64_t>(bh) * bw;
+  const int64_t per_launch = std::max<int64_t>(1, ((1ll << 31) - 1) / per);
+  const FastDiv fd(static_cast<uint32_t>(per)), fr(static_cast<uint32_t>(bw));
+  for (int64_t n0 = 0; n0 < batch; n0 += per_launch) {
+    const int64_t nimg = std::min<int64_t>(per_launch, batch - n0);
+    const uint32_t total = static_cast<uint32_t>(nimg * per);
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>((total + 127) / 128, 148 * 16)),
+                    (g.Co + cob - 1) / cob, 1);
+#define PSPML_SC2(COB, POOLV)                                                              \
+  k_small_conv_2x2_s8<CI, COB, RQ, POOLV><<<grid, 128, 0, s>>>(in, p.wpack, p.nw, p.bias_eff, \
+                                                                p.rq, out, g, n0, total, fd, fr)
+    if (pool) {
+      if (cob == 8) PSPML_SC2(8, true);
+      else if (cob == 16) PSPML_SC2(16, true);
+      else PSPML_SC2(32, true);
+    } else {
+      if (cob == 8) PSPML_SC2(8, false);
+      else if (cob == 16) PSPML_SC2(16, false);
+      else PSPML_SC2(32, false);
+    }
+#undef PSPML_SC2
+  }
+  return cudaGetLastError();
+}
+
 template <int KH, int KW, int CI>
 cudaError_t small_conv_cob(const Geom& g, const PreparedOp& p, int64_t batch, const int8_t* in,
                            int8_t* out, cudaStream_t s, bool pool) {
+  if (KH == 3 && KW == 3 && g.sh == 1 && g.sw == 1 && g.Co % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 3u) == 0 &&
+      (CI % 4 != 0 || (reinterpret_cast<uintptr_t>(in) & (4u * (CI / 4) - 1)) == 0)) {
+    switch (rq_form(p.all_fast_known, g.act_min, g.zp_out)) {
+      case kRqFloor: return small_conv_2x2<CI, kRqFloor>(g, p, batch, in, out, s, pool);
+      case kRqFast: return small_conv_2x2<CI, kRqFast>(g, p, batch, in, out, s, pool);
+      default: return small_conv_2x2<CI, kRqGeneral>(g, p, batch, in, out, s, pool);
+    }
+  }
   switch (rq_form(p.all_fast_known, g.act_min, g.zp_out)) {
     case kRqFloor: return small_conv_cob<KH, KW, CI, kRqFloor>(g, p, batch, in, out, s, pool);
     case kRqFast: return small_conv_cob<KH, KW, CI, kRqFast>(g, p, batch, in, out, s, pool);

@@ -110,6 +110,23 @@ def test_conv_direct(ctx, oracle_mod, B, H, W, Ci, Co, k, stride):
     _check(ctx, oracle_mod, d, B, x, w, b, m, s)
 
 
+# 3x3 stride-1 convs with in_c in {1, 2, 3, 4, 8} run the 2x2-block kernel
+# (one 4x4 input window per thread): odd output sizes leave partial blocks,
+# Co = 36 a partial second channel chunk.
+@pytest.mark.parametrize("B,H,W,Ci,Co", [
+    (2, 7, 9, 2, 12), (3, 5, 11, 4, 8), (2, 13, 6, 8, 36), (4, 1, 1, 3, 4), (2, 9, 3, 1, 16)])
+@pytest.mark.parametrize("zp_in,mode", [(-128, "calibrated"), (7, "calibrated"),
+                                        (-3, "extreme")])
+def test_small_conv_2x2_blocks(ctx, oracle_mod, B, H, W, Ci, Co, zp_in, mode):
+    r = np.random.default_rng(7 * H + W + 11 * Ci + Co + zp_in)
+    d = conv_desc(capi.OP_CONV2D, H, W, Ci, Co, k=3, stride=1, zp_in=zp_in, zp_out=-5,
+                  act=(-5, 127))
+    x = r.integers(-128, 128, (B, H, W, Ci)).astype(np.int8)
+    w = r.integers(-127, 128, (Co, 3, 3, Ci)).astype(np.int8)
+    b, m, s = random_quant(r, Co, mode)
+    _check(ctx, oracle_mod, d, B, x, w, b, m, s)
+
+
 # ------------------------------------------------------------ depthwise conv
 @pytest.mark.parametrize("B,H,W,C,stride", [
     (2, 48, 256, 32, 1), (2, 48, 256, 64, 2), (3, 12, 64, 256, 1), (2, 6, 32, 512, 1),

@@ -997,4 +997,56 @@ cudaError_t launch_dwrs_pair(const pspml_op_desc& dw, const PreparedOp& pdw,
                 in, out, dev_err, num_sms, s);
 }
 
+// ---- dense 3x3 conv on the row-streaming kernel
+// A 32 -> 32 channel 3x3 stride-1 conv is the depthwise kernel with full
+// 32x32 weight blocks in place of the block-diagonal ones: per input row
+// and tap kx one MMA (K = the row's 32 input channels, N = the 32 output
+// channels of each output row the input row feeds) accumulates every
+// (ky, kx) tap, and every input row crosses into shared memory once
+// (the implicit-GEMM conv loads each input pixel once per filter tap).
+// The border-class folded biases are the conv's own (every class sums
+// over the input channels of its in-image taps).
+
+// [9 taps][2 K-halves][32 output channels][16 input-channel bytes], the
+// layout of the depthwise packing with dense blocks.
+__global__ void k_pack_conv32_rs(const int8_t* __restrict__ f, uint8_t* __restrict__ out) {
+  const int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= 9 * 1024) return;
+  const int tap = i / 1024;
+  const int half = (i % 1024) / 512;
+  const int co = (i % 512) / 16;
+  const int j = i % 16;
+  out[i] = static_cast<uint8_t>(f[(co * 9 + tap) * 32 + half * 16 + j]);
+}
+
+namespace {
+pspml_op_desc dense_as_depthwise(const pspml_op_desc& conv) {
+  pspml_op_desc dw = conv;
+  dw.kind = PSPML_OP_DEPTHWISE_CONV2D;
+  return dw;
+}
+}  // namespace
+
+bool dense_rs_supported(const pspml_op_desc& conv, const PreparedOp& p) {
+  if (conv.kind != PSPML_OP_CONV2D || conv.in_c != 32 || conv.out_c != 32 ||
+      conv.kernel_h != 3 || conv.kernel_w != 3 || conv.stride_h != 1 || conv.stride_w != 1)
+    return false;
+  if (p.path != OpPath::kTc4d || p.table == nullptr || !p.all_fast_known || p.ncls > 9)
+    return false;
+  return rs_geometry_ok(dense_as_depthwise(conv));
+}
+
+cudaError_t pack_conv32_rs(const int8_t* filter, uint8_t* out, cudaStream_t s) {
+  k_pack_conv32_rs<<<(9 * 1024 + 255) / 256, 256, 0, s>>>(filter, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dense_rs(const pspml_op_desc& conv, const PreparedOp& p,
+                            const uint8_t* wpack, int64_t batch, const int8_t* in, int8_t* out,
+                            unsigned* dev_err, int num_sms, cudaStream_t s) {
+  PreparedOp q = p;
+  q.wpack = reinterpret_cast<const uint32_t*>(wpack);
+  return launch_dwrs_dw(dense_as_depthwise(conv), q, batch, in, out, dev_err, num_sms, s);
+}
+
 }  // namespace pspml

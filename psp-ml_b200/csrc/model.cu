@@ -50,6 +50,11 @@ int64_t filter_bytes_of(const pspml_op_desc& d) {
 
 int run_op(pspml_model* m, const ModelOp& op, int64_t mb, const int8_t* src, int8_t* dst,
            cudaStream_t s) {
+  if (op.rs_weights != nullptr && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(dst) & 31u) == 0)
+    return cuda_status(launch_dense_rs(op.d, op.prep, op.rs_weights, mb, src, dst,
+                                       m->ctx->dev_err, m->ctx->num_sms, s),
+                       "row-streamed conv");
   return cuda_status(
       launch_op(op.d, op.prep, mb, src, dst, m->ctx->dev_err, m->ctx->num_sms, s), "op launch");
 }
@@ -190,6 +195,7 @@ int pspml_model_destroy(pspml_model* m) {
   if (m->arena) cudaFree(m->arena);
   if (m->weights) cudaFree(m->weights);
   if (m->pair_weights) cudaFree(m->pair_weights);
+  if (m->rs_weights) cudaFree(m->rs_weights);
   delete m;
   return PSPML_OK;
 }
@@ -428,12 +434,32 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     }
   }
 
+  // 32 -> 32 channel 3x3 convs stream their input rows (each input row
+  // loaded once rather than once per filter tap); their max pool, if any,
+  // then runs on its own.
+  if (!st) {
+    std::vector<int> rs_ops;
+    for (int i = 0; i < n_ops; ++i)
+      if (dense_rs_supported(m->ops[i].d, m->ops[i].prep)) rs_ops.push_back(i);
+    if (!rs_ops.empty()) {
+      st = cuda_status(cudaMalloc(&m->rs_weights, rs_ops.size() * 9216), "cudaMalloc(rs weights)");
+      for (size_t k = 0; k < rs_ops.size() && !st; ++k) {
+        ModelOp& op = m->ops[rs_ops[k]];
+        uint8_t* w = m->rs_weights + k * 9216;
+        st = cuda_status(pack_conv32_rs(op.prep.filter, w, ctx->stream), "pack conv weights");
+        op.rs_weights = w;
+      }
+      if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "pack conv weights");
+    }
+  }
+
   // Conv + max pool pairs that run as one kernel (the conv's epilogue
   // pools its requantised outputs).
   for (int i = 0; i + 1 < n_ops && !st; ++i) {
     ModelOp& a = m->ops[i];
     ModelOp& b = m->ops[i + 1];
-    if (a.fuse || b.fuse || !conv_pool_supported(a.d, a.prep, b.d)) continue;
+    if (a.fuse || b.fuse || a.rs_weights != nullptr || !conv_pool_supported(a.d, a.prep, b.d))
+      continue;
     a.fuse = 1;
     a.pool_pair = true;
     b.fuse = 2;

@@ -49,6 +49,9 @@ struct ModelOp {
   // pool after it.
   int fuse = 0;
   bool pool_pair = false;
+  // A 32 -> 32 channel 3x3 conv run on the row-streaming kernel with these
+  // packed dense weights (dense_rs_supported).
+  const uint8_t* rs_weights = nullptr;
   const pspml::DwPwTable* pair_table = nullptr;
   const uint8_t* wpw = nullptr;  // packed pointwise weights of the pair
 };
@@ -74,6 +77,7 @@ struct pspml_model {
   std::vector<std::unique_ptr<pspml::DwPwTable>> pair_tables;
   std::vector<std::unique_ptr<pspml::SmallConvTable>> sc_tables;
   uint8_t* pair_weights = nullptr;  // device: packed pointwise weights of fused pairs
+  uint8_t* rs_weights = nullptr;    // device: packed dense weights of row-streamed convs
   // Host-side failure injection (pspml_model_fail_next): the next
   // `fail_next` forward calls return `fail_status` without touching the GPU.
   int32_t fail_next = 0;

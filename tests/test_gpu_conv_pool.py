@@ -42,6 +42,23 @@ def _model_parts(H, W, ci, co, zp_in, zp_out, conv_act, pool_act, seed):
     return descs, blob
 
 
+def _run_chain(ctx, oracle_mod, descs, blob, batch, micro, seed):
+    import torch
+    r = np.random.default_rng(seed)
+    H, W, ci = int(descs[0]["in_h"]), int(descs[0]["in_w"]), int(descs[0]["in_c"])
+    x = r.integers(-128, 128, (batch, H, W, ci)).astype(np.int8)
+    model = capi.Model(ctx, descs, blob, micro)
+    fused = tuple(model.op_fused(i) for i in range(len(descs)))
+    xi = torch.from_numpy(x.reshape(-1)).cuda()
+    out = torch.full((batch * model.out_bytes,), 77, dtype=torch.int8, device="cuda")
+    model.forward_device(xi.data_ptr(), out.data_ptr(), batch,
+                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    model.close()
+    return fused, out.cpu().numpy().reshape(batch, -1), oracle_mod.net_forward_s8(descs, blob, x)
+
+
 def _run(ctx, oracle_mod, descs, blob, batch, micro, seed):
     import torch
     r = np.random.default_rng(seed)
@@ -62,7 +79,7 @@ def _run(ctx, oracle_mod, descs, blob, batch, micro, seed):
 
 
 @pytest.mark.parametrize("H,W,ci,co,batch", [
-    (64, 64, 32, 32, 3),     # config 2 stage 0 (tiles of 16 x 8 pixels)
+    (64, 64, 16, 32, 3),     # tiles of 16 x 8 pixels over 64-pixel rows
     (32, 32, 64, 64, 5),     # stage 1
     (16, 16, 128, 128, 9),   # stage 2
     (8, 8, 256, 256, 17),    # stage 3 (two images per tile)
@@ -100,3 +117,22 @@ def test_narrower_pool_clamp_is_not_fused(ctx, oracle_mod, ci):
     fused, got, want = _run(ctx, oracle_mod, descs, blob, 3, 3, 3)
     assert fused == (0, 0)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("H,W,zp_in,act", [
+    (64, 64, -128, "relu"),    # config 2's s0b shape
+    (48, 256, 0, "none"),      # two 128-pixel column tiles
+    (12, 20, 21, "relu"),
+    (7, 9, -128, "none"),      # odd sizes
+])
+def test_row_streamed_32_channel_conv(ctx, oracle_mod, H, W, zp_in, act):
+    """A 32 -> 32 channel 3x3 stride-1 conv runs on the row-streaming kernel
+    with dense weight blocks (each input row loaded once); a max pool after
+    it then runs on its own."""
+    conv_act, zp_out = ((-3, 127), -3) if act == "relu" else ((-128, 127), 5)
+    descs, blob = _model_parts(H, W, 32, 32, zp_in, zp_out, conv_act, (-128, 127), H + W)
+    if H % 2 or W % 2:
+        descs = descs[:1].copy()  # the conv alone
+    fused, got, want = _run_chain(ctx, oracle_mod, descs, blob, 5, 5, 4)
+    assert fused[0] == 0
+    assert np.array_equal(got, want), f"{np.count_nonzero(got != want)} outputs differ"

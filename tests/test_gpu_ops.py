@@ -118,7 +118,7 @@ def test_conv_direct(ctx, oracle_mod, B, H, W, Ci, Co, k, stride):
 @pytest.mark.parametrize("zp_in,mode", [(-128, "calibrated"), (7, "calibrated"),
                                         (-3, "extreme")])
 def test_small_conv_2x2_blocks(ctx, oracle_mod, B, H, W, Ci, Co, zp_in, mode):
-    r = np.random.default_rng(7 * H + W + 11 * Ci + Co + zp_in)
+    r = np.random.default_rng(1000 + 7 * H + W + 11 * Ci + Co + zp_in)
     d = conv_desc(capi.OP_CONV2D, H, W, Ci, Co, k=3, stride=1, zp_in=zp_in, zp_out=-5,
                   act=(-5, 127))
     x = r.integers(-128, 128, (B, H, W, Ci)).astype(np.int8)

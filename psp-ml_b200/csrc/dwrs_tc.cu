@@ -832,8 +832,13 @@ bool rs_geometry_ok(const pspml_op_desc& d) {
 
 // Samples per 128-row tile: 1 for rows of more than 64 pixels, 2 for
 // 33..64, 4 for up to 32 (stride 1, C >= 64, depthwise alone).
+// Set in the depthwise-shaped descriptor of a dense 32 -> 32 conv
+// (launch_dense_rs): its 64-pixel rows pack two samples per tile too.
+constexpr int32_t kRsDenseFlag = 1 << 16;
+
 int rs_packing(const pspml_op_desc& d, int npw) {
-  if (npw != 0 || d.in_c < 64 || d.out_w > 64 || d.stride_h != 1) return 1;
+  if (npw != 0 || d.out_w > 64 || d.stride_h != 1) return 1;
+  if (d.in_c < 64) return (d.flags & kRsDenseFlag) != 0 && d.out_w > 32 ? 2 : 1;
   return d.out_w > 32 ? 2 : 4;
 }
 
@@ -916,6 +921,7 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
     }
   } else if (S == 1) {
     if (P == 2) {
+      if (C == 32) return rs_shape<1, 0, 1, 1, 2>(m, a, tab, dwq, 0, num_sms, s);
       if (C == 64) return rs_shape<2, 0, 1, 1, 2>(m, a, tab, dwq, 0, num_sms, s);
       if (C == 128) return rs_shape<2, 0, 1, 2, 2>(m, a, tab, dwq, 0, num_sms, s);
       if (C == 256) return rs_shape<2, 0, 1, 4, 2>(m, a, tab, dwq, 0, num_sms, s);
@@ -1023,6 +1029,7 @@ namespace {
 pspml_op_desc dense_as_depthwise(const pspml_op_desc& conv) {
   pspml_op_desc dw = conv;
   dw.kind = PSPML_OP_DEPTHWISE_CONV2D;
+  dw.flags |= kRsDenseFlag;
   return dw;
 }
 }  // namespace

@@ -113,7 +113,10 @@ struct RsBars {
 // NS: slots; RS: epilogue sets per slot (four warps each, one per
 // tensor-memory lane quarter, taking rows in turn); P: samples packed into
 // the 128 tile rows (rows of at most 128 / P pixels).
-template <int CG, int NPW, int S, int NCB, int P>
+// GI: 0 for the depthwise conv; for a dense 3x3 conv the number of
+// 32-channel input groups (every output group then accumulates every input
+// group: weights [output group][input group][tap]).
+template <int CG, int NPW, int S, int NCB, int P, int GI = 0>
 struct RsShape {
   static constexpr int NS = 2;
   static constexpr int RS = 2;
@@ -129,12 +132,13 @@ struct RsShape {
   // the next sample's pixels).
   static constexpr int kBoxes = P > 1 ? 3 : (S == 1 ? 1 : 2);
   static constexpr int kRegion = P > 1 ? 128 * 16 : kRsRegion;
-  static constexpr int kInRow = CG * 2 * kBoxes * kRegion;
+  static constexpr int GIN = GI > 0 ? GI : CG;        // input groups per row
+  static constexpr int kInRow = GIN * 2 * kBoxes * kRegion;
   static constexpr int kApw = NPW > 0 ? 128 * C : 0;
   static constexpr int kSlotCols = 512 / NS;
   static constexpr int kThreads = 128 + NS * RS * 128;
   static_assert(CG * R * 32 + NPW <= kSlotCols, "tensor memory per slot");
-  static constexpr int kBdw = CG * 3 * kTap;           // resident weights of one block
+  static constexpr int kBdw = CG * (GI > 0 ? GI : 1) * 3 * kTap;  // resident weights of one block
   static_assert(NCB == 1 || NPW == 0, "channel blocks are for the depthwise conv alone");
   static_assert(NCB == 1 || NCB == 2 || NCB == 4 || NCB == 8, "channel blocks");
   static_assert(P == 1 || P == 2 || P == 4, "packed samples");
@@ -142,6 +146,7 @@ struct RsShape {
                 "packed samples are for a stride-1 depthwise conv alone");
   static_assert(NPW == 0 || S == 1, "fused pointwise after a stride-1 depthwise conv");
   static_assert(RS <= kRsMaxSets, "epilogue sets");
+  static_assert(GI == 0 || (NCB == 1 && NPW == 0), "dense conv: one channel block, no pair");
 };
 
 // Weight block order per kx: ky of each 32-row block.
@@ -374,11 +379,13 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
   }
 }
 
-template <int CG, int NPW, int S, int NCB, int P, int DWQ, int PWQ>
-__global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
+template <int CG, int NPW, int S, int NCB, int P, int DWQ, int PWQ, int GI = 0>
+__global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
     k_dwrs_s8(const __grid_constant__ CUtensorMap tmIn, const RsArgs p,
               const __grid_constant__ DwPwTable tab) {
-  using Sh = RsShape<CG, NPW, S, NCB, P>;
+  using Sh = RsShape<CG, NPW, S, NCB, P, GI>;
+  constexpr int GIN = Sh::GIN;
+  static_assert(Sh::Wt * P == 128, "tile rows");
   constexpr int C = Sh::C;
   constexpr int NS = Sh::NS;
   constexpr int RS = Sh::RS;
@@ -405,7 +412,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
   // channel block as NBB ky blocks (two K-halves of NBB*32 rows x 16 B);
   // the pointwise weights as packed.
   {
-    constexpr int nB = CG * 3 * 2 * NBB * 32;  // 16-byte rows
+    constexpr int nB = CG * (GI > 0 ? GI : 1) * 3 * 2 * NBB * 32;  // 16-byte rows
     for (int i = threadIdx.x; i < nB; i += blockDim.x) {
       int t = i;
       const int rr = t % 32;
@@ -484,9 +491,9 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
           uint8_t* a = in_k + s * Sh::kInRow;
           if constexpr (P > 1) {
             // Per tap kx a box of Wt pixels per sample, already shifted.
-            mbar_arrive_expect_tx(&b.in_full[s], CG * 3 * 2 * P * 16 * Sh::Wt);
+            mbar_arrive_expect_tx(&b.in_full[s], GIN * 3 * 2 * P * 16 * Sh::Wt);
 #pragma unroll
-            for (int gq = 0; gq < CG; ++gq)
+            for (int gq = 0; gq < GIN; ++gq)
 #pragma unroll
               for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
@@ -498,10 +505,10 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
                                 y, static_cast<int>(st.n) + pm);
                   }
           } else if constexpr (S == 1) {
-            mbar_arrive_expect_tx(&b.in_full[s], CG * 2 * 16 * 130);
+            mbar_arrive_expect_tx(&b.in_full[s], GIN * 2 * 16 * 130);
             const int x0 = st.tx * 128 - p.pad_l;
 #pragma unroll
-            for (int gq = 0; gq < CG; ++gq)
+            for (int gq = 0; gq < GIN; ++gq)
 #pragma unroll
               for (int h = 0; h < 2; ++h)
                 tma_load_4d(a + (gq * 2 + h) * kRsRegion, &tmIn, &b.in_full[s],
@@ -509,10 +516,10 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
           } else {
             // Even pixels 2j (j from the tile's first output) and odd
             // pixels 2j+1 (from one pair earlier with a left pad).
-            mbar_arrive_expect_tx(&b.in_full[s], CG * 2 * 2 * 16 * 129);
+            mbar_arrive_expect_tx(&b.in_full[s], GIN * 2 * 2 * 16 * 129);
             const int j0 = st.tx * 128;
 #pragma unroll
-            for (int gq = 0; gq < CG; ++gq)
+            for (int gq = 0; gq < GIN; ++gq)
 #pragma unroll
               for (int eo = 0; eo < 2; ++eo)
 #pragma unroll
@@ -641,14 +648,30 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
             while (j1 < R && ((live >> j1) & 1u) != 0) ++j1;
             const uint32_t idesc = j1 - j == 1 ? idesc1 : (j1 - j == 2 ? idesc2 : idesc3);
             const uint64_t bwin = bdesc0 + static_cast<uint64_t>((o + j) * 32);
+            if constexpr (GI == 0) {
 #pragma unroll
-            for (int gq = 0; gq < CG; ++gq) {
+              for (int gq = 0; gq < CG; ++gq) {
 #pragma unroll
-              for (int kx = 0; kx < 3; ++kx) {
-                umma_i8(tm_slot + static_cast<uint32_t>(gq * R * 32 + j * 32),
-                        astage + gq * kGroupA + aoff[kx],
-                        bwin + static_cast<uint64_t>(((gq * 3 + kx) * Sh::kTap) / 16), idesc, 1u);
+                for (int kx = 0; kx < 3; ++kx) {
+                  umma_i8(tm_slot + static_cast<uint32_t>(gq * R * 32 + j * 32),
+                          astage + gq * kGroupA + aoff[kx],
+                          bwin + static_cast<uint64_t>(((gq * 3 + kx) * Sh::kTap) / 16), idesc,
+                          1u);
+                }
               }
+            } else {
+              // Dense: output group go sums every input group gi.
+#pragma unroll
+              for (int go = 0; go < CG; ++go)
+#pragma unroll
+                for (int gi = 0; gi < GI; ++gi)
+#pragma unroll
+                  for (int kx = 0; kx < 3; ++kx)
+                    umma_i8(tm_slot + static_cast<uint32_t>(go * R * 32 + j * 32),
+                            astage + gi * kGroupA + aoff[kx],
+                            bwin + static_cast<uint64_t>((((go * GI + gi) * 3 + kx) * Sh::kTap) /
+                                                         16),
+                            idesc, 1u);
             }
             j = j1;
           }
@@ -735,7 +758,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P>::kThreads, 1)
   }
 }
 
-template <int CG, int NPW, int S, int NCB, int P, int DWC, int PWC>
+template <int CG, int NPW, int S, int NCB, int P, int DWC, int PWC, int GI = 0>
 cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int grid,
                       int smem, cudaStream_t s) {
   static std::atomic<uint64_t> done{0};
@@ -743,23 +766,23 @@ cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& ta
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load() & bit) == 0) {
-    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC>,
+    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC, GI>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kRsSmemLimit);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit);
   }
-  k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC>
-      <<<grid, RsShape<CG, NPW, S, NCB, P>::kThreads, smem, s>>>(m, a, tab);
+  k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC, GI>
+      <<<grid, RsShape<CG, NPW, S, NCB, P, GI>::kThreads, smem, s>>>(m, a, tab);
   return cudaGetLastError();
 }
 
 // The pointwise epilogue variant (ep_flags of the pointwise op).
-template <int CG, int NPW, int S, int NCB, int P, int DWQ>
+template <int CG, int NPW, int S, int NCB, int P, int DWQ, int GI = 0>
 cudaError_t rs_launch_pw(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int pwq,
                          int grid, int smem, cudaStream_t s) {
   if constexpr (NPW == 0) {
-    return rs_launch<CG, NPW, S, NCB, P, DWQ, 0>(m, a, tab, grid, smem, s);
+    return rs_launch<CG, NPW, S, NCB, P, DWQ, 0, GI>(m, a, tab, grid, smem, s);
   } else {
     switch (pwq) {
       case 0: return rs_launch<CG, NPW, S, NCB, P, DWQ, 0>(m, a, tab, grid, smem, s);
@@ -771,9 +794,9 @@ cudaError_t rs_launch_pw(const CUtensorMap& m, const RsArgs& a, const DwPwTable&
 }
 
 // Shared memory of one launch (bytes) and its input stages.
-template <int CG, int NPW, int S, int NCB, int P>
+template <int CG, int NPW, int S, int NCB, int P, int GI = 0>
 bool rs_smem(int* smem, int* stages) {
-  using Sh = RsShape<CG, NPW, S, NCB, P>;
+  using Sh = RsShape<CG, NPW, S, NCB, P, GI>;
   const int fixed = Sh::kBdw + NPW * Sh::C + Sh::NS * Sh::RS * Sh::kApw;
   const int overhead = 1024 + fixed + Sh::NS * static_cast<int>(sizeof(RsBars)) + 64;
   const int st = std::min(kRsMaxStages, (kRsSmemLimit - overhead) / (Sh::NS * Sh::kInRow));
@@ -783,22 +806,22 @@ bool rs_smem(int* smem, int* stages) {
   return true;
 }
 
-template <int CG, int NPW, int S, int NCB, int P>
+template <int CG, int NPW, int S, int NCB, int P, int GI = 0>
 cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, int dwq, int pwq,
                      int num_sms, cudaStream_t s) {
-  using Sh = RsShape<CG, NPW, S, NCB, P>;
+  using Sh = RsShape<CG, NPW, S, NCB, P, GI>;
   int smem = 0;
-  if (!rs_smem<CG, NPW, S, NCB, P>(&smem, &a.stages)) return cudaErrorInvalidValue;
+  if (!rs_smem<CG, NPW, S, NCB, P, GI>(&smem, &a.stages)) return cudaErrorInvalidValue;
   // NCB CTAs per group of strips, one per channel block.
   const int per_block = static_cast<int>(std::min<int64_t>(
       (static_cast<int64_t>(a.strips) + Sh::NS - 1) / Sh::NS, std::max(1, num_sms / NCB)));
   const int grid = per_block * NCB;
   if (a.strips <= 0) return cudaSuccess;
   switch (dwq) {
-    case 0: return rs_launch_pw<CG, NPW, S, NCB, P, 0>(m, a, tab, pwq, grid, smem, s);
-    case 1: return rs_launch_pw<CG, NPW, S, NCB, P, 1>(m, a, tab, pwq, grid, smem, s);
-    case 2: return rs_launch_pw<CG, NPW, S, NCB, P, 2>(m, a, tab, pwq, grid, smem, s);
-    default: return rs_launch_pw<CG, NPW, S, NCB, P, 3>(m, a, tab, pwq, grid, smem, s);
+    case 0: return rs_launch_pw<CG, NPW, S, NCB, P, 0, GI>(m, a, tab, pwq, grid, smem, s);
+    case 1: return rs_launch_pw<CG, NPW, S, NCB, P, 1, GI>(m, a, tab, pwq, grid, smem, s);
+    case 2: return rs_launch_pw<CG, NPW, S, NCB, P, 2, GI>(m, a, tab, pwq, grid, smem, s);
+    default: return rs_launch_pw<CG, NPW, S, NCB, P, 3, GI>(m, a, tab, pwq, grid, smem, s);
   }
 }
 
@@ -838,7 +861,11 @@ constexpr int32_t kRsDenseFlag = 1 << 16;
 
 int rs_packing(const pspml_op_desc& d, int npw) {
   if (npw != 0 || d.out_w > 64 || d.stride_h != 1) return 1;
-  if (d.in_c < 64) return (d.flags & kRsDenseFlag) != 0 && d.out_w > 32 ? 2 : 1;
+  if ((d.flags & kRsDenseFlag) != 0) {
+    if (d.out_c == 32) return d.out_w > 32 ? 2 : 1;  // 32 -> 32: one or two samples per tile
+    return d.out_w > 32 ? 2 : 4;
+  }
+  if (d.in_c < 64) return 1;
   return d.out_w > 32 ? 2 : 4;
 }
 
@@ -903,6 +930,21 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
     if (encode_tensor_map(&m, in, 5, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
+  }
+  if ((dw.flags & kRsDenseFlag) != 0 && dw.out_c != 32) {
+    // Dense 32 -> 64 (one input group) and 64 -> 64 (two), stride 1.
+    if (S != 1 || dw.out_c != 64 || npw != 0) return cudaErrorInvalidValue;
+    if (C == 32) {
+      if (P == 1) return rs_shape<2, 0, 1, 1, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (P == 2) return rs_shape<2, 0, 1, 1, 2, 1>(m, a, tab, dwq, 0, num_sms, s);
+      return rs_shape<2, 0, 1, 1, 4, 1>(m, a, tab, dwq, 0, num_sms, s);
+    }
+    if (C == 64) {
+      if (P == 1) return rs_shape<2, 0, 1, 1, 1, 2>(m, a, tab, dwq, 0, num_sms, s);
+      if (P == 2) return rs_shape<2, 0, 1, 1, 2, 2>(m, a, tab, dwq, 0, num_sms, s);
+      return rs_shape<2, 0, 1, 1, 4, 2>(m, a, tab, dwq, 0, num_sms, s);
+    }
+    return cudaErrorInvalidValue;
   }
   if (npw == 64 && C == 64 && S == 1 && P == 1)
     return rs_shape<2, 64, 1, 1, 1>(m, a, tab, dwq, pwq, num_sms, s);
@@ -1004,25 +1046,32 @@ cudaError_t launch_dwrs_pair(const pspml_op_desc& dw, const PreparedOp& pdw,
 }
 
 // ---- dense 3x3 conv on the row-streaming kernel
-// A 32 -> 32 channel 3x3 stride-1 conv is the depthwise kernel with full
-// 32x32 weight blocks in place of the block-diagonal ones: per input row
-// and tap kx one MMA (K = the row's 32 input channels, N = the 32 output
+// A 3x3 stride-1 conv with 32 or 64 input and output channels is the
+// depthwise kernel with full 32x32 weight blocks in place of the
+// block-diagonal ones: per input row, tap kx and (output group, input
+// group) one MMA (K = 32 input channels, N = the group's 32 output
 // channels of each output row the input row feeds) accumulates every
-// (ky, kx) tap, and every input row crosses into shared memory once
-// (the implicit-GEMM conv loads each input pixel once per filter tap).
-// The border-class folded biases are the conv's own (every class sums
-// over the input channels of its in-image taps).
+// (ky, kx) tap, and every input row crosses into shared memory once (the
+// implicit-GEMM conv loads each input pixel once per filter tap).  The
+// border-class folded biases are the conv's own (every class sums over the
+// input channels of its in-image taps).
 
-// [9 taps][2 K-halves][32 output channels][16 input-channel bytes], the
-// layout of the depthwise packing with dense blocks.
-__global__ void k_pack_conv32_rs(const int8_t* __restrict__ f, uint8_t* __restrict__ out) {
+// [Co/32 x Ci/32 blocks (output group major)][9 taps][2 K-halves]
+// [32 output channels][16 input-channel bytes]: the layout of the depthwise
+// packing with dense blocks.
+__global__ void k_pack_conv_rs(const int8_t* __restrict__ f, int32_t ci, int32_t co,
+                               uint8_t* __restrict__ out) {
   const int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
-  if (i >= 9 * 1024) return;
-  const int tap = i / 1024;
-  const int half = (i % 1024) / 512;
-  const int co = (i % 512) / 16;
-  const int j = i % 16;
-  out[i] = static_cast<uint8_t>(f[(co * 9 + tap) * 32 + half * 16 + j]);
+  const int gi_n = ci / 32;
+  if (i >= (co / 32) * gi_n * 9 * 1024) return;
+  const int blk = i / (9 * 1024);
+  const int go = blk / gi_n, gi = blk % gi_n;
+  const int r = i % (9 * 1024);
+  const int tap = r / 1024;
+  const int half = (r % 1024) / 512;
+  const int row = (r % 512) / 16;
+  const int j = r % 16;
+  out[i] = static_cast<uint8_t>(f[((go * 32 + row) * 9 + tap) * ci + gi * 32 + half * 16 + j]);
 }
 
 namespace {
@@ -1035,25 +1084,49 @@ pspml_op_desc dense_as_depthwise(const pspml_op_desc& conv) {
 }  // namespace
 
 bool dense_rs_supported(const pspml_op_desc& conv, const PreparedOp& p) {
-  if (conv.kind != PSPML_OP_CONV2D || conv.in_c != 32 || conv.out_c != 32 ||
-      conv.kernel_h != 3 || conv.kernel_w != 3 || conv.stride_h != 1 || conv.stride_w != 1)
+  if (conv.kind != PSPML_OP_CONV2D || conv.kernel_h != 3 || conv.kernel_w != 3 ||
+      conv.stride_h != 1 || conv.stride_w != 1)
     return false;
+  const bool shape = (conv.in_c == 32 && (conv.out_c == 32 || conv.out_c == 64)) ||
+                     (conv.in_c == 64 && conv.out_c == 64);
+  if (!shape) return false;
   if (p.path != OpPath::kTc4d || p.table == nullptr || !p.all_fast_known || p.ncls > 9)
     return false;
-  return rs_geometry_ok(dense_as_depthwise(conv));
+  pspml_op_desc g = dense_as_depthwise(conv);
+  g.in_c = g.out_c;  // the geometry check of the depthwise shapes
+  return rs_geometry_ok(g);
 }
 
-cudaError_t pack_conv32_rs(const int8_t* filter, uint8_t* out, cudaStream_t s) {
-  k_pack_conv32_rs<<<(9 * 1024 + 255) / 256, 256, 0, s>>>(filter, out);
+size_t conv_rs_packed_bytes(const pspml_op_desc& conv) {
+  return static_cast<size_t>(conv.out_c / 32) * (conv.in_c / 32) * 9 * 1024;
+}
+
+cudaError_t pack_conv_rs(const pspml_op_desc& conv, const int8_t* filter, uint8_t* out,
+                         cudaStream_t s) {
+  const int total = static_cast<int>(conv_rs_packed_bytes(conv));
+  k_pack_conv_rs<<<(total + 255) / 256, 256, 0, s>>>(filter, conv.in_c, conv.out_c, out);
   return cudaGetLastError();
 }
 
 cudaError_t launch_dense_rs(const pspml_op_desc& conv, const PreparedOp& p,
                             const uint8_t* wpack, int64_t batch, const int8_t* in, int8_t* out,
                             unsigned* dev_err, int num_sms, cudaStream_t s) {
+  const int N = conv.out_c;
+  if (p.table == nullptr || !p.all_fast_known || p.ncls > 9 || N > kDwTabC)
+    return cudaErrorInvalidValue;
+  static thread_local DwPwTable tab;
+  std::memset(&tab, 0, sizeof(tab));
+  for (int c = 0; c < N; ++c) {
+    tab.dw_mh[c] = p.table->mh[c];
+    tab.dw_bs[c] = p.table->bs[c];
+  }
+  for (int k = 0; k < p.ncls; ++k)
+    for (int c = 0; c < N; ++c) tab.dw_dbias[k * N + c] = p.table->dbias[k * N + c];
   PreparedOp q = p;
   q.wpack = reinterpret_cast<const uint32_t*>(wpack);
-  return launch_dwrs_dw(dense_as_depthwise(conv), q, batch, in, out, dev_err, num_sms, s);
+  const int64_t out_per = static_cast<int64_t>(conv.out_h) * conv.out_w * N;
+  return rs_run(dense_as_depthwise(conv), q, 0, nullptr, tab, 0, -128, 127, out_per, batch, in,
+                out, dev_err, num_sms, s);
 }
 
 }  // namespace pspml

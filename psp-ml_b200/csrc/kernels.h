@@ -261,12 +261,15 @@ cudaError_t launch_dwrs_pair(const pspml_op_desc& dw, const PreparedOp& pdw,
                              const DwPwTable& tab, int64_t batch, const int8_t* in, int8_t* out,
                              unsigned* dev_err, int num_sms, cudaStream_t s);
 
-// A 32 -> 32 channel 3x3 stride-1 conv prepared for the implicit GEMM
-// (kTc4d, constant table) run on the row-streaming kernel with dense
-// weight blocks (dwrs_tc.cu): every input row is loaded once instead of once
-// per filter tap.  pack_conv32_rs writes the 9216-byte packed weights.
+// A 3x3 stride-1 conv of 32 -> 32, 32 -> 64 or 64 -> 64 channels prepared
+// for the implicit GEMM (kTc4d, constant table) run on the row-streaming
+// kernel with dense weight blocks (dwrs_tc.cu): every input row is loaded
+// once instead of once per filter tap.  pack_conv_rs writes the
+// conv_rs_packed_bytes packed weights.
 bool dense_rs_supported(const pspml_op_desc& conv, const PreparedOp& p);
-cudaError_t pack_conv32_rs(const int8_t* filter, uint8_t* out, cudaStream_t s);
+size_t conv_rs_packed_bytes(const pspml_op_desc& conv);
+cudaError_t pack_conv_rs(const pspml_op_desc& conv, const int8_t* filter, uint8_t* out,
+                         cudaStream_t s);
 cudaError_t launch_dense_rs(const pspml_op_desc& conv, const PreparedOp& p,
                             const uint8_t* wpack, int64_t batch, const int8_t* in, int8_t* out,
                             unsigned* dev_err, int num_sms, cudaStream_t s);

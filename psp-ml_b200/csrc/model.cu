@@ -434,7 +434,7 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     }
   }
 
-  // 32 -> 32 channel 3x3 convs stream their input rows (each input row
+  // 3x3 convs of 32/64 channels stream their input rows (each input row
   // loaded once rather than once per filter tap); their max pool, if any,
   // then runs on its own.
   if (!st) {
@@ -442,11 +442,15 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     for (int i = 0; i < n_ops; ++i)
       if (dense_rs_supported(m->ops[i].d, m->ops[i].prep)) rs_ops.push_back(i);
     if (!rs_ops.empty()) {
-      st = cuda_status(cudaMalloc(&m->rs_weights, rs_ops.size() * 9216), "cudaMalloc(rs weights)");
+      size_t bytes = 0;
+      for (int i : rs_ops) bytes += align_up(conv_rs_packed_bytes(m->ops[i].d), 256);
+      st = cuda_status(cudaMalloc(&m->rs_weights, bytes), "cudaMalloc(rs weights)");
+      size_t off = 0;
       for (size_t k = 0; k < rs_ops.size() && !st; ++k) {
         ModelOp& op = m->ops[rs_ops[k]];
-        uint8_t* w = m->rs_weights + k * 9216;
-        st = cuda_status(pack_conv32_rs(op.prep.filter, w, ctx->stream), "pack conv weights");
+        uint8_t* w = m->rs_weights + off;
+        off += align_up(conv_rs_packed_bytes(op.d), 256);
+        st = cuda_status(pack_conv_rs(op.d, op.prep.filter, w, ctx->stream), "pack conv weights");
         op.rs_weights = w;
       }
       if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "pack conv weights");

@@ -49,7 +49,7 @@ struct ModelOp {
   // pool after it.
   int fuse = 0;
   bool pool_pair = false;
-  // A 32 -> 32 channel 3x3 conv run on the row-streaming kernel with these
+  // A 3x3 conv of 32/64 channels run on the row-streaming kernel with these
   // packed dense weights (dense_rs_supported).
   const uint8_t* rs_weights = nullptr;
   const pspml::DwPwTable* pair_table = nullptr;

@@ -80,7 +80,7 @@ def _run(ctx, oracle_mod, descs, blob, batch, micro, seed):
 
 @pytest.mark.parametrize("H,W,ci,co,batch", [
     (64, 64, 16, 32, 3),     # tiles of 16 x 8 pixels over 64-pixel rows
-    (32, 32, 64, 64, 5),     # stage 1
+    (32, 32, 64, 128, 5),    # 32-pixel rows
     (16, 16, 128, 128, 9),   # stage 2
     (8, 8, 256, 256, 17),    # stage 3 (two images per tile)
     (6, 6, 32, 48, 7),       # 8-pixel tile rows with two invalid columns; N = 48 in a 64 tile
@@ -119,18 +119,23 @@ def test_narrower_pool_clamp_is_not_fused(ctx, oracle_mod, ci):
     assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("H,W,zp_in,act", [
-    (64, 64, -128, "relu"),    # config 2's s0b shape
-    (48, 256, 0, "none"),      # two 128-pixel column tiles
-    (12, 20, 21, "relu"),
-    (7, 9, -128, "none"),      # odd sizes
+@pytest.mark.parametrize("H,W,ci,co,zp_in,act", [
+    (64, 64, 32, 32, -128, "relu"),   # config 2's s0b shape (two samples per tile)
+    (48, 256, 32, 32, 0, "none"),     # two 128-pixel column tiles
+    (12, 20, 32, 32, 21, "relu"),     # one sample per tile
+    (7, 9, 32, 32, -128, "none"),     # odd sizes
+    (32, 32, 32, 64, -128, "relu"),   # config 2's s1a shape (four samples per tile)
+    (32, 32, 64, 64, -128, "relu"),   # config 2's s1b shape
+    (20, 48, 32, 64, 9, "none"),      # two samples per tile
+    (9, 100, 64, 64, 0, "relu"),      # one sample per tile, odd height
+    (5, 17, 64, 64, -7, "none"),
 ])
-def test_row_streamed_32_channel_conv(ctx, oracle_mod, H, W, zp_in, act):
-    """A 32 -> 32 channel 3x3 stride-1 conv runs on the row-streaming kernel
-    with dense weight blocks (each input row loaded once); a max pool after
-    it then runs on its own."""
+def test_row_streamed_dense_conv(ctx, oracle_mod, H, W, ci, co, zp_in, act):
+    """3x3 stride-1 convs of 32 -> 32, 32 -> 64 and 64 -> 64 channels run on
+    the row-streaming kernel with dense weight blocks (each input row loaded
+    once); a max pool after one then runs on its own."""
     conv_act, zp_out = ((-3, 127), -3) if act == "relu" else ((-128, 127), 5)
-    descs, blob = _model_parts(H, W, 32, 32, zp_in, zp_out, conv_act, (-128, 127), H + W)
+    descs, blob = _model_parts(H, W, ci, co, zp_in, zp_out, conv_act, (-128, 127), H + W + ci)
     if H % 2 or W % 2:
         descs = descs[:1].copy()  # the conv alone
     fused, got, want = _run_chain(ctx, oracle_mod, descs, blob, 5, 5, 4)

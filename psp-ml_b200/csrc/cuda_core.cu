@@ -567,13 +567,14 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
         for (int w4 = 0; w4 < NW4; ++w4) {
           const uint4 wv = sw[c4 * 4 + j][w4];
+          const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
           for (int sub = 0; sub < 4; ++sub) {
             int32_t acc = a[sub][j];
-            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 0]), static_cast<int>(wv.x), acc);
-            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 1]), static_cast<int>(wv.y), acc);
-            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 2]), static_cast<int>(wv.z), acc);
-            acc = __dp4a(static_cast<int>(x[sub][4 * w4 + 3]), static_cast<int>(wv.w), acc);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)  // the patch's padding words are zero: skipped
+              if (4 * w4 + q < NW)
+                acc = __dp4a(static_cast<int>(x[sub][4 * w4 + q]), static_cast<int>(wq[q]), acc);
             a[sub][j] = acc;
           }
         }

@@ -87,6 +87,12 @@ struct TcGemmArgs {
   // l ^ bw ^ 1 of one epilogue warp.
   int32_t pool;
   int32_t Hp, Wp;
+  // kEpiConvStatic: bytes of shared memory holding the border-class bias
+  // differences, rows of BN + 1 words (0: no border classes).  Lanes of one
+  // warp hold pixels of up to nine classes; read from the constant bank at
+  // per-lane offsets those loads serialise, from shared memory the padded
+  // rows put each class on its own bank.
+  int32_t dbias_smem;
 };
 
 // Signed byte-wise max of a 16-byte chunk with the same chunk of lane ^ m.
@@ -321,27 +327,32 @@ __device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_
 // operand, no load): the run-time-offset loop of kEpiTable loads two table
 // words per output.  Tensor-memory loads run one 16-column chunk ahead.
 // `border`: the pixel's class is not the table's base class (its bias
-// difference is added from dbias[cls_off + channel]).  POOL: the 2x2 max
+// differences are drow[channel], the class's row in shared memory).  POOL: the 2x2 max
 // over lanes l, l ^ 1, l ^ vert (see the pooled branch of the kernel); the
 // window's top-left lane stores the pooled chunk at `orow`.  Q: the op's
 // ep_flags.
 template <int BN, int Q, bool POOL>
 __device__ __forceinline__ void epilogue_row_conv(const EpiTable& tab, uint32_t taddr,
                                                   int8_t* orow, bool store, bool border,
-                                                  int cls_off, int vert, const TcGemmArgs& p) {
+                                                  const int32_t* drow, int vert,
+                                                  const TcGemmArgs& p) {
   uint32_t v0[16], v1[16];
   tmem_ld16_nowait(taddr, v0);
 #pragma unroll
   for (int c = 0; c < BN; c += 32) {
     tmem_wait_ld(v0);
     tmem_ld16_nowait(taddr + c + 16, v1);
-    if (border) add_class_delta(v0, tab, cls_off + c, 16);
+    if (border)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v0[j] += static_cast<uint32_t>(drow[c + j]);
     uint4 w0 = requant16_tab<Q>(v0, tab, c, p.lo4, p.hi4);
     if constexpr (POOL) w0 = vmax_xor(vmax_xor(w0, 1), vert);
     if (store) store16(orow + c, w0);
     tmem_wait_ld(v1);
     if (c + 32 < BN) tmem_ld16_nowait(taddr + c + 32, v0);
-    if (border) add_class_delta(v1, tab, cls_off + c + 16, 16);
+    if (border)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v1[j] += static_cast<uint32_t>(drow[c + 16 + j]);
     uint4 w1 = requant16_tab<Q>(v1, tab, c + 16, p.lo4, p.hi4);
     if constexpr (POOL) w1 = vmax_xor(vmax_xor(w1, 1), vert);
     if (store) store16(orow + c + 16, w1);
@@ -373,7 +384,8 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
   uint8_t* sP = sB + (p.b_res ? kiters : stages * grp) * B_BYTES;  // staged requant + bias tables
   RqChannel* srq = reinterpret_cast<RqChannel*>(sP);
   int32_t* sbias = reinterpret_cast<int32_t*>(sP + static_cast<size_t>(p.N) * sizeof(RqChannel));
-  uint64_t* full = reinterpret_cast<uint64_t*>(sP + p.param_smem);
+  int32_t* sdb = reinterpret_cast<int32_t*>(sP + p.param_smem);  // [ncls][BN + 1]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sP + p.param_smem + p.dbias_smem);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + NB;
@@ -410,6 +422,11 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
   if (p.param_smem) {
     for (int i = threadIdx.x; i < p.N; i += blockDim.x) srq[i] = p.rq[i];
     for (int i = threadIdx.x; i < p.ncls * p.N; i += blockDim.x) sbias[i] = p.bias[i];
+  }
+  if constexpr (MODE == kEpiConvStatic) {
+    if (p.dbias_smem)
+      for (int i = threadIdx.x; i < p.ncls * BN; i += blockDim.x)
+        sdb[(i / BN) * (BN + 1) + i % BN] = tab.dbias[i];
   }
   tc_fence_before();
   __syncthreads();
@@ -666,21 +683,21 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
         const int32_t y = o.y0 + ((row >> p.bw_log2) & ((1 << p.bh_log2) - 1));
         const int64_t n = o.n0 + (row >> (p.bw_log2 + p.bh_log2));
         const bool valid = x < p.Wo && y < p.Ho && n < p.nimg;
-        int cls_off = 0;
+        const int32_t* drow = sdb;
         bool border = false;
         if (valid && p.ycls != nullptr) {
           const int cls = p.ycls[y] * p.n_xcls + p.xcls[x];
-          cls_off = cls * BN;
+          drow = sdb + cls * (BN + 1);
           border = cls != p.base_cls;
         }
         if (p.pool) {
           int8_t* prow =
               p.out + ((n * p.Hp + (y >> 1)) * p.Wp + (x >> 1)) * static_cast<int64_t>(BN);
           epilogue_row_conv<BN, Q, true>(tab, tb0, prow, valid && ((x | y) & 1) == 0, border,
-                                         cls_off, 1 << p.bw_log2, p);
+                                         drow, 1 << p.bw_log2, p);
         } else {
           int8_t* orow = p.out + ((n * p.Ho + y) * p.Wo + x) * static_cast<int64_t>(BN);
-          epilogue_row_conv<BN, Q, false>(tab, tb0, orow, valid, border, cls_off, 0, p);
+          epilogue_row_conv<BN, Q, false>(tab, tb0, orow, valid, border, drow, 0, p);
         }
       } else {
 #pragma unroll 1
@@ -881,7 +898,14 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
   const bool fixed_n = grid % args.tiles_n == 0 || grid == args.tiles_total;
   const int kiters = args.taps * args.kblocks;
   const int bres_bytes = kiters * BN * BK;
-  const int base_overhead = 1024 + 64 * 8 + 64 + args.param_smem;
+  // The conv epilogue with compile-time table offsets (N == BN, one N tile)
+  // stages the border-class bias differences in shared memory.
+  const bool conv_static = MT == 1 && table != nullptr && args.conv4d && args.tiles_n == 1 &&
+                           args.N == BN;
+  args.dbias_smem = conv_static && args.ycls != nullptr
+                        ? (args.ncls * (BN + 1) * 4 + 15) / 16 * 16
+                        : 0;
+  const int base_overhead = 1024 + 64 * 8 + 64 + args.param_smem + args.dbias_smem;
   args.b_res = fixed_n && base_overhead + bres_bytes + 4 * A_BYTES <= kSmemLimit;
   const int iter_bytes = args.b_res ? A_BYTES : A_BYTES + BN * BK;
   const int overhead = base_overhead + (args.b_res ? bres_bytes : 0);

@@ -11,10 +11,16 @@
 // layout), and every input row is loaded once.
 //
 // Stride 1: an input row feeds three output rows; accumulators sit in a
-// ring of three 32-column tensor-memory blocks per group (row r in block
-// r % 3).  Which weight block meets which accumulator block rotates with
-// y % 3, so the weights of each kx are kept as five ky blocks [2 1 0 2 1]
-// and the MMA takes the three-block window that starts at (1, 0, 2)[y % 3].
+// ring of R 32-column tensor-memory blocks per group (row r in block r % R).
+// R = 4 for the depthwise (or dense) conv alone: the block a new row takes
+// was freed by the row completed two input rows earlier, so the MMA thread
+// runs a row ahead of the epilogue; an input row's blocks form one or two
+// runs of consecutive blocks, one MMA per run against a window of the
+// weights kept as ky blocks [2 1 0].  R = 3 for the fused pair: the three
+// blocks are always all live, which weight block meets which accumulator
+// block rotates with y % 3, so the weights of each kx are kept as five ky
+// blocks [2 1 0 2 1] and the MMA takes the three-block window that starts
+// at (1, 0, 2)[y % 3].
 // Stride 2: an input row feeds one (ky = 1) or two (ky = 2 and 0) output
 // rows; a ring of two blocks, weights as [2 0 2 1].  The input is viewed as
 // [C][2][W/2][H][N] so that one box holds the even and another the odd
@@ -68,10 +74,10 @@ namespace pspml {
 
 namespace {
 
-constexpr int kRsRegion = 2176;  // one input box of 16 channels: up to 130 px x 16 B, padded
 constexpr int kRsSmemLimit = 232448;
 constexpr int kRsMaxStages = 8;
 constexpr int kRsMaxSets = 4;
+constexpr int kRsMaxRing = 4;  // accumulator blocks per group
 
 struct RsArgs {
   int32_t strips;  // batch * tiles_x, or batch / P rounded up (per channel block)
@@ -100,8 +106,8 @@ struct RsArgs {
 struct RsBars {
   uint64_t in_full[kRsMaxStages];
   uint64_t in_empty[kRsMaxStages];
-  uint64_t dw_full[kRsMaxSets * 3];  // MMA -> set: row complete, [set][block]
-  uint64_t dw_free[3];               // set -> MMA: block read and zeroed
+  uint64_t dw_full[kRsMaxSets * kRsMaxRing];  // MMA -> set: row complete, [set][block]
+  uint64_t dw_free[kRsMaxRing];               // set -> MMA: block read and zeroed
   uint64_t apw_full[kRsMaxSets];     // set -> MMA: its pointwise A tile written
   uint64_t pw_full[kRsMaxSets];      // MMA -> set: its row's pointwise accumulator complete
   uint64_t pw_empty;                 // set -> MMA: pointwise accumulator read
@@ -121,19 +127,39 @@ struct RsShape {
   static constexpr int NS = 2;
   static constexpr int RS = 2;
   static constexpr int C = CG * 32;                    // channels of a strip
-  static constexpr int R = S == 1 ? 3 : 2;             // accumulator ring blocks
-  static constexpr int NBB = S == 1 ? 5 : 4;           // weight blocks per kx
+  // Accumulator ring blocks.  Stride 1: an input row reaches three output
+  // rows; with four blocks (the depthwise or dense conv alone) the block a
+  // new row takes was read one input row earlier, so the MMAs of one row
+  // never wait for the epilogue of the row completed just before.  The
+  // fused pair keeps three (its pointwise accumulator needs the rest).
+  static constexpr int R = S == 1 ? (NPW == 0 ? 4 : 3) : 2;
+  static constexpr int NBB = S == 1 ? (R == 4 ? 3 : 5) : 4;  // weight blocks per kx
   static constexpr int kHalf = NBB * 32 * 16;          // one K-half of a kx's weights
   static constexpr int kTap = 2 * kHalf;               // weights of one (group, kx)
   static constexpr int Wt = 128 / P;                   // tile columns per sample
-  // One box per 16 channels and row (stride 1), an even and an odd box
-  // (stride 2), or with packed samples one box per tap kx, each already
-  // shifted by its tap (a 16-byte move of the descriptor would cross into
-  // the next sample's pixels).
-  static constexpr int kBoxes = P > 1 ? 3 : (S == 1 ? 1 : 2);
-  static constexpr int kRegion = P > 1 ? 128 * 16 : kRsRegion;
+  // TMA boxes per input row: one (stride 1), an even and an odd one
+  // (stride 2), or with packed samples one per tap kx, each already shifted
+  // by its tap (a 16-byte move of the descriptor would cross into the next
+  // sample's pixels).  Full rows: a box holds every 16-channel chunk of the
+  // row's input groups as [chunk][pixel][16 B] (the K-major A layout
+  // without swizzle, one chunk per K-half).  Packed samples: a box is
+  // [sample][pixel][32 B per input group] in the 32- or 64-byte swizzled
+  // K-major layout (group gi's MMA starts 32 B into the swizzle row), so
+  // the copy moves whole 32-byte sectors: 16-byte rows cost one L2 request
+  // and a 32-byte sector each.
   static constexpr int GIN = GI > 0 ? GI : CG;        // input groups per row
-  static constexpr int kInRow = GIN * 2 * kBoxes * kRegion;
+  static constexpr bool kSwz = P > 1;
+  static constexpr int kBoxes = P > 1 ? 3 : (S == 1 ? 1 : 2);
+  static constexpr int kBoxPx = P > 1 ? 128 : (S == 1 ? 130 : 129);  // pixels per chunk
+  static constexpr int kRegion = kBoxPx * 16;         // one chunk: the K-half stride
+  static constexpr int kBoxBytes = GIN * 2 * kRegion;
+  // Swizzled boxes start on 1024-byte boundaries, the others on 128.
+  static constexpr int kBoxStride =
+      kSwz ? (kBoxBytes + 1023) / 1024 * 1024 : (kBoxBytes + 127) / 128 * 128;
+  static constexpr uint32_t kALayout = !kSwz ? 0u : (GIN == 1 ? 6u : 4u);  // none, 32B, 64B
+  static constexpr uint32_t kALbo = kSwz ? 16u : static_cast<uint32_t>(kRegion);
+  static constexpr uint32_t kASbo = kSwz ? 256u * GIN : 128u;  // between 8-row groups
+  static constexpr int kInRow = kBoxes * kBoxStride;
   static constexpr int kApw = NPW > 0 ? 128 * C : 0;
   static constexpr int kSlotCols = 512 / NS;
   static constexpr int kThreads = 128 + NS * RS * 128;
@@ -146,12 +172,16 @@ struct RsShape {
                 "packed samples are for a stride-1 depthwise conv alone");
   static_assert(NPW == 0 || S == 1, "fused pointwise after a stride-1 depthwise conv");
   static_assert(RS <= kRsMaxSets, "epilogue sets");
+  static_assert(R <= kRsMaxRing, "accumulator ring");
   static_assert(GI == 0 || (NCB == 1 && NPW == 0), "dense conv: one channel block, no pair");
 };
 
-// Weight block order per kx: ky of each 32-row block.
-__host__ __device__ constexpr int rs_block_ky(int S, int blk) {
-  return S == 1 ? (blk == 2 ? 0 : ((blk == 1 || blk == 4) ? 1 : 2))
+// Weight block order per kx: ky of each 32-row block.  Stride 1, 3-block
+// ring: [2 1 0 2 1] (every rotation of [2 1 0] is a window); 4-block ring:
+// [2 1 0] (a run of consecutive blocks holds consecutive rows, so its
+// windows are pieces of [2 1 0]); stride 2: [2 0 2 1].
+__host__ __device__ constexpr int rs_block_ky(int S, int nbb, int blk) {
+  return S == 1 ? (nbb == 3 ? 2 - blk : (blk == 2 ? 0 : ((blk == 1 || blk == 4) ? 1 : 2)))
                 : (blk == 1 ? 0 : (blk == 3 ? 1 : 2));
 }
 
@@ -284,7 +314,8 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
     for (int r = 0; r < Ho; ++r, ++g) {
       if (static_cast<int>(g % RS) != set) continue;
       const int rb = r % R;
-      if (!warp_wait(&bars.dw_full[set * 3 + rb], (full_ph >> rb) & 1u, abort_flag, lane)) {
+      if (!warp_wait(&bars.dw_full[set * kRsMaxRing + rb], (full_ph >> rb) & 1u, abort_flag,
+                     lane)) {
         if (lane == 0) rs_record_error(p.err, abort_flag, kDevErrEpiWait);
         return;
       }
@@ -384,7 +415,6 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
     k_dwrs_s8(const __grid_constant__ CUtensorMap tmIn, const RsArgs p,
               const __grid_constant__ DwPwTable tab) {
   using Sh = RsShape<CG, NPW, S, NCB, P, GI>;
-  constexpr int GIN = Sh::GIN;
   static_assert(Sh::Wt * P == 128, "tile rows");
   constexpr int C = Sh::C;
   constexpr int NS = Sh::NS;
@@ -399,7 +429,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
   uint8_t* sBdw = smem;
   uint8_t* sBpw = sBdw + Sh::kBdw;
   uint8_t* sApw = sBpw + NPW * C;             // [slot][set][C/16][128][16]
-  uint8_t* sIn = sApw + NS * RS * Sh::kApw;   // [slot][stage][group][box][half][kRsRegion]
+  uint8_t* sIn = sApw + NS * RS * Sh::kApw;   // [slot][stage][box][group][half][kRegion]
   RsBars* bars = reinterpret_cast<RsBars*>(sIn + NS * stages * Sh::kInRow);
   uint64_t* mma_done = reinterpret_cast<uint64_t*>(bars + NS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + NS);
@@ -423,7 +453,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
       t /= 2;
       const int kx = t % 3;
       const int gg = t / 3;
-      const int ky = rs_block_ky(S, blk);
+      const int ky = rs_block_ky(S, NBB, blk);
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(
           p.wdw + ((cb * CG + gg) * 9 + ky * 3 + kx) * 1024 + h * 512 + rr * 16));
       *reinterpret_cast<uint4*>(sBdw + (gg * 3 + kx) * Sh::kTap + h * Sh::kHalf +
@@ -443,8 +473,8 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
         mbar_init(&b.in_full[s], 1);
         mbar_init(&b.in_empty[s], 1);
       }
-      for (int j = 0; j < RS * 3; ++j) mbar_init(&b.dw_full[j], 1);
-      for (int j = 0; j < 3; ++j) mbar_init(&b.dw_free[j], 4);
+      for (int j = 0; j < RS * kRsMaxRing; ++j) mbar_init(&b.dw_full[j], 1);
+      for (int j = 0; j < kRsMaxRing; ++j) mbar_init(&b.dw_free[j], 4);
       for (int j = 0; j < RS; ++j) {
         mbar_init(&b.apw_full[j], 4);
         mbar_init(&b.pw_full[j], 1);
@@ -489,44 +519,32 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
             break;
           }
           uint8_t* a = in_k + s * Sh::kInRow;
+          // Full rows: stride-1 view [16 ch][W][N][C/16 chunks][H], stride-2 view
+          // [16 ch][W/2 pairs][C/16 chunks][parity][H*N] (rows are always
+          // inside the image, so rows and samples merge into one dimension).
+          const int chunk0 = c0 / 16;
           if constexpr (P > 1) {
-            // Per tap kx a box of Wt pixels per sample, already shifted.
-            mbar_arrive_expect_tx(&b.in_full[s], GIN * 3 * 2 * P * 16 * Sh::Wt);
+            // Per tap kx one box of Wt pixels x P samples, already shifted
+            // (view [C][W][N][H], box {32 x groups, Wt, P, 1}).
+            mbar_arrive_expect_tx(&b.in_full[s], 3 * Sh::kBoxBytes);
 #pragma unroll
-            for (int gq = 0; gq < GIN; ++gq)
-#pragma unroll
-              for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                  for (int pm = 0; pm < P; ++pm) {
-                    uint8_t* dst = a + ((gq * 3 + kx) * 2 + h) * Sh::kRegion + pm * Sh::Wt * 16;
-                    tma_load_4d(dst, &tmIn, &b.in_full[s], c0 + gq * 32 + h * 16, kx - p.pad_l,
-                                y, static_cast<int>(st.n) + pm);
-                  }
+            for (int kx = 0; kx < 3; ++kx)
+              tma_load_4d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0, kx - p.pad_l,
+                          static_cast<int>(st.n), y);
           } else if constexpr (S == 1) {
-            mbar_arrive_expect_tx(&b.in_full[s], GIN * 2 * 16 * 130);
-            const int x0 = st.tx * 128 - p.pad_l;
-#pragma unroll
-            for (int gq = 0; gq < GIN; ++gq)
-#pragma unroll
-              for (int h = 0; h < 2; ++h)
-                tma_load_4d(a + (gq * 2 + h) * kRsRegion, &tmIn, &b.in_full[s],
-                            c0 + gq * 32 + h * 16, x0, y, static_cast<int>(st.n));
+            mbar_arrive_expect_tx(&b.in_full[s], Sh::kBoxBytes);
+            tma_load_5d(a, &tmIn, &b.in_full[s], 0, st.tx * 128 - p.pad_l,
+                        static_cast<int>(st.n), chunk0, y);
           } else {
             // Even pixels 2j (j from the tile's first output) and odd
             // pixels 2j+1 (from one pair earlier with a left pad).
-            mbar_arrive_expect_tx(&b.in_full[s], GIN * 2 * 2 * 16 * 129);
+            mbar_arrive_expect_tx(&b.in_full[s], 2 * Sh::kBoxBytes);
             const int j0 = st.tx * 128;
+            const int yr = static_cast<int>(st.n) * Hin + y;
 #pragma unroll
-            for (int gq = 0; gq < GIN; ++gq)
-#pragma unroll
-              for (int eo = 0; eo < 2; ++eo)
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                  tma_load_5d(a + ((gq * 2 + eo) * 2 + h) * kRsRegion, &tmIn, &b.in_full[s],
-                              c0 + gq * 32 + h * 16, eo, j0 - (eo == 1 ? p.pad_l : 0), y,
-                              static_cast<int>(st.n));
+            for (int eo = 0; eo < 2; ++eo)
+              tma_load_5d(a + eo * Sh::kBoxStride, &tmIn, &b.in_full[s], 0,
+                          j0 - (eo == 1 ? p.pad_l : 0), chunk0, eo, yr);
           }
           ++issued;
           if (++s == stages) {
@@ -584,22 +602,23 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
       // Descriptor templates: an operand's descriptor differs from these only
       // in the start-address field (address >> 4, below 2^14 for shared
       // memory), so each MMA adds an offset to one 64-bit value.
-      const uint64_t adesc0 = make_sdesc(in0, Sh::kRegion, 128, 0);
+      const uint64_t adesc0 = make_sdesc(in0, Sh::kALbo, Sh::kASbo, Sh::kALayout);
       const uint64_t bdesc_smem = make_sdesc(smem_u32(sBdw), Sh::kHalf, 128, 0);
       uint32_t aoff[3];  // A start of tap kx within a stage, group 0 (16-byte units)
 #pragma unroll
       for (int kx = 0; kx < 3; ++kx) {
         if constexpr (P > 1) {
-          aoff[kx] = static_cast<uint32_t>((kx * 2 * Sh::kRegion) / 16);
+          aoff[kx] = static_cast<uint32_t>((kx * Sh::kBoxStride) / 16);
         } else if constexpr (S == 1) {
           aoff[kx] = static_cast<uint32_t>(kx);
         } else {
           // pad 0: kx 0 even+0, 1 odd+0, 2 even+16; pad 1: odd+0, even+0, odd+16.
           const int eo = ((kx == 1) ? 1 : 0) ^ pt;
-          aoff[kx] = static_cast<uint32_t>((eo * 2 * kRsRegion) / 16 + (kx == 2 ? 1 : 0));
+          aoff[kx] = static_cast<uint32_t>((eo * Sh::kBoxStride) / 16 + (kx == 2 ? 1 : 0));
         }
       }
-      constexpr uint32_t kGroupA = (2 * Sh::kBoxes * Sh::kRegion) / 16;
+      // Input group stride in a box (16-byte units).
+      constexpr uint32_t kGroupA = Sh::kSwz ? 2u : (2 * Sh::kRegion) / 16;
       const uint32_t idesc1 = make_idesc_s8(128, 32);
       const uint32_t idesc2 = make_idesc_s8(128, 64);
       const uint32_t idesc3 = make_idesc_s8(128, 96);
@@ -647,7 +666,11 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
             int j1 = j + 1;
             while (j1 < R && ((live >> j1) & 1u) != 0) ++j1;
             const uint32_t idesc = j1 - j == 1 ? idesc1 : (j1 - j == 2 ? idesc2 : idesc3);
-            const uint64_t bwin = bdesc0 + static_cast<uint64_t>((o + j) * 32);
+            // Weight window of the run: its first block j holds row
+            // nc + (j - nc_blk) mod R, whose tap is ky = y + pt - row.
+            int wb = o + j;
+            if constexpr (R == 4) wb = 2 - (y + pt - (nc + ((j - nc_blk + R) & 3)));
+            const uint64_t bwin = bdesc0 + static_cast<uint64_t>(wb * 32);
             if constexpr (GI == 0) {
 #pragma unroll
               for (int gq = 0; gq < CG; ++gq) {
@@ -683,7 +706,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
           // Rows whose last input row this is are complete.
           while (nc < Ho && (S * nc - pt + 2 <= y || y == Hin - 1)) {
             const uint32_t gr = gbase + static_cast<uint32_t>(nc);
-            umma_commit(&b.dw_full[(gr % RS) * 3 + nc_blk]);
+            umma_commit(&b.dw_full[(gr % RS) * kRsMaxRing + nc_blk]);
             ++nc;
             if (++nc_blk == R) nc_blk = 0;
           }
@@ -907,26 +930,40 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
   a.err = dev_err;
   const int dwq = ep_flags(dw.act_min, dw.act_max, dw.zp_out);
 
+  // Full rows: views whose boxes hold every 16-channel chunk of a row's
+  // input groups (the chunk is a dimension of stride 16 bytes):
+  //   stride 1: [16 ch][W][N][C/16][H], box {16, 130, 1, chunks, 1}
+  //   stride 2: [16 ch][W/2][C/16][parity][H*N], box {16, 129, chunks, 1, 1}
+  // chunks = 2 x the input groups of a strip (the depthwise channel block,
+  // or every input channel of a dense conv).
+  const int gin = (dw.flags & kRsDenseFlag) != 0 ? C / 32 : (C == 32 ? 1 : 2);
+  const uint32_t chunks = static_cast<uint32_t>(2 * gin);
+  const uint64_t W = static_cast<uint64_t>(dw.in_w), H = static_cast<uint64_t>(dw.in_h);
+  const uint64_t Cu = static_cast<uint64_t>(C);
   CUtensorMap m;
-  if (S == 1) {
-    const uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(dw.in_w),
-                              static_cast<uint64_t>(dw.in_h), static_cast<uint64_t>(batch)};
-    const uint64_t strides[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(dw.in_w) * C,
-                                 static_cast<uint64_t>(dw.in_h) * dw.in_w * C};
-    const uint32_t box[4] = {16, P > 1 ? static_cast<uint32_t>(128 / P) : 130u, 1, 1};
-    const uint32_t estr[4] = {1, 1, 1, 1};
-    if (encode_tensor_map(&m, in, 4, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+  const uint32_t estr[5] = {1, 1, 1, 1, 1};
+  if (S == 1 && P > 1) {
+    // Packed samples: [C][W][N][H], box {32 x groups, 128/P, P, 1}, 32- or
+    // 64-byte swizzle.
+    const uint64_t dims[4] = {Cu, W, static_cast<uint64_t>(batch), H};
+    const uint64_t strides[3] = {Cu, H * W * Cu, W * Cu};
+    const uint32_t box[4] = {16 * chunks, static_cast<uint32_t>(128 / P),
+                             static_cast<uint32_t>(P), 1};
+    if (encode_tensor_map(&m, in, 4, dims, strides, box, estr,
+                          gin == 1 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B) !=
+        CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  } else if (S == 1) {
+    const uint64_t dims[5] = {16, W, static_cast<uint64_t>(batch), Cu / 16, H};
+    const uint64_t strides[4] = {Cu, H * W * Cu, 16, W * Cu};
+    const uint32_t box[5] = {16, 130, 1, chunks, 1};
+    if (encode_tensor_map(&m, in, 5, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   } else {
-    // [C][parity][W/2][H][N]: pixel 2j + parity.
-    const uint64_t dims[5] = {static_cast<uint64_t>(C), 2, static_cast<uint64_t>(dw.in_w / 2),
-                              static_cast<uint64_t>(dw.in_h), static_cast<uint64_t>(batch)};
-    const uint64_t strides[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(C) * 2,
-                                 static_cast<uint64_t>(dw.in_w) * C,
-                                 static_cast<uint64_t>(dw.in_h) * dw.in_w * C};
-    const uint32_t box[5] = {16, 1, 129, 1, 1};
-    const uint32_t estr[5] = {1, 1, 1, 1, 1};
+    const uint64_t dims[5] = {16, W / 2, Cu / 16, 2, H * static_cast<uint64_t>(batch)};
+    const uint64_t strides[4] = {2 * Cu, 16, Cu, W * Cu};
+    const uint32_t box[5] = {16, 129, chunks, 1, 1};
     if (encode_tensor_map(&m, in, 5, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;

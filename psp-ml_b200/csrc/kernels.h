@@ -274,6 +274,16 @@ cudaError_t launch_dense_rs(const pspml_op_desc& conv, const PreparedOp& p,
                             const uint8_t* wpack, int64_t batch, const int8_t* in, int8_t* out,
                             unsigned* dev_err, int num_sms, cudaStream_t s);
 
+// 3x3 convs with 1, 2, 3, 4 or 8 input channels and 16, 32 or 64 outputs
+// on the tensor cores (im2col_tc.cu): patches gathered into a shared-memory
+// A tile per 128 output pixels, requantised from tensor memory with the
+// op's constant table.
+bool im2col_conv_supported(const pspml_op_desc& d, const PreparedOp& p, const int8_t* in,
+                           const int8_t* out);
+cudaError_t launch_im2col_conv(const pspml_op_desc& d, const PreparedOp& p, int64_t batch,
+                               const int8_t* in, int8_t* out, unsigned* dev_err, int num_sms,
+                               cudaStream_t s);
+
 // Path for op `d` given operand alignment (16-byte aligned pointers allow the
 // TMA / vector paths).
 OpPath choose_path(const pspml_op_desc& d, bool aligned16);

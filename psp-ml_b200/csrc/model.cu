@@ -304,8 +304,8 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
   for (int i = 0; i < n_ops && !st; ++i) {
     PreparedOp& p = m->ops[i].prep;
     const int n = m->ops[i].d.out_c;
-    const bool tc =
-        p.path == OpPath::kTc2d || p.path == OpPath::kTc4d || p.path == OpPath::kDwTc;
+    const bool tc = p.path == OpPath::kTc2d || p.path == OpPath::kTc4d ||
+                    p.path == OpPath::kDwTc || p.path == OpPath::kSmallConv;
     if (!tc || !p.all_fast_known || n > kTabRq || (p.ncls > 1 && p.ncls * n > kTabDelta))
       continue;
     std::vector<RqChannel> rq(n);

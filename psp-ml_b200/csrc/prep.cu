@@ -379,6 +379,8 @@ cudaError_t launch_op(const pspml_op_desc& d, const PreparedOp& p, int64_t batch
     case OpPath::kTc4d:
       return launch_tc_gemm(d, p, batch, in, out, dev_err, num_sms, s);
     case OpPath::kSmallConv:
+      if (im2col_conv_supported(d, p, in, out))
+        return launch_im2col_conv(d, p, batch, in, out, dev_err, num_sms, s);
       return launch_small_conv(d, p, batch, in, out, s);
     case OpPath::kDirect:
       return launch_conv_direct(d, p, batch, in, out, s);

@@ -226,6 +226,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// 16 lanes x 16 columns (two 16x256b blocks) from lane field of taddr on,
+// waited: the warp-wide fragment of the m16n8 accumulator layout, per
+// 8-column block b (registers 4b .. 4b+3) thread t holds lane t/4 at
+// columns 2(t%4) and 2(t%4)+1, then lane t/4 + 8 at the same columns.
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+}
+
 // 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(

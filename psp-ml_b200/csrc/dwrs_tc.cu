@@ -122,7 +122,7 @@ struct RsBars {
 // GI: 0 for the depthwise conv; for a dense 3x3 conv the number of
 // 32-channel input groups (every output group then accumulates every input
 // group: weights [output group][input group][tap]).
-template <int CG, int NPW, int S, int NCB, int P, int GI = 0>
+template <int CG, int NPW, int S, int NCB, int P, int GI = 0, int POOL = 0>
 struct RsShape {
   static constexpr int NS = 2;
   static constexpr int RS = 2;
@@ -160,7 +160,9 @@ struct RsShape {
   static constexpr uint32_t kALbo = kSwz ? 16u : static_cast<uint32_t>(kRegion);
   static constexpr uint32_t kASbo = kSwz ? 256u * GIN : 128u;  // between 8-row groups
   static constexpr int kInRow = kBoxes * kBoxStride;
-  static constexpr int kApw = NPW > 0 ? 128 * C : 0;
+  // Per (slot, set): the pointwise A tile, or with the pool the window's
+  // first row (both [C/16][128 rows][16 B]).
+  static constexpr int kApw = NPW > 0 || POOL != 0 ? 128 * C : 0;
   static constexpr int kSlotCols = 512 / NS;
   static constexpr int kThreads = 128 + NS * RS * 128;
   static_assert(CG * R * 32 + NPW <= kSlotCols, "tensor memory per slot");
@@ -174,6 +176,7 @@ struct RsShape {
   static_assert(RS <= kRsMaxSets, "epilogue sets");
   static_assert(R <= kRsMaxRing, "accumulator ring");
   static_assert(GI == 0 || (NCB == 1 && NPW == 0), "dense conv: one channel block, no pair");
+  static_assert(POOL == 0 || (NPW == 0 && NCB == 1 && S == 1), "pool after a dense conv");
 };
 
 // Weight block order per kx: ky of each 32-row block.  Stride 1, 3-block
@@ -256,11 +259,11 @@ __device__ __forceinline__ void rs_strip_range(int ncb, int k, int ns, int* firs
 // Epilogue of one warp: set `set` of slot `k`, lane quarter q, every
 // channel of the strip.  All epilogue warps of a kernel run this one code
 // path.
-template <int CG, int NPW, int S, int NCB, int P, int CB, int DWQ, int PWQ>
+template <int CG, int NPW, int S, int NCB, int P, int CB, int DWQ, int PWQ, int GI, int POOL>
 __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& tab, RsBars& bars,
                                             uint8_t* sA, uint32_t tm_slot, int k, int set, int q,
                                             int lane, volatile int* abort_flag) {
-  using Sh = RsShape<CG, NPW, S, NCB, P>;
+  using Sh = RsShape<CG, NPW, S, NCB, P, GI, POOL>;
   constexpr int C = Sh::C;
   constexpr int R = Sh::R;
   constexpr int RS = Sh::RS;
@@ -312,7 +315,9 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
     }
     const int64_t pix0 = (static_cast<int64_t>(n) * Ho) * p.Wo + x;
     for (int r = 0; r < Ho; ++r, ++g) {
-      if (static_cast<int>(g % RS) != set) continue;
+      // With the pool, a set takes output rows in pairs (both rows of a
+      // pooling window).
+      if (static_cast<int>((POOL ? g >> 1 : g) % RS) != set) continue;
       const int rb = r % R;
       if (!warp_wait(&bars.dw_full[set * kRsMaxRing + rb], (full_ph >> rb) & 1u, abort_flag,
                      lane)) {
@@ -385,6 +390,56 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
                          rs_requant16<PWQ>(u[h + 1], tab.pw_mh, tab.pw_bs, h * 16 + 16,
                                            p.pw_lo4, p.pw_hi4));
         }
+      } else if constexpr (POOL != 0) {
+        // 2x2 max pool: every lane requantises its pixel (the window's
+        // other column is lane row ^ 1, its other row the set's previous
+        // row), even columns of odd rows store the window's maximum.
+        if (valid) {
+          const int cls = r == 0 ? cls_top : (r == Ho - 1 ? cls_bot : cls_mid);
+          if (cls != p.base_cls) {
+            const int off = cls * Cop + cbase;
+#pragma unroll
+            for (int h = 0; h < NV; ++h)
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                v[h][j] += static_cast<uint32_t>(tab.dw_dbias[off + h * 16 + j]);
+          }
+        }
+        const int2* mh = tab.dw_mh + cbase;
+        const int2* bs = tab.dw_bs + cbase;
+        const bool first = (r & 1) == 0;
+        const bool store = !first && valid && (x & 1) == 0;
+        int8_t* o = p.out +
+                    ((static_cast<int64_t>(n) * (Ho / 2) + (r >> 1)) * (p.Wo / 2) + (x >> 1)) *
+                        Cop +
+                    cbase;
+        static_assert(NV % 2 == 0, "32-byte stores");
+        // 32 channels at a time; the set's shared-memory row buffer keeps
+        // the first row (each thread rereads only what it wrote).
+#pragma unroll
+        for (int h = 0; h < NV; h += 2) {
+          uint4 wv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            uint4 a = rs_requant16<DWQ>(v[h + e], mh, bs, (h + e) * 16, p.dw_lo4, p.dw_hi4);
+            a.x = __vmaxs4(a.x, __shfl_xor_sync(0xFFFFFFFFu, a.x, 1));
+            a.y = __vmaxs4(a.y, __shfl_xor_sync(0xFFFFFFFFu, a.y, 1));
+            a.z = __vmaxs4(a.z, __shfl_xor_sync(0xFFFFFFFFu, a.z, 1));
+            a.w = __vmaxs4(a.w, __shfl_xor_sync(0xFFFFFFFFu, a.w, 1));
+            uint4* keep = reinterpret_cast<uint4*>(atile + (h + e) * 2048);
+            if (first) {
+              *keep = a;
+            } else {
+              const uint4 k0 = *keep;
+              a.x = __vmaxs4(a.x, k0.x);
+              a.y = __vmaxs4(a.y, k0.y);
+              a.z = __vmaxs4(a.z, k0.z);
+              a.w = __vmaxs4(a.w, k0.w);
+            }
+            wv[e] = a;
+          }
+          if (store) st_global_v8(o + 16 * h, wv[0], wv[1]);
+        }
       } else {
         if (valid) {
           const int cls = r == 0 ? cls_top : (r == Ho - 1 ? cls_bot : cls_mid);
@@ -410,11 +465,11 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
   }
 }
 
-template <int CG, int NPW, int S, int NCB, int P, int DWQ, int PWQ, int GI = 0>
-__global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
+template <int CG, int NPW, int S, int NCB, int P, int DWQ, int PWQ, int GI = 0, int POOL = 0>
+__global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI, POOL>::kThreads, 1)
     k_dwrs_s8(const __grid_constant__ CUtensorMap tmIn, const RsArgs p,
               const __grid_constant__ DwPwTable tab) {
-  using Sh = RsShape<CG, NPW, S, NCB, P, GI>;
+  using Sh = RsShape<CG, NPW, S, NCB, P, GI, POOL>;
   static_assert(Sh::Wt * P == 128, "tile rows");
   constexpr int C = Sh::C;
   constexpr int NS = Sh::NS;
@@ -706,7 +761,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
           // Rows whose last input row this is are complete.
           while (nc < Ho && (S * nc - pt + 2 <= y || y == Hin - 1)) {
             const uint32_t gr = gbase + static_cast<uint32_t>(nc);
-            umma_commit(&b.dw_full[(gr % RS) * kRsMaxRing + nc_blk]);
+            umma_commit(&b.dw_full[((POOL ? gr >> 1 : gr) % RS) * kRsMaxRing + nc_blk]);
             ++nc;
             if (++nc_blk == R) nc_blk = 0;
           }
@@ -742,31 +797,31 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
     // One code path per CTA: its channel block's table offsets are
     // compile-time constants.
     if (cb == 0) {
-      rs_epilogue<CG, NPW, S, NCB, P, 0, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q, lane,
+      rs_epilogue<CG, NPW, S, NCB, P, 0, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q, lane,
                                                         abort_flag);
     } else if constexpr (NCB >= 2) {
       if (cb == 1) {
-        rs_epilogue<CG, NPW, S, NCB, P, 1, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+        rs_epilogue<CG, NPW, S, NCB, P, 1, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q,
                                                           lane, abort_flag);
       } else if constexpr (NCB >= 4) {
         if (cb == 2) {
-          rs_epilogue<CG, NPW, S, NCB, P, 2, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+          rs_epilogue<CG, NPW, S, NCB, P, 2, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
         } else if (cb == 3) {
-          rs_epilogue<CG, NPW, S, NCB, P, 3, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+          rs_epilogue<CG, NPW, S, NCB, P, 3, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q,
                                                             lane, abort_flag);
         } else if constexpr (NCB >= 8) {
           if (cb == 4)
-            rs_epilogue<CG, NPW, S, NCB, P, 4, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+            rs_epilogue<CG, NPW, S, NCB, P, 4, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q,
                                                               lane, abort_flag);
           else if (cb == 5)
-            rs_epilogue<CG, NPW, S, NCB, P, 5, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+            rs_epilogue<CG, NPW, S, NCB, P, 5, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q,
                                                               lane, abort_flag);
           else if (cb == 6)
-            rs_epilogue<CG, NPW, S, NCB, P, 6, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+            rs_epilogue<CG, NPW, S, NCB, P, 6, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q,
                                                               lane, abort_flag);
           else
-            rs_epilogue<CG, NPW, S, NCB, P, 7, DWQ, PWQ>(p, tab, bars[k], sA, tm, k, set, q,
+            rs_epilogue<CG, NPW, S, NCB, P, 7, DWQ, PWQ, GI, POOL>(p, tab, bars[k], sA, tm, k, set, q,
                                                               lane, abort_flag);
         }
       }
@@ -781,7 +836,7 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI>::kThreads, 1)
   }
 }
 
-template <int CG, int NPW, int S, int NCB, int P, int DWC, int PWC, int GI = 0>
+template <int CG, int NPW, int S, int NCB, int P, int DWC, int PWC, int GI = 0, int POOL = 0>
 cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int grid,
                       int smem, cudaStream_t s) {
   static std::atomic<uint64_t> done{0};
@@ -789,23 +844,23 @@ cudaError_t rs_launch(const CUtensorMap& m, const RsArgs& a, const DwPwTable& ta
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load() & bit) == 0) {
-    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC, GI>,
+    const cudaError_t e = cudaFuncSetAttribute(k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC, GI, POOL>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kRsSmemLimit);
     if (e != cudaSuccess) return e;
     done.fetch_or(bit);
   }
-  k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC, GI>
+  k_dwrs_s8<CG, NPW, S, NCB, P, DWC, PWC, GI, POOL>
       <<<grid, RsShape<CG, NPW, S, NCB, P, GI>::kThreads, smem, s>>>(m, a, tab);
   return cudaGetLastError();
 }
 
 // The pointwise epilogue variant (ep_flags of the pointwise op).
-template <int CG, int NPW, int S, int NCB, int P, int DWQ, int GI = 0>
+template <int CG, int NPW, int S, int NCB, int P, int DWQ, int GI = 0, int POOL = 0>
 cudaError_t rs_launch_pw(const CUtensorMap& m, const RsArgs& a, const DwPwTable& tab, int pwq,
                          int grid, int smem, cudaStream_t s) {
   if constexpr (NPW == 0) {
-    return rs_launch<CG, NPW, S, NCB, P, DWQ, 0, GI>(m, a, tab, grid, smem, s);
+    return rs_launch<CG, NPW, S, NCB, P, DWQ, 0, GI, POOL>(m, a, tab, grid, smem, s);
   } else {
     switch (pwq) {
       case 0: return rs_launch<CG, NPW, S, NCB, P, DWQ, 0>(m, a, tab, grid, smem, s);
@@ -817,9 +872,9 @@ cudaError_t rs_launch_pw(const CUtensorMap& m, const RsArgs& a, const DwPwTable&
 }
 
 // Shared memory of one launch (bytes) and its input stages.
-template <int CG, int NPW, int S, int NCB, int P, int GI = 0>
+template <int CG, int NPW, int S, int NCB, int P, int GI = 0, int POOL = 0>
 bool rs_smem(int* smem, int* stages) {
-  using Sh = RsShape<CG, NPW, S, NCB, P, GI>;
+  using Sh = RsShape<CG, NPW, S, NCB, P, GI, POOL>;
   const int fixed = Sh::kBdw + NPW * Sh::C + Sh::NS * Sh::RS * Sh::kApw;
   const int overhead = 1024 + fixed + Sh::NS * static_cast<int>(sizeof(RsBars)) + 64;
   const int st = std::min(kRsMaxStages, (kRsSmemLimit - overhead) / (Sh::NS * Sh::kInRow));
@@ -829,22 +884,22 @@ bool rs_smem(int* smem, int* stages) {
   return true;
 }
 
-template <int CG, int NPW, int S, int NCB, int P, int GI = 0>
+template <int CG, int NPW, int S, int NCB, int P, int GI = 0, int POOL = 0>
 cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, int dwq, int pwq,
                      int num_sms, cudaStream_t s) {
-  using Sh = RsShape<CG, NPW, S, NCB, P, GI>;
+  using Sh = RsShape<CG, NPW, S, NCB, P, GI, POOL>;
   int smem = 0;
-  if (!rs_smem<CG, NPW, S, NCB, P, GI>(&smem, &a.stages)) return cudaErrorInvalidValue;
+  if (!rs_smem<CG, NPW, S, NCB, P, GI, POOL>(&smem, &a.stages)) return cudaErrorInvalidValue;
   // NCB CTAs per group of strips, one per channel block.
   const int per_block = static_cast<int>(std::min<int64_t>(
       (static_cast<int64_t>(a.strips) + Sh::NS - 1) / Sh::NS, std::max(1, num_sms / NCB)));
   const int grid = per_block * NCB;
   if (a.strips <= 0) return cudaSuccess;
   switch (dwq) {
-    case 0: return rs_launch_pw<CG, NPW, S, NCB, P, 0, GI>(m, a, tab, pwq, grid, smem, s);
-    case 1: return rs_launch_pw<CG, NPW, S, NCB, P, 1, GI>(m, a, tab, pwq, grid, smem, s);
-    case 2: return rs_launch_pw<CG, NPW, S, NCB, P, 2, GI>(m, a, tab, pwq, grid, smem, s);
-    default: return rs_launch_pw<CG, NPW, S, NCB, P, 3, GI>(m, a, tab, pwq, grid, smem, s);
+    case 0: return rs_launch_pw<CG, NPW, S, NCB, P, 0, GI, POOL>(m, a, tab, pwq, grid, smem, s);
+    case 1: return rs_launch_pw<CG, NPW, S, NCB, P, 1, GI, POOL>(m, a, tab, pwq, grid, smem, s);
+    case 2: return rs_launch_pw<CG, NPW, S, NCB, P, 2, GI, POOL>(m, a, tab, pwq, grid, smem, s);
+    default: return rs_launch_pw<CG, NPW, S, NCB, P, 3, GI, POOL>(m, a, tab, pwq, grid, smem, s);
   }
 }
 
@@ -896,7 +951,7 @@ int rs_packing(const pspml_op_desc& d, int npw) {
 cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                     const uint8_t* wpw_packed, const DwPwTable& tab, int pwq, int32_t pw_min,
                     int32_t pw_max, int64_t batch, const int8_t* in, int8_t* out,
-                    unsigned* dev_err, int num_sms, cudaStream_t s) {
+                    unsigned* dev_err, int num_sms, cudaStream_t s, bool pool) {
   const int C = dw.in_c;
   const int S = dw.stride_h;
   // Samples packed per 128-row tile: rows of at most 32 or 64 pixels share
@@ -968,6 +1023,23 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  if (pool) {
+    // A dense conv with the 2x2 max pool after it in its epilogue.
+    if ((dw.flags & kRsDenseFlag) == 0 || S != 1 || npw != 0) return cudaErrorInvalidValue;
+    if (dw.out_c == 32 && C == 32) {
+      if (P == 1) return rs_shape<1, 0, 1, 1, 1, 0, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (P == 2) return rs_shape<1, 0, 1, 1, 2, 0, 1>(m, a, tab, dwq, 0, num_sms, s);
+    } else if (dw.out_c == 64 && C == 32) {
+      if (P == 1) return rs_shape<2, 0, 1, 1, 1, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (P == 2) return rs_shape<2, 0, 1, 1, 2, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+      return rs_shape<2, 0, 1, 1, 4, 1, 1>(m, a, tab, dwq, 0, num_sms, s);
+    } else if (dw.out_c == 64 && C == 64) {
+      if (P == 1) return rs_shape<2, 0, 1, 1, 1, 2, 1>(m, a, tab, dwq, 0, num_sms, s);
+      if (P == 2) return rs_shape<2, 0, 1, 1, 2, 2, 1>(m, a, tab, dwq, 0, num_sms, s);
+      return rs_shape<2, 0, 1, 1, 4, 2, 1>(m, a, tab, dwq, 0, num_sms, s);
+    }
+    return cudaErrorInvalidValue;
+  }
   if ((dw.flags & kRsDenseFlag) != 0 && dw.out_c != 32) {
     // Dense 32 -> 64 (one input group) and 64 -> 64 (two), stride 1.
     if (S != 1 || dw.out_c != 64 || npw != 0) return cudaErrorInvalidValue;
@@ -1017,7 +1089,7 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
 cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                    const uint8_t* wpw_packed, const DwPwTable& tab, int pwq, int32_t pw_min,
                    int32_t pw_max, int64_t out_per, int64_t batch, const int8_t* in, int8_t* out,
-                   unsigned* dev_err, int num_sms, cudaStream_t s) {
+                   unsigned* dev_err, int num_sms, cudaStream_t s, bool pool = false) {
   const int64_t per_sample = static_cast<int64_t>((dw.out_w + 127) / 128);
   // Whole packed groups per launch.
   const int64_t chunk = std::max<int64_t>(4, ((1ll << 31) - 1) / per_sample) / 4 * 4;
@@ -1025,7 +1097,7 @@ cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
   for (int64_t b0 = 0; b0 < batch; b0 += chunk) {
     const cudaError_t e =
         rs_once(dw, pdw, npw, wpw_packed, tab, pwq, pw_min, pw_max, std::min(chunk, batch - b0),
-                in + b0 * in_per, out + b0 * out_per, dev_err, num_sms, s);
+                in + b0 * in_per, out + b0 * out_per, dev_err, num_sms, s, pool);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -1147,7 +1219,7 @@ cudaError_t pack_conv_rs(const pspml_op_desc& conv, const int8_t* filter, uint8_
 
 cudaError_t launch_dense_rs(const pspml_op_desc& conv, const PreparedOp& p,
                             const uint8_t* wpack, int64_t batch, const int8_t* in, int8_t* out,
-                            unsigned* dev_err, int num_sms, cudaStream_t s) {
+                            unsigned* dev_err, int num_sms, cudaStream_t s, bool pool) {
   const int N = conv.out_c;
   if (p.table == nullptr || !p.all_fast_known || p.ncls > 9 || N > kDwTabC)
     return cudaErrorInvalidValue;
@@ -1161,9 +1233,11 @@ cudaError_t launch_dense_rs(const pspml_op_desc& conv, const PreparedOp& p,
     for (int c = 0; c < N; ++c) tab.dw_dbias[k * N + c] = p.table->dbias[k * N + c];
   PreparedOp q = p;
   q.wpack = reinterpret_cast<const uint32_t*>(wpack);
-  const int64_t out_per = static_cast<int64_t>(conv.out_h) * conv.out_w * N;
+  if (pool && (conv.out_h % 2 != 0 || conv.out_w % 2 != 0)) return cudaErrorInvalidValue;
+  const int64_t out_per = pool ? static_cast<int64_t>(conv.out_h / 2) * (conv.out_w / 2) * N
+                               : static_cast<int64_t>(conv.out_h) * conv.out_w * N;
   return rs_run(dense_as_depthwise(conv), q, 0, nullptr, tab, 0, -128, 127, out_per, batch, in,
-                out, dev_err, num_sms, s);
+                out, dev_err, num_sms, s, pool);
 }
 
 }  // namespace pspml

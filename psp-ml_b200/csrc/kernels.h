@@ -265,14 +265,16 @@ cudaError_t launch_dwrs_pair(const pspml_op_desc& dw, const PreparedOp& pdw,
 // for the implicit GEMM (kTc4d, constant table) run on the row-streaming
 // kernel with dense weight blocks (dwrs_tc.cu): every input row is loaded
 // once instead of once per filter tap.  pack_conv_rs writes the
-// conv_rs_packed_bytes packed weights.
+// conv_rs_packed_bytes packed weights.  pool: the 2x2 / stride-2 max pool
+// after the conv runs in its epilogue (out is then the pool's output; the
+// pool descriptor must pass conv_pool_supported).
 bool dense_rs_supported(const pspml_op_desc& conv, const PreparedOp& p);
 size_t conv_rs_packed_bytes(const pspml_op_desc& conv);
 cudaError_t pack_conv_rs(const pspml_op_desc& conv, const int8_t* filter, uint8_t* out,
                          cudaStream_t s);
 cudaError_t launch_dense_rs(const pspml_op_desc& conv, const PreparedOp& p,
                             const uint8_t* wpack, int64_t batch, const int8_t* in, int8_t* out,
-                            unsigned* dev_err, int num_sms, cudaStream_t s);
+                            unsigned* dev_err, int num_sms, cudaStream_t s, bool pool = false);
 
 // 3x3 convs with 1, 2, 3, 4 or 8 input channels and 16, 32 or 64 outputs
 // on the tensor cores (im2col_tc.cu): patches gathered into a shared-memory

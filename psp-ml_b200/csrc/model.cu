@@ -88,10 +88,17 @@ int forward_chunk(pspml_model* m, const int8_t* in, int8_t* out, int64_t mb, cud
     const ModelOp& op = m->ops[i];
     const int8_t* src = i == 0 ? in : ptrs[i - 1];
     if (op.fuse == 1 && op.pool_pair && aligned(src) && aligned(ptrs[i + 1])) {
-      // Conv + max pool in one kernel; the pair's time is the conv's.
-      const int st = cuda_status(launch_conv_pool(op.d, op.prep, mb, src, ptrs[i + 1],
-                                                  m->ctx->dev_err, m->ctx->num_sms, s),
-                                 "fused conv + max pool");
+      // Conv + max pool in one kernel; the pair's time is the conv's.  A
+      // conv on the row-streaming kernel pools in its epilogue (32-byte
+      // stores), the others on their own conv path.
+      const bool rs = op.rs_weights != nullptr &&
+                      (reinterpret_cast<uintptr_t>(ptrs[i + 1]) & 31u) == 0;
+      const int st = cuda_status(
+          rs ? launch_dense_rs(op.d, op.prep, op.rs_weights, mb, src, ptrs[i + 1],
+                               m->ctx->dev_err, m->ctx->num_sms, s, true)
+             : launch_conv_pool(op.d, op.prep, mb, src, ptrs[i + 1], m->ctx->dev_err,
+                                m->ctx->num_sms, s),
+          "fused conv + max pool");
       if (st) return st;
       if (events) {
         cudaEventRecord((*events)[i + 1], s);
@@ -462,8 +469,7 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
   for (int i = 0; i + 1 < n_ops && !st; ++i) {
     ModelOp& a = m->ops[i];
     ModelOp& b = m->ops[i + 1];
-    if (a.fuse || b.fuse || a.rs_weights != nullptr || !conv_pool_supported(a.d, a.prep, b.d))
-      continue;
+    if (a.fuse || b.fuse || !conv_pool_supported(a.d, a.prep, b.d)) continue;
     a.fuse = 1;
     a.pool_pair = true;
     b.fuse = 2;

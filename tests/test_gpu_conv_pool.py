@@ -4,9 +4,11 @@ pools its requantised outputs), bit-exact against the oracle's two ops.
 The reference runs a separate max_pool2d pass after each conv
 (psp-ml/src/kernels/naive.rs:98-132; examples/mnist-bench/src/generated.rs:
 88-91,122-125).  A compiled model fuses a 3x3 conv with the 2x2 / stride-2
-max pool after it on both conv paths: the tensor-core implicit GEMM
-(in_c % 16 == 0; the window's four pixels are lanes of one epilogue warp)
-and the small-channel dp4a conv (in_c in {1, 2, 3, 4, 8}).  Shapes cover the
+max pool after it on all three conv paths: the tensor-core implicit GEMM
+(in_c % 16 == 0; the window's four pixels are lanes of one epilogue warp),
+the row-streaming dense conv (32 -> 32, 32 -> 64, 64 -> 64; the window's rows
+go to one epilogue set) and the small-channel dp4a conv (in_c in
+{1, 2, 3, 4, 8}).  Shapes cover the
 config 0 and config 2 layers, partial tiles (widths that are not powers of
 two, N not a multiple of the tile), and a pool whose clamp is narrower than
 the conv's, which must not fuse.
@@ -121,11 +123,13 @@ def test_narrower_pool_clamp_is_not_fused(ctx, oracle_mod, ci):
 
 @pytest.mark.parametrize("H,W,ci,co,zp_in,act", [
     (64, 64, 32, 32, -128, "relu"),   # config 2's s0b shape (two samples per tile)
+    (64, 64, 32, 32, 3, "none"),      # s0b shape, fast requantisation form under the pool
     (48, 256, 32, 32, 0, "none"),     # two 128-pixel column tiles
     (12, 20, 32, 32, 21, "relu"),     # one sample per tile
     (7, 9, 32, 32, -128, "none"),     # odd sizes
     (32, 32, 32, 64, -128, "relu"),   # config 2's s1a shape (four samples per tile)
     (32, 32, 64, 64, -128, "relu"),   # config 2's s1b shape
+    (16, 32, 64, 64, 40, "none"),     # four samples per tile, fast form under the pool
     (20, 48, 32, 64, 9, "none"),      # two samples per tile
     (9, 100, 64, 64, 0, "relu"),      # one sample per tile, odd height
     (5, 17, 64, 64, -7, "none"),
@@ -133,11 +137,14 @@ def test_narrower_pool_clamp_is_not_fused(ctx, oracle_mod, ci):
 def test_row_streamed_dense_conv(ctx, oracle_mod, H, W, ci, co, zp_in, act):
     """3x3 stride-1 convs of 32 -> 32, 32 -> 64 and 64 -> 64 channels run on
     the row-streaming kernel with dense weight blocks (each input row loaded
-    once); a max pool after one then runs on its own."""
+    once); with even sizes the 2x2 max pool after the conv runs in its
+    epilogue (a set of epilogue warps takes the window's two rows, lanes x
+    and x ^ 1 its two columns)."""
     conv_act, zp_out = ((-3, 127), -3) if act == "relu" else ((-128, 127), 5)
     descs, blob = _model_parts(H, W, ci, co, zp_in, zp_out, conv_act, (-128, 127), H + W + ci)
-    if H % 2 or W % 2:
+    pooled = H % 2 == 0 and W % 2 == 0
+    if not pooled:
         descs = descs[:1].copy()  # the conv alone
     fused, got, want = _run_chain(ctx, oracle_mod, descs, blob, 5, 5, 4)
-    assert fused[0] == 0
+    assert fused == ((1, 2) if pooled else (0,))
     assert np.array_equal(got, want), f"{np.count_nonzero(got != want)} outputs differ"

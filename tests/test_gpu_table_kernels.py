@@ -106,6 +106,8 @@ def test_pointwise_static_table(ctx, oracle_mod, B, H, W, K, N, act):
     (2, 3, 256, 64, 64, (-128, 127), (-128, 127)),   # block 1
     (2, 2, 200, 64, 64, (-100, 120), (-20, 90)),      # partial tile, both clamps
     (1, 5, 130, 32, 64, (0, 127), (-128, 127)),
+    (2, 7, 300, 32, 64, (4, 127), (-128, 127)),       # 32 channels: floor form, 3 column tiles
+    (3, 9, 128, 32, 64, (-128, 127), (-30, 60)),      # 32 channels: pointwise clamp
     (3, 3, 128, 128, 128, (-128, 127), (-128, 127)),  # not fused: two kernels
 ])
 def test_depthwise_pointwise_pair(ctx, oracle_mod, B, H, W, C, N, dw_act, pw_act):

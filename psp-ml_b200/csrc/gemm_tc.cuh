@@ -234,8 +234,7 @@ enum : int {
   kEpiGeneral = 0,  // tables in smem or global, runtime fast/general requant
   kEpiTable = 1,    // fast requant, tables a kernel parameter, runtime offsets
   kEpiStatic = 2,   // as kEpiTable with every offset a compile-time constant:
-                    // 2D A, up to four N tiles (N == tiles_n * BN) with a
-                    // fixed N tile per CTA, 16-byte aligned rows
+                    // 2D A, one N tile (N == BN), 16-byte aligned rows
   kEpiConvStatic = 3  // 4D (implicit-GEMM conv) A with N == BN (one N tile):
                       // compile-time table offsets, border-class bias
                       // differences and the fused max pool as in kEpiTable
@@ -659,21 +658,14 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
       const uint32_t tb0 = tlane + static_cast<uint32_t>(b * kCols);
 
       if constexpr (MODE == kEpiStatic) {
-        // Up to four N tiles; this CTA's is fixed (blockIdx.x % tiles_n).
-        const uint32_t tm = p.fd_tiles_n.div(static_cast<uint32_t>(t));
-        const int tn = static_cast<int>(blockIdx.x % p.tiles_n);
+        // One N tile (the host picks this variant only then).
+        const uint32_t tm = static_cast<uint32_t>(t);
 #pragma unroll 1
         for (int mt = 0; mt < MT; ++mt) {
           const int64_t r = static_cast<int64_t>(tm) * TM + mt * kBM + row;
           int8_t* orow = p.out + r * p.ldo;
           const uint32_t ta = tb0 + static_cast<uint32_t>(mt * BN);
-          const bool ok = r < p.rows;
-          switch (tn) {
-            case 0: epilogue_row_static<BN, 0, Q>(tab, ta, orow, ok, p); break;
-            case 1: epilogue_row_static<BN, BN, Q>(tab, ta, orow, ok, p); break;
-            case 2: epilogue_row_static<BN, 2 * BN, Q>(tab, ta, orow, ok, p); break;
-            default: epilogue_row_static<BN, 3 * BN, Q>(tab, ta, orow, ok, p); break;
-          }
+          epilogue_row_static<BN, 0, Q>(tab, ta, orow, r < p.rows, p);
         }
       } else if constexpr (MODE == kEpiConvStatic) {
         // Implicit-GEMM conv, one N tile: pixel (x, y) of image n.
@@ -881,9 +873,12 @@ cudaError_t launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const T
 }
 
 // Epilogue variant per op: the static constant-table epilogue for 2D
-// operands with up to four N tiles, the run-time-offset table epilogue for
-// other ops whose host holds a table, the general one (tables in smem or
-// global, runtime fast/general flag) otherwise.
+// operands with one N tile, the run-time-offset table epilogue for other
+// ops whose host holds a table, the general one (tables in smem or global,
+// runtime fast/general flag) otherwise.  (With four N tiles the static
+// epilogue ran four compile-time bodies side by side, one per tile, and its
+// warps stalled on instruction fetch: 4.1-4.5 cycles per issue against 0.26
+// for the same kernel with one N tile.)
 template <int BN, int BK, int MT>
 cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args,
                    const EpiTable* table, int num_sms, cudaStream_t s) {
@@ -948,7 +943,7 @@ cudaError_t run_tc(const CUtensorMap& ma, const CUtensorMap& mb, TcGemmArgs args
       }
     }
   }
-  const bool is_static = !args.conv4d && fixed_n && args.tiles_n <= 4 &&
+  const bool is_static = !args.conv4d && fixed_n && args.tiles_n == 1 &&
                          args.N == args.tiles_n * BN && args.ldo == args.N &&
                          (reinterpret_cast<uintptr_t>(args.out) & 31u) == 0;
   if (!is_static) {

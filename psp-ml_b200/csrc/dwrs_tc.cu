@@ -170,8 +170,7 @@ struct RsShape {
   static_assert(NCB == 1 || NPW == 0, "channel blocks are for the depthwise conv alone");
   static_assert(NCB == 1 || NCB == 2 || NCB == 4 || NCB == 8, "channel blocks");
   static_assert(P == 1 || P == 2 || P == 4, "packed samples");
-  static_assert(P == 1 || (NPW == 0 && S == 1),
-                "packed samples are for a stride-1 depthwise conv alone");
+  static_assert(P == 1 || NPW == 0, "packed samples are for a depthwise (or dense) conv alone");
   static_assert(NPW == 0 || S == 1, "fused pointwise after a stride-1 depthwise conv");
   static_assert(RS <= kRsMaxSets, "epilogue sets");
   static_assert(R <= kRsMaxRing, "accumulator ring");
@@ -579,13 +578,23 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI, POOL>::kThread
           // inside the image, so rows and samples merge into one dimension).
           const int chunk0 = c0 / 16;
           if constexpr (P > 1) {
-            // Per tap kx one box of Wt pixels x P samples, already shifted
-            // (view [C][W][N][H], box {32 x groups, Wt, P, 1}).
+            // Per tap kx one box of Wt pixels x P samples, already shifted:
+            // stride 1 over [C][W][N][H] (box {32 x groups, Wt, P, 1}),
+            // stride 2 over [C][parity][W/2][N][H] (box {32 x groups, 1,
+            // Wt, P, 1}: input pixel 2j + kx - pad_l is pair j + ((kx -
+            // pad_l) >> 1) of parity (kx - pad_l) & 1).
             mbar_arrive_expect_tx(&b.in_full[s], 3 * Sh::kBoxBytes);
 #pragma unroll
-            for (int kx = 0; kx < 3; ++kx)
-              tma_load_4d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0, kx - p.pad_l,
-                          static_cast<int>(st.n), y);
+            for (int kx = 0; kx < 3; ++kx) {
+              if constexpr (S == 1) {
+                tma_load_4d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0, kx - p.pad_l,
+                            static_cast<int>(st.n), y);
+              } else {
+                const int t = kx - p.pad_l;
+                tma_load_5d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0, t & 1, t >> 1,
+                            static_cast<int>(st.n), y);
+              }
+            }
           } else if constexpr (S == 1) {
             mbar_arrive_expect_tx(&b.in_full[s], Sh::kBoxBytes);
             tma_load_5d(a, &tmIn, &b.in_full[s], 0, st.tx * 128 - p.pad_l,
@@ -938,8 +947,9 @@ bool rs_geometry_ok(const pspml_op_desc& d) {
 constexpr int32_t kRsDenseFlag = 1 << 16;
 
 int rs_packing(const pspml_op_desc& d, int npw) {
-  if (npw != 0 || d.out_w > 64 || d.stride_h != 1) return 1;
+  if (npw != 0 || d.out_w > 64) return 1;
   if ((d.flags & kRsDenseFlag) != 0) {
+    if (d.stride_h != 1) return 1;
     if (d.out_c == 32) return d.out_w > 32 ? 2 : 1;  // 32 -> 32: one or two samples per tile
     return d.out_w > 32 ? 2 : 4;
   }
@@ -1008,6 +1018,17 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                           gin == 1 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
+  } else if (P > 1) {
+    // Packed stride-2 samples: [C][parity][W/2][N][H], box {32 x groups, 1,
+    // 128/P, P, 1}, 32- or 64-byte swizzle.
+    const uint64_t dims[5] = {Cu, 2, W / 2, static_cast<uint64_t>(batch), H};
+    const uint64_t strides[4] = {Cu, 2 * Cu, H * W * Cu, W * Cu};
+    const uint32_t box[5] = {16 * chunks, 1, static_cast<uint32_t>(128 / P),
+                             static_cast<uint32_t>(P), 1};
+    if (encode_tensor_map(&m, in, 5, dims, strides, box, estr,
+                          gin == 1 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B) !=
+        CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
   } else if (S == 1) {
     const uint64_t dims[5] = {16, W, static_cast<uint64_t>(batch), Cu / 16, H};
     const uint64_t strides[4] = {Cu, H * W * Cu, 16, W * Cu};
@@ -1070,6 +1091,16 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
       if (C == 128) return rs_shape<2, 0, 2, 2, 1>(m, a, tab, dwq, 0, num_sms, s);
       if (C == 256) return rs_shape<2, 0, 2, 4, 1>(m, a, tab, dwq, 0, num_sms, s);
     }
+  } else if (S == 2) {
+    if (P == 2) {
+      if (C == 64) return rs_shape<2, 0, 2, 1, 2>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 2, 2, 2>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 2, 4, 2>(m, a, tab, dwq, 0, num_sms, s);
+    } else {
+      if (C == 64) return rs_shape<2, 0, 2, 1, 4>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 128) return rs_shape<2, 0, 2, 2, 4>(m, a, tab, dwq, 0, num_sms, s);
+      if (C == 256) return rs_shape<2, 0, 2, 4, 4>(m, a, tab, dwq, 0, num_sms, s);
+    }
   } else if (S == 1) {
     if (P == 2) {
       if (C == 32) return rs_shape<1, 0, 1, 1, 2>(m, a, tab, dwq, 0, num_sms, s);
@@ -1105,13 +1136,15 @@ cudaError_t rs_run(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
 
 }  // namespace
 
-// Rows of 65..127 pixels leave tile lanes idle; narrower stride-1 rows
-// pack several samples per tile (C >= 64).  Packed stride-2 rows measured
-// slower than the CUDA-core kernel, so those shapes stay there.
+// Rows of 65..127 pixels leave tile lanes idle; narrower rows pack several
+// samples per tile (C >= 64, stride 1 or 2).  (Packed stride-2 rows had
+// measured slower than the CUDA-core kernel while their boxes had 16-byte
+// rows; with 64-byte swizzled rows they take config 3's blocks 4 and 6 at
+// 0.90-0.94 of HBM.)
 bool dwrs_dw_supported(const pspml_op_desc& d) {
   if (!rs_geometry_ok(d)) return false;
   if (d.out_w >= 128) return true;
-  return d.out_w <= 64 && d.in_c >= 64 && d.stride_h == 1;
+  return d.out_w <= 64 && d.in_c >= 64;
 }
 
 // The 32-channel pair measured faster on the tile-per-row kernel

@@ -50,10 +50,12 @@ def test_depthwise_static_table(ctx, oracle_mod, B, H, W, C, zp_in, act):
     (1, 12, 200, 128, 1, None, 9, (-128, 127)),          # partial second tile, channel blocks
     (2, 1, 160, 64, 1, None, 2, (-128, 127)),            # one row, partial second tile
     (2, 2, 256, 32, 2, None, -7, (-128, 127)),           # one output row, stride 2
-    (2, 6, 128, 128, 2, None, 0, (-128, 127)),           # stride 2, 64-px rows (CUDA cores)
+    (2, 6, 128, 128, 2, None, 0, (-128, 127)),           # stride 2, 64-px rows: two per tile
     (3, 5, 64, 256, 1, None, -128, (0, 127)),            # two per tile, odd batch
     (5, 4, 32, 128, 1, None, 4, (-128, 127)),            # 32-px rows: four per tile, partial group
-    (2, 12, 64, 256, 2, None, -128, (-128, 127)),        # stride 2, 32-px rows (CUDA cores)
+    (2, 12, 64, 256, 2, None, -128, (-128, 127)),        # stride 2, 32-px rows: four per tile
+    (3, 8, 96, 128, 2, None, 7, (-30, 100)),             # stride 2, 48-px rows, partial group
+    (5, 6, 48, 64, 2, None, -128, (0, 127)),             # stride 2, 24-px rows, partial group
     (3, 7, 50, 64, 1, None, 3, (-30, 100)),              # 50-px rows, clamp
     (2, 9, 40, 64, 2, (1, 1, 1, 1), -2, (-128, 127)),    # stride 2 top/left pad, narrow
     (6, 6, 32, 512, 1, None, -128, (-128, 127)),         # eight channel blocks, four per tile

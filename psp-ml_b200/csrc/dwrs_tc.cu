@@ -23,9 +23,8 @@
 // at (1, 0, 2)[y % 3].
 // Stride 2: an input row feeds one (ky = 1) or two (ky = 2 and 0) output
 // rows; a ring of two blocks, weights as [2 0 2 1].  The input is viewed as
-// [C][2][W/2][H][N] so that one box holds the even and another the odd
-// pixels of a row, each as consecutive 16-byte rows: tap kx reads the even
-// or odd box at a 0 or 16-byte offset.
+// [C][parity][W/2][N][H], so that tap kx's pixels 2j + kx - pad_left are
+// one box of consecutive pairs of one parity (each tap its own box).
 //
 // A block must hold zeros before its row takes its first contribution, so
 // the epilogue zeroes it right after reading the finished row, before the
@@ -148,9 +147,9 @@ struct RsShape {
   // the copy moves whole 32-byte sectors: 16-byte rows cost one L2 request
   // and a 32-byte sector each.
   static constexpr int GIN = GI > 0 ? GI : CG;        // input groups per row
-  static constexpr bool kSwz = P > 1;
-  static constexpr int kBoxes = P > 1 ? 3 : (S == 1 ? 1 : 2);
-  static constexpr int kBoxPx = P > 1 ? 128 : (S == 1 ? 130 : 129);  // pixels per chunk
+  static constexpr bool kSwz = P > 1 || S == 2;  // pre-shifted swizzled boxes
+  static constexpr int kBoxes = kSwz ? 3 : 1;
+  static constexpr int kBoxPx = kSwz ? 128 : 130;  // pixels per chunk
   static constexpr int kRegion = kBoxPx * 16;         // one chunk: the K-half stride
   static constexpr int kBoxBytes = GIN * 2 * kRegion;
   // Swizzled boxes start on 1024-byte boundaries, the others on 128.
@@ -573,42 +572,32 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI, POOL>::kThread
             break;
           }
           uint8_t* a = in_k + s * Sh::kInRow;
-          // Full rows: stride-1 view [16 ch][W][N][C/16 chunks][H], stride-2 view
-          // [16 ch][W/2 pairs][C/16 chunks][parity][H*N] (rows are always
-          // inside the image, so rows and samples merge into one dimension).
-          const int chunk0 = c0 / 16;
-          if constexpr (P > 1) {
-            // Per tap kx one box of Wt pixels x P samples, already shifted:
+          if constexpr (Sh::kSwz) {
+            // Per tap kx one box of Wt pixels x P samples, already shifted
+            // (column tile tx starts at output pixel 128 tx):
             // stride 1 over [C][W][N][H] (box {32 x groups, Wt, P, 1}),
             // stride 2 over [C][parity][W/2][N][H] (box {32 x groups, 1,
             // Wt, P, 1}: input pixel 2j + kx - pad_l is pair j + ((kx -
             // pad_l) >> 1) of parity (kx - pad_l) & 1).
             mbar_arrive_expect_tx(&b.in_full[s], 3 * Sh::kBoxBytes);
+            const int x0 = st.tx * 128;
 #pragma unroll
             for (int kx = 0; kx < 3; ++kx) {
               if constexpr (S == 1) {
-                tma_load_4d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0, kx - p.pad_l,
-                            static_cast<int>(st.n), y);
+                tma_load_4d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0,
+                            x0 + kx - p.pad_l, static_cast<int>(st.n), y);
               } else {
                 const int t = kx - p.pad_l;
-                tma_load_5d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0, t & 1, t >> 1,
-                            static_cast<int>(st.n), y);
+                tma_load_5d(a + kx * Sh::kBoxStride, &tmIn, &b.in_full[s], c0, t & 1,
+                            x0 + (t >> 1), static_cast<int>(st.n), y);
               }
             }
-          } else if constexpr (S == 1) {
+          } else {
+            // Full stride-1 rows: one box over [16 ch][W][N][C/16 chunks][H]
+            // holding every 16-channel chunk of the strip's input groups.
             mbar_arrive_expect_tx(&b.in_full[s], Sh::kBoxBytes);
             tma_load_5d(a, &tmIn, &b.in_full[s], 0, st.tx * 128 - p.pad_l,
-                        static_cast<int>(st.n), chunk0, y);
-          } else {
-            // Even pixels 2j (j from the tile's first output) and odd
-            // pixels 2j+1 (from one pair earlier with a left pad).
-            mbar_arrive_expect_tx(&b.in_full[s], 2 * Sh::kBoxBytes);
-            const int j0 = st.tx * 128;
-            const int yr = static_cast<int>(st.n) * Hin + y;
-#pragma unroll
-            for (int eo = 0; eo < 2; ++eo)
-              tma_load_5d(a + eo * Sh::kBoxStride, &tmIn, &b.in_full[s], 0,
-                          j0 - (eo == 1 ? p.pad_l : 0), chunk0, eo, yr);
+                        static_cast<int>(st.n), c0 / 16, y);
           }
           ++issued;
           if (++s == stages) {
@@ -671,14 +660,10 @@ __global__ void __launch_bounds__(RsShape<CG, NPW, S, NCB, P, GI, POOL>::kThread
       uint32_t aoff[3];  // A start of tap kx within a stage, group 0 (16-byte units)
 #pragma unroll
       for (int kx = 0; kx < 3; ++kx) {
-        if constexpr (P > 1) {
+        if constexpr (Sh::kSwz) {
           aoff[kx] = static_cast<uint32_t>((kx * Sh::kBoxStride) / 16);
-        } else if constexpr (S == 1) {
-          aoff[kx] = static_cast<uint32_t>(kx);
         } else {
-          // pad 0: kx 0 even+0, 1 odd+0, 2 even+16; pad 1: odd+0, even+0, odd+16.
-          const int eo = ((kx == 1) ? 1 : 0) ^ pt;
-          aoff[kx] = static_cast<uint32_t>((eo * Sh::kBoxStride) / 16 + (kx == 2 ? 1 : 0));
+          aoff[kx] = static_cast<uint32_t>(kx);  // a one-pixel (16-byte) move
         }
       }
       // Input group stride in a box (16-byte units).
@@ -916,7 +901,7 @@ cudaError_t rs_shape(const CUtensorMap& m, RsArgs a, const DwPwTable& tab, int d
 // one row/column of top/left padding, 64 or more output pixels per row; C
 // in {32, 64} or a multiple of 64 up to 256 (channel blocks), or 512 for
 // stride-1 rows of at most 32 pixels (four samples per tile); stride 2
-// needs an even input width (the even/odd pixel view).
+// needs an even input width (the [C][parity][W/2] pixel view).
 bool rs_geometry_ok(const pspml_op_desc& d) {
   if (d.kind != PSPML_OP_DEPTHWISE_CONV2D || d.kernel_h != 3 || d.kernel_w != 3 ||
       d.stride_h != d.stride_w || d.in_c != d.out_c)
@@ -995,12 +980,13 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
   a.err = dev_err;
   const int dwq = ep_flags(dw.act_min, dw.act_max, dw.zp_out);
 
-  // Full rows: views whose boxes hold every 16-channel chunk of a row's
-  // input groups (the chunk is a dimension of stride 16 bytes):
-  //   stride 1: [16 ch][W][N][C/16][H], box {16, 130, 1, chunks, 1}
-  //   stride 2: [16 ch][W/2][C/16][parity][H*N], box {16, 129, chunks, 1, 1}
-  // chunks = 2 x the input groups of a strip (the depthwise channel block,
-  // or every input channel of a dense conv).
+  // Full stride-1 rows: a view whose box holds every 16-channel chunk of a
+  // row's input groups (the chunk is a dimension of stride 16 bytes),
+  // [16 ch][W][N][C/16][H], box {16, 130, 1, chunks, 1}.  Packed samples and
+  // stride 2: one pre-shifted box per tap with rows of 32 x groups channels
+  // in the 32- or 64-byte swizzled layout.  chunks = 2 x the input groups of
+  // a strip (the depthwise channel block, or every input channel of a dense
+  // conv).
   const int gin = (dw.flags & kRsDenseFlag) != 0 ? C / 32 : (C == 32 ? 1 : 2);
   const uint32_t chunks = static_cast<uint32_t>(2 * gin);
   const uint64_t W = static_cast<uint64_t>(dw.in_w), H = static_cast<uint64_t>(dw.in_h);
@@ -1018,9 +1004,9 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                           gin == 1 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
-  } else if (P > 1) {
-    // Packed stride-2 samples: [C][parity][W/2][N][H], box {32 x groups, 1,
-    // 128/P, P, 1}, 32- or 64-byte swizzle.
+  } else if (S == 2) {
+    // Stride 2: [C][parity][W/2][N][H], box {32 x groups, 1, 128/P, P, 1},
+    // 32- or 64-byte swizzle.
     const uint64_t dims[5] = {Cu, 2, W / 2, static_cast<uint64_t>(batch), H};
     const uint64_t strides[4] = {Cu, 2 * Cu, H * W * Cu, W * Cu};
     const uint32_t box[5] = {16 * chunks, 1, static_cast<uint32_t>(128 / P),
@@ -1029,17 +1015,10 @@ cudaError_t rs_once(const pspml_op_desc& dw, const PreparedOp& pdw, int npw,
                           gin == 1 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
-  } else if (S == 1) {
+  } else {
     const uint64_t dims[5] = {16, W, static_cast<uint64_t>(batch), Cu / 16, H};
     const uint64_t strides[4] = {Cu, H * W * Cu, 16, W * Cu};
     const uint32_t box[5] = {16, 130, 1, chunks, 1};
-    if (encode_tensor_map(&m, in, 5, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
-        CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
-  } else {
-    const uint64_t dims[5] = {16, W / 2, Cu / 16, 2, H * static_cast<uint64_t>(batch)};
-    const uint64_t strides[4] = {2 * Cu, 16, Cu, W * Cu};
-    const uint32_t box[5] = {16, 129, chunks, 1, 1};
     if (encode_tensor_map(&m, in, 5, dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_NONE) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;

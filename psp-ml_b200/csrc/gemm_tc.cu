@@ -48,8 +48,10 @@ cudaError_t launch_tc_gemm_once(const pspml_op_desc& d, const PreparedOp& pp, in
   const int taps = is_fc ? 1 : d.kernel_h * d.kernel_w;
   // With a constant table, N = 257..512 runs as up to four 128-column tiles
   // (each CTA on one): an epilogue warp then reads 2 KB of the table per
-  // tile, and B stays resident.  (For N <= 256 one 256-column tile is
-  // faster: splitting it makes every CTA pair read A twice.)
+  // tile, which stays in the constant cache, and B stays resident.  (Two
+  // 256-column tiles measured slower at N = 512: b6/b7 pointwise 17.8/22.8
+  // against 18.8/37.9 ms per config-4 step.  For N <= 256 one 256-column
+  // tile is faster: splitting it makes every CTA pair read A twice.)
   const bool tab = pp.all_fast_known && pp.table != nullptr;
   int bn = N <= 32 ? 32 : N <= 64 ? 64 : (N <= 128 || (tab && N > 256 && N <= 512)) ? 128 : 256;
   // A 2D GEMM with few row tiles (an FC over a small batch) would leave

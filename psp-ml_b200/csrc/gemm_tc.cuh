@@ -126,16 +126,33 @@ struct SwizzleFor<32> {
   static constexpr uint32_t kLayout = 6;  // 32B swizzle
 };
 
+// Epilogue variants of k_gemm_s8.
+enum : int {
+  kEpiGeneral = 0,  // tables in smem or global, runtime fast/general requant
+  kEpiTable = 1,    // fast requant, tables a kernel parameter, runtime offsets
+  kEpiStatic = 2,   // as kEpiTable with every offset a compile-time constant:
+                    // 2D A, one N tile (N == BN), 16-byte aligned rows
+  kEpiConvStatic = 3  // 4D (implicit-GEMM conv) A with N == BN (one N tile):
+                      // compile-time table offsets, border-class bias
+                      // differences and the fused max pool as in kEpiTable
+};
+
 // Tensor-memory accumulator buffers and epilogue groups per tile width.
 // MT accumulators of 128 rows x BN columns per tile (a tile has 128 * MT
 // rows: one TMA box, MT MMAs per k step, one handoff).
-template <int BN, int MT>
+template <int BN, int MT, int MODE>
 struct EpiShape {
   static constexpr int kCols = BN * MT;  // tensor-memory columns per buffer
   static constexpr int kBufs = (512 / kCols) >= 8 ? 8 : (512 / kCols);
+  // 256-column tiles of the table epilogues: two groups drain each tile,
+  // one 128-column half each, so four groups work over the two buffers
+  // (with one group per tile these kernels had half the epilogue warps of
+  // the 128-column ones).
+  static constexpr int kSplit =
+      (BN == 256 && MT == 1 && (MODE == kEpiStatic || MODE == kEpiTable)) ? 2 : 1;
   // Three groups for 256-row tiles: 14 warps leave 128 registers a thread
   // (an SM sub-partition holds at most four of them).
-  static constexpr int kGroups = MT == 2 ? 3 : (kBufs >= 4 ? 4 : kBufs);
+  static constexpr int kGroups = (MT == 2 ? 3 : (kBufs >= 4 ? 4 : kBufs)) * kSplit;
   static constexpr int kThreads = 64 + 128 * kGroups;
   static constexpr uint32_t kTmemCols = kBufs * kCols;
 };
@@ -229,16 +246,6 @@ struct NoTable {
   int32_t unused;
 };
 
-// Epilogue variants of k_gemm_s8.
-enum : int {
-  kEpiGeneral = 0,  // tables in smem or global, runtime fast/general requant
-  kEpiTable = 1,    // fast requant, tables a kernel parameter, runtime offsets
-  kEpiStatic = 2,   // as kEpiTable with every offset a compile-time constant:
-                    // 2D A, one N tile (N == BN), 16-byte aligned rows
-  kEpiConvStatic = 3  // 4D (implicit-GEMM conv) A with N == BN (one N tile):
-                      // compile-time table offsets, border-class bias
-                      // differences and the fused max pool as in kEpiTable
-};
 template <int MODE>
 struct TabOf {
   using type = EpiTable;
@@ -321,6 +328,31 @@ __device__ __forceinline__ void epilogue_row_static(const EpiTable& tab, uint32_
   }
 }
 
+// One output row of a 2D tile at a run-time table offset n0 (kEpiTable, the
+// group's columns inside N, 32-byte aligned rows): as epilogue_row_static,
+// but the loop over 32-column pairs is not unrolled and the constants are
+// loaded at run-time offsets, so one small body serves every N tile of the
+// grid.  Q: the op's ep_flags.
+template <int BN, int Q>
+__device__ __forceinline__ void epilogue_row_tab(const EpiTable& tab, uint32_t taddr,
+                                                 int8_t* orow, int n0, bool valid,
+                                                 const TcGemmArgs& p) {
+  static_assert(BN % 32 == 0, "32-byte stores");
+  orow += n0;
+  uint32_t v0[16], v1[16];
+  tmem_ld16_nowait(taddr, v0);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    tmem_wait_ld(v0);
+    tmem_ld16_nowait(taddr + c + 16, v1);
+    const uint4 w0 = requant16_tab<Q>(v0, tab, n0 + c, p.lo4, p.hi4);
+    tmem_wait_ld(v1);
+    if (c + 32 < BN) tmem_ld16_nowait(taddr + c + 32, v0);
+    const uint4 w1 = requant16_tab<Q>(v1, tab, n0 + c + 16, p.lo4, p.hi4);
+    if (valid) st_global_v8(orow + c, w0, w1);
+  }
+}
+
 // One output pixel of a conv tile whose N is the tile width, every
 // requantisation constant at a compile-time table offset (a constant-bank
 // operand, no load): the run-time-offset loop of kEpiTable loads two table
@@ -359,7 +391,7 @@ __device__ __forceinline__ void epilogue_row_conv(const EpiTable& tab, uint32_t 
 }
 
 template <int BN, int BK, int MT, int MODE, int Q>
-__global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
+__global__ void __launch_bounds__(EpiShape<BN, MT, MODE>::kThreads, 1)
     k_gemm_s8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const TcGemmArgs p, const __grid_constant__ typename TabOf<MODE>::type tab) {
   constexpr int TM = kBM * MT;  // rows per tile
@@ -367,10 +399,13 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
   constexpr int B_BYTES = BN * BK;
   constexpr uint32_t kLayout = SwizzleFor<BK>::kLayout;
   constexpr uint32_t kSbo = 8 * BK;  // bytes between 8-row groups
-  constexpr int NB = EpiShape<BN, MT>::kBufs;
-  constexpr int G = EpiShape<BN, MT>::kGroups;
-  constexpr int kCols = EpiShape<BN, MT>::kCols;
-  constexpr uint32_t kTmemCols = EpiShape<BN, MT>::kTmemCols;
+  using Shape = EpiShape<BN, MT, MODE>;
+  constexpr int NB = Shape::kBufs;
+  constexpr int G = Shape::kGroups;
+  constexpr int SPL = Shape::kSplit;  // epilogue groups per tile
+  constexpr int W = BN / SPL;         // columns a group drains
+  constexpr int kCols = Shape::kCols;
+  constexpr uint32_t kTmemCols = Shape::kTmemCols;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -403,7 +438,7 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
     }
     for (int a = 0; a < NB; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], 4 * SPL);
     }
     mbar_init(mma_done, 1);
     mbar_init(bres_full, 1);
@@ -636,15 +671,17 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
   } else {
     // --------------------------------------------------------- epilogue
     const int grp = (warp - 2) >> 2;
+    const int gt = grp / SPL;                // tile slot of this group
+    const int c_lo = (grp - gt * SPL) * W;   // its first column in the tile
     const int q = warp & 3;  // tensor-memory lane quarter this warp may read
     const int row = q * 32 + lane;
     const uint32_t tlane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     const bool fast = MODE != kEpiGeneral || *p.all_fast != 0;
     const RqChannel* rqb = p.param_smem ? srq : p.rq;
     const int32_t* bb = p.param_smem ? sbias : p.bias;
-    int64_t i = grp;
-    for (int64_t t = blockIdx.x + static_cast<int64_t>(grp) * gridDim.x; t < p.tiles_total;
-         t += static_cast<int64_t>(G) * gridDim.x, i += G) {
+    int64_t i = gt;
+    for (int64_t t = blockIdx.x + static_cast<int64_t>(gt) * gridDim.x; t < p.tiles_total;
+         t += static_cast<int64_t>(G / SPL) * gridDim.x, i += G / SPL) {
       const int b = static_cast<int>(i % NB);
       const uint32_t use = static_cast<uint32_t>(i / NB);
       int ready = 0;
@@ -665,7 +702,12 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
           const int64_t r = static_cast<int64_t>(tm) * TM + mt * kBM + row;
           int8_t* orow = p.out + r * p.ldo;
           const uint32_t ta = tb0 + static_cast<uint32_t>(mt * BN);
-          epilogue_row_static<BN, 0, Q>(tab, ta, orow, r < p.rows, p);
+          if constexpr (SPL == 1)
+            epilogue_row_static<BN, 0, Q>(tab, ta, orow, r < p.rows, p);
+          else if (c_lo == 0)
+            epilogue_row_static<W, 0, Q>(tab, ta, orow, r < p.rows, p);
+          else
+            epilogue_row_static<W, W, Q>(tab, ta + W, orow, r < p.rows, p);
         }
       } else if constexpr (MODE == kEpiConvStatic) {
         // Implicit-GEMM conv, one N tile: pixel (x, y) of image n.
@@ -730,7 +772,7 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
               const bool store = valid && ((x | y) & 1) == 0;
               const int vert = 1 << p.bw_log2;
 #pragma unroll 1
-              for (int c = 0; c < BN; c += 16) {
+              for (int c = c_lo; c < c_lo + W; c += 16) {
                 uint32_t v[16];
                 tmem_ld16(tb + static_cast<uint32_t>(c), v);
                 const int32_t nc = tn * BN + c;
@@ -752,6 +794,17 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
           orow = p.out + r * p.ldo;
         }
         const int32_t n0 = tn * BN;
+        if constexpr (MODE == kEpiTable && W <= 128) {
+          if (!p.conv4d && n0 + c_lo + W <= p.N &&
+              ((reinterpret_cast<uintptr_t>(p.out) | static_cast<uintptr_t>(p.ldo)) & 31u) == 0) {
+            const uint32_t th = tb + static_cast<uint32_t>(c_lo);
+            if (p.clamp)
+              epilogue_row_tab<W, (Q & kEpFloor) | kEpClamp>(tab, th, orow, n0 + c_lo, valid, p);
+            else
+              epilogue_row_tab<W, Q & kEpFloor>(tab, th, orow, n0 + c_lo, valid, p);
+            continue;
+          }
+        }
         // (256-column tiles only: the tile the host picks for odd N > 256
         // without a constant table; narrower variants keep their registers.)
         if constexpr (MODE == kEpiGeneral && BN == 256)
@@ -802,7 +855,7 @@ __global__ void __launch_bounds__(EpiShape<BN, MT>::kThreads, 1)
           continue;
         }
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = c_lo; c < c_lo + W; c += 16) {
           uint32_t v[16];
           tmem_ld16(tb + static_cast<uint32_t>(c), v);
           const int32_t nc = n0 + c;
@@ -868,7 +921,7 @@ cudaError_t launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const T
   const cudaError_t e = ensure_smem_attr<BN, BK, MT, MODE, Q>();
   if (e != cudaSuccess) return e;
   k_gemm_s8<BN, BK, MT, MODE, Q>
-      <<<static_cast<unsigned>(grid), EpiShape<BN, MT>::kThreads, smem, s>>>(ma, mb, args, tab);
+      <<<static_cast<unsigned>(grid), EpiShape<BN, MT, MODE>::kThreads, smem, s>>>(ma, mb, args, tab);
   return cudaGetLastError();
 }
 

@@ -85,6 +85,7 @@ def _run(ctx, oracle_mod, descs, blob, batch, micro, seed):
     (32, 32, 64, 128, 5),    # 32-pixel rows
     (16, 16, 128, 128, 9),   # stage 2
     (8, 8, 256, 256, 17),    # stage 3 (two images per tile)
+    (8, 8, 128, 192, 6),     # N = 192 in a 256-column tile (two epilogue groups, one half each)
     (6, 6, 32, 48, 7),       # 8-pixel tile rows with two invalid columns; N = 48 in a 64 tile
     (12, 20, 16, 32, 4),     # a second, mostly empty tile column
     (2, 2, 32, 16, 70),      # one pooled pixel per image

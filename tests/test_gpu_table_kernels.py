@@ -91,6 +91,11 @@ def test_depthwise_row_streaming_shapes(ctx, oracle_mod, B, H, W, C, stride, pad
     (3, 5, 33, 64, 32, (-10, 100)),      # 256-row tiles, ragged last tile, clamp
     (2, 6, 40, 128, 128, (-128, 127)),
     (1, 4, 50, 64, 256, (0, 127)),
+    # Several 128-column N tiles (run-time table offsets, one N tile per CTA)
+    (2, 6, 32, 256, 512, (-128, 127)),
+    (3, 5, 21, 512, 384, (-20, 90)),     # ragged last row tile, clamp
+    (1, 3, 7, 128, 320, (-128, 127)),    # last N tile partial
+    (2, 5, 30, 64, 200, (-128, 127)),    # one 256-column tile, its second half partial
 ])
 def test_pointwise_static_table(ctx, oracle_mod, B, H, W, K, N, act):
     r = np.random.default_rng(8000 + H * W + K + N)
@@ -182,6 +187,11 @@ FLOOR_CASES = [
     ("cuda-core dw s1, 36 channels", 2, [_dw(5, 40, 36, 1, 2, -128, (-128, 120))]),
     ("gemm static 128", 2, [_pw(6, 40, 64, 128, -128, -128, (-128, 127))]),
     ("gemm static 256-row tiles, clamp", 2, [_pw(8, 64, 32, 64, 5, 3, (3, 100))]),
+    ("gemm static 256 columns", 2, [_pw(6, 40, 64, 256, -128, -128, (-128, 127))]),
+    ("gemm static 256 columns, clamp", 3, [_pw(5, 33, 128, 256, 2, 3, (3, 90))]),
+    ("gemm 200 columns, run-time offsets", 2, [_pw(4, 30, 64, 200, -128, -128, (-128, 127))]),
+    ("gemm 512 columns, run-time offsets", 2, [_pw(6, 32, 256, 512, -128, -128, (-128, 127))]),
+    ("gemm 384 columns, run-time offsets, clamp", 3, [_pw(5, 21, 128, 384, 3, 4, (4, 110))]),
     ("gemm 3x3 table", 2, [conv_desc(capi.OP_CONV2D, 9, 20, 32, 64, k=3, stride=1, zp_in=-128,
                                      zp_out=-128, act=(-128, 127))]),
     ("gemm 3x3 table, clamp", 2, [conv_desc(capi.OP_CONV2D, 7, 12, 16, 48, k=3, stride=1,

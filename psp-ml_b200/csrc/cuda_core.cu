@@ -1087,6 +1087,52 @@ __global__ void k_avgpool_s8(const int8_t* __restrict__ in, int8_t* __restrict__
     op[0] = static_cast<int8_t>(r[0]);
 }
 
+// Global average pool (the window is the whole image, no padding): a thread
+// sums 16 channels of one sample over every pixel with eight 16-byte loads
+// in flight (the windowed kernel above keeps one load in flight per thread,
+// too few to cover HBM latency), then divides as k_avgpool_s8 does.
+__global__ void k_gap_s8(const int8_t* __restrict__ in, int8_t* __restrict__ out, int32_t hw,
+                         int32_t C, int32_t act_min, int32_t act_max, int64_t total) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int cv = C / 16;
+  const int64_t n = idx / cv;
+  const int c0 = static_cast<int>(idx - n * cv) * 16;
+  const int8_t* px = in + n * hw * static_cast<int64_t>(C) + c0;
+  int32_t acc[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc[j] = 0;
+  auto add16 = [&](const uint4 v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[4 * q + j] += sbyte(w[q], j);
+  };
+  int i = 0;
+  for (; i + 8 <= hw; i += 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      v[u] = __ldg(reinterpret_cast<const uint4*>(px + static_cast<int64_t>(i + u) * C));
+#pragma unroll
+    for (int u = 0; u < 8; ++u) add16(v[u]);
+  }
+  for (; i < hw; ++i) add16(__ldg(reinterpret_cast<const uint4*>(px + static_cast<int64_t>(i) * C)));
+  int32_t r[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    int32_t a = acc[j];
+    a = a > 0 ? (a + hw / 2) / hw : (a - hw / 2) / hw;
+    a = max(a, act_min);
+    a = min(a, act_max);
+    r[j] = a;
+  }
+  *reinterpret_cast<uint4*>(out + n * C + c0) =
+      make_uint4(pack4_s8(r[0], r[1], r[2], r[3]), pack4_s8(r[4], r[5], r[6], r[7]),
+                 pack4_s8(r[8], r[9], r[10], r[11]), pack4_s8(r[12], r[13], r[14], r[15]));
+}
+
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 template <int KH, int KW, int CI, int RQ>
@@ -1382,7 +1428,13 @@ cudaError_t launch_avgpool(const pspml_op_desc& d, int64_t batch, const int8_t* 
                            int8_t* out, cudaStream_t s) {
   const Geom g = geom_of(d);
   const int64_t pix = batch * g.Ho * g.Wo;
-  if (g.C % 16 == 0 && aligned(in, 16) && aligned(out, 16)) {
+  const bool global = g.Ho == 1 && g.Wo == 1 && g.KH == g.H && g.KW == g.W && g.pt == 0 &&
+                      g.pl == 0;
+  if (global && g.C % 16 == 0 && aligned(in, 16) && aligned(out, 16)) {
+    const int64_t total = batch * (g.C / 16);
+    k_gap_s8<<<grid_for(total), kBlock, 0, s>>>(in, out, g.H * g.W, g.C, d.act_min, d.act_max,
+                                                total);
+  } else if (g.C % 16 == 0 && aligned(in, 16) && aligned(out, 16)) {
     // 16 channels a thread: a warp reads 512 contiguous bytes per pixel.
     const int64_t total = pix * (g.C / 16);
     k_avgpool_s8<16><<<grid_for(total), kBlock, 0, s>>>(in, out, g, d.act_min, d.act_max, total);

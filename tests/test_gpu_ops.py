@@ -165,6 +165,20 @@ def test_global_avgpool(ctx, oracle_mod, B, H, W, C):
     _check(ctx, oracle_mod, d, B, x)
 
 
+@pytest.mark.parametrize("lo,hi,act", [(-128, -90, (-128, 127)), (90, 128, (-128, 127)),
+                                       (-128, 128, (-40, 50))])
+def test_global_avgpool_rounding_and_clamp(ctx, oracle_mod, lo, hi, act):
+    # One-signed sums take each rounding branch; 39 pixels leave a remainder
+    # after the eight-pixel steps of the global kernel.
+    B, H, W, C = 6, 13, 3, 64
+    r = np.random.default_rng(lo + 1000)
+    d = make_desc(kind=capi.OP_AVERAGE_POOL2D, in_h=H, in_w=W, in_c=C, out_h=1, out_w=1,
+                  out_c=C, kernel_h=H, kernel_w=W, stride_h=H, stride_w=W, act_min=act[0],
+                  act_max=act[1])
+    x = r.integers(lo, hi, (B, H, W, C)).astype(np.int8)
+    _check(ctx, oracle_mod, d, B, x)
+
+
 def test_empty_batch_is_a_no_op(ctx):
     d = make_desc(kind=capi.OP_MAX_POOL2D, in_h=4, in_w=4, in_c=16, out_h=2, out_w=2, out_c=16,
                   kernel_h=2, kernel_w=2, stride_h=2, stride_w=2)

@@ -229,12 +229,16 @@ int pspml_ctx_create(int device, size_t workspace_bytes, pspml_ctx** out) {
   ctx->num_sms = prop.multiProcessorCount;
   ctx->workspace_bytes = workspace_bytes ? workspace_bytes : (64u << 20);
   st = cuda_status(cudaMalloc(&ctx->dev_err, 256), "cudaMalloc(error word)");
-  if (!st) st = cuda_status(cudaMemset(ctx->dev_err, 0, 256), "cudaMemset");
   if (!st)
     st = cuda_status(cudaMalloc(&ctx->workspace, ctx->workspace_bytes), "cudaMalloc(workspace)");
   if (!st)
     st = cuda_status(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking),
                      "cudaStreamCreate");
+  // Cleared on the context's own stream and waited for: a plain cudaMemset
+  // runs on the legacy default stream, which non-blocking streams do not
+  // wait for.
+  if (!st) st = cuda_status(cudaMemsetAsync(ctx->dev_err, 0, 256, ctx->stream), "cudaMemset");
+  if (!st) st = cuda_status(cudaStreamSynchronize(ctx->stream), "cudaMemset");
   if (st) {
     pspml_ctx_destroy(ctx);
     return st;
@@ -267,7 +271,8 @@ int pspml_ctx_check_device(pspml_ctx* ctx) {
                        "read device error word");
   if (st) return st;
   if (v != 0) {
-    cudaMemset(ctx->dev_err, 0, sizeof(unsigned));
+    cudaMemsetAsync(ctx->dev_err, 0, sizeof(unsigned), ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
     char buf[96];
     std::snprintf(buf, sizeof(buf), "a kernel gave up on a bounded wait (code %u)", v);
     return set_error(PSPML_ERR_DEVICE_WAIT, buf);

@@ -281,9 +281,14 @@ int pspml_model_create(pspml_ctx* ctx, const pspml_op_desc* ops, int32_t n_ops,
     wbytes += need;
   }
   st = cuda_status(cudaMalloc(&m->weights, wbytes), "cudaMalloc(weights)");
+  // The upload is ordered on the preparation stream: a plain cudaMemcpy from
+  // pageable memory runs on the legacy default stream and may return before
+  // its DMA lands, which the context's non-blocking stream does not wait for
+  // (the table-building kernels below then read stale multipliers).
   if (!st && blob_bytes > 0)
-    st = cuda_status(cudaMemcpy(m->weights, blob, blob_bytes, cudaMemcpyHostToDevice),
-                     "weight upload");
+    st = cuda_status(
+        cudaMemcpyAsync(m->weights, blob, blob_bytes, cudaMemcpyHostToDevice, ctx->stream),
+        "weight upload");
   for (int i = 0; i < n_ops && !st; ++i) {
     ModelOp& op = m->ops[i];
     const pspml_op_desc& d = op.d;

@@ -119,6 +119,10 @@ extern "C" int pspml_noalloc_check_device(void) {
   const unsigned zero = 0;
   st = cuda_status(cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(zero)),
                    "clear no-allocation error word");
+  // A copy from pageable memory may return before its DMA lands; wait for it
+  // so that no later kernel's error code is cleared by it.
+  if (!st)
+    st = cuda_status(cudaStreamSynchronize(cudaStreamLegacy), "clear no-allocation error word");
   if (st) return st;
   return set_error(PSPML_ERR_DEVICE_WAIT,
                    "a no-allocation kernel gave up on a bounded wait (code " +

@@ -289,12 +289,115 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
       for (int j = 0; j < R; ++j) mbar_arrive(&bars.dw_free[j]);
   }
 
-  uint32_t full_ph = 0;  // bit j: parity of the next wait on dw_full[set][j]
-  uint32_t pw_ph = 0;
-  uint8_t* atile = sA + set * Sh::kApw + row * 16;
   int first, step;
   rs_strip_range(NCB, k, Sh::NS, &first, &step);
   const int Ho = p.Ho;
+
+  if constexpr (NPW > 0) {
+    // Fused pair: set 0 requantises every row's depthwise output into the
+    // pointwise A tile of buffer g % RS, set 1 every row's pointwise output,
+    // so neither set waits for the other half of its own row.  Barriers:
+    // dw_full[g % RS][r % R] (rows of one barrier complete in row order and
+    // set 0 frees a block only after waiting for its previous row), apw_full
+    // and pw_full per A buffer, pw_empty for the one pointwise accumulator.
+    // Set 0 rewrites buffer b only after the pointwise MMAs of row g - RS
+    // that read it have completed.
+    uint32_t full_ph = 0;  // bit (b * R + rb): parity of the next wait on dw_full[b][rb]
+    uint32_t g = 0;        // row number within the slot
+    for (int i = first; i < p.strips; i += step) {
+      const RsStrip st = rs_strip<P>(p, i);
+      const int x = st.tx * 128 + row;
+      const bool valid = x < p.Wo;
+      int cls_top = p.base_cls, cls_mid = p.base_cls, cls_bot = p.base_cls;
+      if (set == 0 && valid && p.borders) {
+        const int xc = p.xcls[x];
+        cls_top = p.ycls[0] * p.n_xcls + xc;
+        cls_mid = p.ycls[Ho > 1 ? 1 : 0] * p.n_xcls + xc;
+        cls_bot = p.ycls[Ho - 1] * p.n_xcls + xc;
+      }
+      const int64_t pix0 = (static_cast<int64_t>(st.n) * Ho) * p.Wo + x;
+      for (int r = 0; r < Ho; ++r, ++g) {
+        const int b = static_cast<int>(g % RS);
+        if (set == 0) {
+          const int rb = r % R;
+          const int bit = b * R + rb;
+          if (!warp_wait(&bars.dw_full[b * kRsMaxRing + rb], (full_ph >> bit) & 1u, abort_flag,
+                         lane)) {
+            if (lane == 0) rs_record_error(p.err, abort_flag, kDevErrEpiWait);
+            return;
+          }
+          full_ph ^= 1u << bit;
+          tc_fence_after();
+          uint32_t v[NV][16];
+#pragma unroll
+          for (int h = 0; h < NV; ++h)
+            tmem_ld16_nowait(
+                tl + static_cast<uint32_t>((h / 2) * R * 32 + rb * 32 + (h % 2) * 16), v[h]);
+#pragma unroll
+          for (int h = 0; h < NV; ++h) tmem_wait_ld(v[h]);
+#pragma unroll
+          for (int h = 0; h < NV; ++h)
+            tmem_st16_zero(tl + static_cast<uint32_t>((h / 2) * R * 32 + rb * 32 + (h % 2) * 16));
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.dw_free[rb]);
+          const int cls = r == 0 ? cls_top : (r == Ho - 1 ? cls_bot : cls_mid);
+          if (valid && cls != p.base_cls) {
+            const int off = cls * C;
+#pragma unroll
+            for (int h = 0; h < NV; ++h)
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                v[h][j] += static_cast<uint32_t>(tab.dw_dbias[off + h * 16 + j]);
+          }
+          if (g >= static_cast<uint32_t>(RS) &&
+              !warp_wait(&bars.pw_full[b], ((g / RS) - 1u) & 1u, abort_flag, lane)) {
+            if (lane == 0) rs_record_error(p.err, abort_flag, kDevErrEpiWait);
+            return;
+          }
+          uint8_t* atile = sA + b * Sh::kApw + row * 16;
+#pragma unroll
+          for (int h = 0; h < NV; ++h)
+            *reinterpret_cast<uint4*>(atile + h * 2048) =
+                rs_requant16<DWQ>(v[h], tab.dw_mh, tab.dw_bs, h * 16, p.dw_lo4, p.dw_hi4);
+          rs_fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.apw_full[b]);
+        } else {
+          if (!warp_wait(&bars.pw_full[b], (g / RS) & 1u, abort_flag, lane)) {
+            if (lane == 0) rs_record_error(p.err, abort_flag, kDevErrEpiWait);
+            return;
+          }
+          tc_fence_after();
+          uint32_t u[NP][16];
+          const uint32_t tp = tl + static_cast<uint32_t>(CG * R * 32);
+#pragma unroll
+          for (int h = 0; h < NP; ++h) tmem_ld16_nowait(tp + h * 16, u[h]);
+#pragma unroll
+          for (int h = 0; h < NP; ++h) tmem_wait_ld(u[h]);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.pw_empty);
+          if (valid) {
+            int8_t* o = p.out + (pix0 + static_cast<int64_t>(r) * p.Wo) * NPW;
+            static_assert(NP % 2 == 0, "32-byte stores");
+#pragma unroll
+            for (int h = 0; h < NP; h += 2)
+              st_global_v8(o + 16 * h,
+                           rs_requant16<PWQ>(u[h], tab.pw_mh, tab.pw_bs, h * 16, p.pw_lo4,
+                                             p.pw_hi4),
+                           rs_requant16<PWQ>(u[h + 1], tab.pw_mh, tab.pw_bs, h * 16 + 16,
+                                             p.pw_lo4, p.pw_hi4));
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  uint32_t full_ph = 0;  // bit j: parity of the next wait on dw_full[set][j]
+  uint8_t* atile = sA + set * Sh::kApw + row * 16;
   uint32_t g = 0;  // row number within the slot
   for (int i = first; i < p.strips; i += step) {
     const RsStrip st = rs_strip<P>(p, i);
@@ -324,9 +427,7 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
       }
       full_ph ^= 1u << rb;
       tc_fence_after();
-      // (The fused path, rows of >= 128 px, always loads: a guard there
-      // made the compiler spill.)
-      const bool load = NPW > 0 || any_valid;
+      const bool load = any_valid;
       uint32_t v[NV][16];
       if (load) {
 #pragma unroll
@@ -345,50 +446,7 @@ __device__ __forceinline__ void rs_epilogue(const RsArgs& p, const DwPwTable& ta
       if (lane == 0) mbar_arrive(&bars.dw_free[rb]);
 
       const int64_t pix = pix0 + static_cast<int64_t>(r) * p.Wo;
-      if constexpr (NPW > 0) {
-        const int cls = r == 0 ? cls_top : (r == Ho - 1 ? cls_bot : cls_mid);
-        if (valid && cls != p.base_cls) {
-          const int off = cls * C;
-#pragma unroll
-          for (int h = 0; h < NV; ++h)
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              v[h][j] += static_cast<uint32_t>(tab.dw_dbias[off + h * 16 + j]);
-        }
-#pragma unroll
-        for (int h = 0; h < NV; ++h)
-          *reinterpret_cast<uint4*>(atile + h * 2048) =
-              rs_requant16<DWQ>(v[h], tab.dw_mh, tab.dw_bs, h * 16, p.dw_lo4, p.dw_hi4);
-        rs_fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.apw_full[set]);
-        // This row's pointwise accumulator.
-        if (!warp_wait(&bars.pw_full[set], pw_ph, abort_flag, lane)) {
-          if (lane == 0) rs_record_error(p.err, abort_flag, kDevErrEpiWait);
-          return;
-        }
-        pw_ph ^= 1u;
-        tc_fence_after();
-        uint32_t u[NP][16];
-        const uint32_t tp = tl + static_cast<uint32_t>(CG * R * 32);
-#pragma unroll
-        for (int h = 0; h < NP; ++h) tmem_ld16_nowait(tp + h * 16, u[h]);
-#pragma unroll
-        for (int h = 0; h < NP; ++h) tmem_wait_ld(u[h]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.pw_empty);
-        if (valid) {
-          int8_t* o = p.out + pix * NPW;
-          static_assert(NP % 2 == 0, "32-byte stores");
-#pragma unroll
-          for (int h = 0; h < NP; h += 2)
-            st_global_v8(o + 16 * h,
-                         rs_requant16<PWQ>(u[h], tab.pw_mh, tab.pw_bs, h * 16, p.pw_lo4, p.pw_hi4),
-                         rs_requant16<PWQ>(u[h + 1], tab.pw_mh, tab.pw_bs, h * 16 + 16,
-                                           p.pw_lo4, p.pw_hi4));
-        }
-      } else if constexpr (POOL != 0) {
+      if constexpr (POOL != 0) {
         // 2x2 max pool: every lane requantises its pixel (the window's
         // other column is lane row ^ 1, its other row the set's previous
         // row), even columns of odd rows store the window's maximum.

@@ -44,11 +44,12 @@
 // the tile idle; warps whose 32 pixels are all outside the row skip the
 // arithmetic.
 //
-// Fused pointwise (stride 1, 64 channels): the epilogue writes the
-// requantised depthwise row into a shared-memory A tile [C/16][128][16 B];
-// the MMA thread runs C/32 MMAs (M=128, N=NPW, K=32) against the resident
-// 1x1 weights into a pointwise accumulator; the epilogue requantises that
-// and stores NHWC.  The depthwise output never reaches global memory.
+// Fused pointwise (stride 1, 64 channels): one epilogue set writes every
+// requantised depthwise row into a shared-memory A tile [C/16][128][16 B]
+// (two buffers, rows alternating); the MMA thread runs C/32 MMAs (M=128,
+// N=NPW, K=32) against the resident 1x1 weights into a pointwise
+// accumulator; the other set requantises that and stores NHWC.  The
+// depthwise output never reaches global memory.
 //
 // Requantisation constants come from a kernel-parameter table: at
 // compile-time offsets for a single channel block, at warp-uniform run-time

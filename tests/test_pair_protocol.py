@@ -23,7 +23,10 @@ The checks: every actor finishes (no deadlock), every wait starts no more
 than one phase ahead and is never overtaken by two completions, a ring block
 is written only while free and read only for its row, an A buffer is never
 rewritten while a pointwise MMA that reads it is in flight, and the
-pointwise accumulator holds the row set 1 expects.
+pointwise accumulator holds the row set 1 expects.  A second model covers
+the depthwise (or dense) conv alone: stride 1 with a 4-block ring, stride 2
+with a 2-block ring, sets taking rows in turn or row pairs with the fused
+2x2 max pool.
 """
 import random
 
@@ -154,8 +157,11 @@ class Model:
             self.acc = ("full", g)
             self.pw_full[x].arrive()
 
+    def actors(self):
+        return {"mma": self.mma(), "set0": self.set0(), "set1": self.set1()}
+
     def run(self):
-        actors = {"mma": self.mma(), "set0": self.set0(), "set1": self.set1()}
+        actors = self.actors()
         pending = {k: None for k in actors}
         live = set(actors)
         for k in list(actors):
@@ -188,3 +194,86 @@ class Model:
 def test_pair_protocol_random_schedules(ho, strips):
     for seed in range(40 if ho < 48 else 4):
         Model(ho, strips, random.Random(1000 * ho + 10 * strips + seed)).run()
+
+
+class RowModel(Model):
+    """The depthwise (or dense) conv alone: stride S, an R-block ring, two
+    epilogue sets taking rows in turn (row pairs with the fused 2x2 pool),
+    dw_full per (set, block) and dw_free per block, as in k_dwrs_s8 with
+    NPW = 0."""
+
+    def __init__(self, s, r, pt, ho, hin, pool, strips, rng):
+        self.s, self.r, self.pt, self.hin, self.pool = s, r, pt, hin, pool
+        super().__init__(ho, strips, rng)
+        self.dw_full = [[Barrier(f"dw_full[{b}][{j}]", 1) for j in range(r)] for b in range(RS)]
+        self.dw_free = [Barrier(f"dw_free[{j}]", 4) for j in range(r)]
+        self.block = [None] * r
+
+    def owner(self, g):
+        return ((g >> 1) if self.pool else g) % RS
+
+    def mma(self):
+        s, r, pt, ho, hin = self.s, self.r, self.pt, self.ho, self.hin
+        free_cnt = [0] * r
+        gbase = 0
+        for _ in range(self.strips):
+            nn = nc = nn_blk = nc_blk = 0
+            for y in range(hin):
+                while nn < ho and s * nn - pt <= y:
+                    yield self.wait(self.dw_free[nn_blk], free_cnt[nn_blk])
+                    free_cnt[nn_blk] += 1
+                    assert self.block[nn_blk] is None, "ring block taken while in use"
+                    self.block[nn_blk] = (gbase + nn, False)
+                    nn += 1
+                    nn_blk = (nn_blk + 1) % r
+                while nc < ho and (s * nc - pt + 2 <= y or y == hin - 1):
+                    self.pipe.append(("dw", gbase + nc, nc_blk))
+                    nc += 1
+                    nc_blk = (nc_blk + 1) % r
+            assert nc == ho and nn == ho
+            gbase += ho
+
+    def epilogue(self, st):
+        if st == 0:
+            for j in range(self.r):
+                self.dw_free[j].arrive(4)
+        full_cnt = [0] * self.r
+        g = 0
+        for _ in range(self.strips):
+            for row in range(self.ho):
+                if self.owner(g) == st:
+                    rb = row % self.r
+                    yield self.wait(self.dw_full[st][rb], full_cnt[rb])
+                    full_cnt[rb] += 1
+                    assert self.block[rb] == (g, True), f"block {rb}: {self.block[rb]}, row {g}"
+                    self.block[rb] = None
+                    self.dw_free[rb].arrive(4)
+                g += 1
+
+    def complete_one(self):
+        kind, g, x = self.pipe.pop(0)
+        assert self.block[x] == (g, False)
+        self.block[x] = (g, True)
+        self.dw_full[self.owner(g)][x].arrive()
+
+    def actors(self):
+        return {"mma": self.mma(), "set0": self.epilogue(0), "set1": self.epilogue(1)}
+
+# (stride, ring blocks, pad top, output rows, input rows, pooled row pairs)
+ROW_CASES = [
+    (1, 4, 1, 1, 1, False), (1, 4, 1, 2, 2, False), (1, 4, 1, 5, 5, False),
+    (1, 4, 1, 6, 6, False), (1, 4, 1, 24, 24, False),
+    (1, 4, 0, 4, 6, False),                      # valid padding
+    (1, 4, 1, 4, 4, True), (1, 4, 1, 8, 8, True),  # dense conv with the 2x2 pool
+    (2, 2, 0, 3, 6, False), (2, 2, 0, 12, 24, False),  # stride 2, even input
+    (2, 2, 1, 3, 5, False), (2, 2, 1, 6, 11, False),   # stride 2, odd input
+    (2, 2, 0, 1, 2, False),
+]
+
+
+@pytest.mark.parametrize("s,r,pt,ho,hin,pool", ROW_CASES)
+@pytest.mark.parametrize("strips", [1, 2, 3])
+def test_row_streaming_protocol_random_schedules(s, r, pt, ho, hin, pool, strips):
+    for seed in range(30):
+        RowModel(s, r, pt, ho, hin, pool, strips,
+                 random.Random(7919 * ho + 31 * hin + 3 * strips + seed)).run()

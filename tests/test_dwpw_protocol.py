@@ -1,0 +1,246 @@
+"""A model of the barrier protocol of the tile-per-row depthwise + pointwise
+pair (csrc/dwpw_tc.cu, k_dwpw_s8), run under random schedules on the CPU.
+
+Actors of one CTA, mirroring the kernel's loops: the TMA producer (per
+local tile i, stage i % stages: waits in_empty, issues the halo rows, which
+land on in_full at a random later time); two MMA threads, one for the even
+and one for the odd local tiles (per tile: wait tmem_empty[b] for the
+buffer, in_full for the rows; depthwise MMAs; commit in_empty and
+dw_full[b]; then the pointwise MMAs of the thread's previous tile once its
+A tile is ready, apw_full, committing pw_full), each with its own in-order
+commit stream; and G epilogue groups taking tiles in turn (wait dw_full,
+write the A tile, arrive apw_full; wait pw_full, store, arrive tmem_empty).
+The checks: no deadlock, no parity wait more than one phase off, a stage or
+buffer reused only after its release, the pointwise MMAs read the A tile of
+their own tile, and each tile's outputs are the ones its group expects.
+
+The kernel's present scheme fails the parity check under some schedules
+(test_dwpw_protocol_kernel_scheme, an expected failure): with five buffers
+over four epilogue groups the next tile of a buffer belongs to another
+group, and if the MMA thread of the buffer's previous tile lags a full tile
+behind the other thread, that group's wait for its tile returns at once.
+Two fixes pass every schedule: two dw_full / pw_full barriers per buffer,
+alternating with its use count, and one MMA thread per half of the pair.
+"""
+import random
+
+import pytest
+
+from test_pair_protocol import Barrier
+
+
+def dwpw_shape(cg, n):
+    """(buffers, groups) as DwPwShape<CG, N> computes them."""
+    bufs = min(8, 512 // (cg * 32 + n))
+    return bufs, (4 if bufs >= 4 else bufs)
+
+
+class DwPwModel:
+    def __init__(self, nb, g, stages, tiles, rng, even_odd=False, double=False):
+        self.nb, self.g, self.stages, self.tiles, self.rng = nb, g, stages, tiles, rng
+        self.even_odd, self.double = even_odd, double
+        self.in_full = [Barrier(f"in_full[{s}]", 1) for s in range(stages)]
+        self.in_empty = [Barrier(f"in_empty[{s}]", 1) for s in range(stages)]
+        # double: two dw_full / pw_full barriers per buffer, alternating with
+        # the buffer's use count (the fix kept for the even/odd threads).
+        nh = 2 if double else 1
+        self.dw_full = [[Barrier(f"dw_full[{b}][{h}]", 1) for h in range(nh)] for b in range(nb)]
+        self.apw_full = [Barrier(f"apw_full[{b}]", 4) for b in range(nb)]
+        self.pw_full = [[Barrier(f"pw_full[{b}][{h}]", 1) for h in range(nh)] for b in range(nb)]
+        self.tmem_empty = [Barrier(f"tmem_empty[{b}]", 4) for b in range(nb)]
+        self.loads = []              # stages whose rows are in flight
+        self.pipes = ([], [])        # per MMA thread, commits in issue order
+        self.stage = [None] * stages  # stage -> ("loading"/"ready"/"reading", tile) or "used"
+        self.buf = [None] * nb       # buffer -> [tile, state]
+        self.atile = [None] * nb     # A tile of buffer b -> tile
+        self.out = set()
+
+    def full_bar(self, bars, i):
+        """The dw_full / pw_full barrier of tile i and the phase to wait for."""
+        b, u = i % self.nb, i // self.nb
+        if self.double:
+            return bars[b][u & 1], u >> 1
+        return bars[b][0], u
+
+    @staticmethod
+    def wait(bar, target):
+        assert bar.done >= target, f"{bar.name}: wait for phase {target} at {bar.done} (two ahead)"
+        return bar, target
+
+    def producer(self):
+        for i in range(self.tiles):
+            s = i % self.stages
+            if i >= self.stages:
+                yield self.wait(self.in_empty[s], i // self.stages - 1)
+            assert self.stage[s] in (None, "used"), f"stage {s} overwritten: {self.stage[s]}"
+            self.stage[s] = ("loading", i)
+            self.loads.append(s)
+
+    def mma_dw(self):
+        """Depthwise MMAs of every tile, in tile order (the first MMA thread)."""
+        for i in range(self.tiles):
+            s, b = i % self.stages, i % self.nb
+            if i >= self.nb:
+                yield self.wait(self.tmem_empty[b], i // self.nb - 1)
+            yield self.wait(self.in_full[s], i // self.stages)
+            assert self.buf[b] is None, f"buffer {b} reused before its tile was stored"
+            assert self.stage[s] == ("ready", i), f"stage {s}: {self.stage[s]}"
+            self.buf[b] = [i, "dw"]
+            self.stage[s] = ("reading", i)
+            self.pipes[0].append(("in_empty", s, i))
+            self.pipes[0].append(("dw_full", b, i))
+
+    def mma_pw(self):
+        """Pointwise MMAs of every tile, in tile order (the second MMA thread)."""
+        for i in range(self.tiles):
+            b = i % self.nb
+            yield self.wait(self.apw_full[b], i // self.nb)
+            assert self.atile[b] == i, f"A tile of buffer {b} holds {self.atile[b]}, not {i}"
+            self.pipes[1].append(("pw_full", b, i))
+
+    def mma_even_odd(self, k):
+        """The earlier split: thread k took tiles k, k + 2, ..., issuing the
+        pointwise MMAs of a tile after the depthwise MMAs of its next one."""
+        prev = None
+        for i in range(k, self.tiles, 2):
+            s, b = i % self.stages, i % self.nb
+            if i >= self.nb:
+                yield self.wait(self.tmem_empty[b], i // self.nb - 1)
+            yield self.wait(self.in_full[s], i // self.stages)
+            assert self.buf[b] is None, f"buffer {b} reused before its tile was stored"
+            assert self.stage[s] == ("ready", i), f"stage {s}: {self.stage[s]}"
+            self.buf[b] = [i, "dw"]
+            self.stage[s] = ("reading", i)
+            self.pipes[k].append(("in_empty", s, i))
+            self.pipes[k].append(("dw_full", b, i))
+            if prev is not None:
+                yield from self.pointwise_of(k, prev)
+            prev = i
+        if prev is not None:
+            yield from self.pointwise_of(k, prev)
+
+    def pointwise_of(self, k, i):
+        b = i % self.nb
+        yield self.wait(self.apw_full[b], i // self.nb)
+        assert self.atile[b] == i, f"A tile of buffer {b} holds {self.atile[b]}, not {i}"
+        self.pipes[k].append(("pw_full", b, i))
+
+    def epilogue(self, grp):
+        for i in range(grp, self.tiles, self.g):
+            b = i % self.nb
+            yield self.wait(*self.full_bar(self.dw_full, i))
+            assert self.buf[b] == [i, "dw done"], f"buffer {b}: {self.buf[b]}, tile {i}"
+            self.atile[b] = i
+            self.apw_full[b].arrive(4)
+            yield self.wait(*self.full_bar(self.pw_full, i))
+            assert self.buf[b] == [i, "pw done"], f"buffer {b}: {self.buf[b]}, tile {i}"
+            self.out.add(i)
+            self.buf[b] = None
+            self.tmem_empty[b].arrive(4)
+
+    def complete(self, k):
+        kind, x, i = self.pipes[k].pop(0)
+        if kind == "in_empty":
+            self.stage[x] = "used"
+            self.in_empty[x].arrive()
+        elif kind == "dw_full":
+            self.buf[x][1] = "dw done"
+            self.full_bar(self.dw_full, i)[0].arrive()
+        else:
+            assert self.buf[x] == [i, "dw done"]
+            self.buf[x][1] = "pw done"
+            self.full_bar(self.pw_full, i)[0].arrive()
+
+    def run(self):
+        if self.even_odd:
+            actors = {"prod": self.producer(), "mma0": self.mma_even_odd(0),
+                      "mma1": self.mma_even_odd(1)}
+        else:
+            actors = {"prod": self.producer(), "mma0": self.mma_dw(), "mma1": self.mma_pw()}
+        for grp in range(self.g):
+            actors[f"epi{grp}"] = self.epilogue(grp)
+        pending = {}
+        live = set(actors)
+
+        def advance(k):
+            try:
+                bar, target = next(actors[k])
+                bar.waiters.append(target)
+                pending[k] = (bar, target)
+            except StopIteration:
+                live.discard(k)
+
+        for k in list(actors):
+            advance(k)
+        while live or self.loads or any(self.pipes):
+            ready = [k for k in live if pending[k][0].done > pending[k][1]]
+            choices = (ready + (["load"] if self.loads else []) +
+                       [f"pipe{k}" for k in (0, 1) if self.pipes[k]])
+            assert choices, f"deadlock: {[(k, pending[k][0].name, pending[k][1]) for k in live]}"
+            k = self.rng.choice(choices)
+            if k == "load":
+                s = self.loads.pop(self.rng.randrange(len(self.loads)))
+                self.stage[s] = ("ready", self.stage[s][1])
+                self.in_full[s].arrive()
+            elif k.startswith("pipe"):
+                self.complete(int(k[4:]))
+            else:
+                bar, target = pending.pop(k)
+                bar.waiters.remove(target)
+                advance(k)
+        assert self.out == set(range(self.tiles))
+
+
+SHAPES = [(1, 64), (2, 64), (1, 32), (1, 128), (2, 128)]
+
+
+@pytest.mark.xfail(strict=True, reason=(
+    "known: with the MMA threads on even and odd tiles and one dw_full barrier per buffer, "
+    "five buffers over four epilogue groups let a group's parity wait run a phase ahead "
+    "when one MMA thread lags a tile behind the other"))
+def test_dwpw_protocol_kernel_scheme():
+    """The kernel's present scheme (32 -> 64 channels: five buffers, four
+    groups, four stages, MMA threads on even and odd tiles)."""
+    for seed in range(300):
+        DwPwModel(5, 4, 4, 30, random.Random(seed), even_odd=True).run()
+
+
+@pytest.mark.parametrize("cg,n", [(1, 64), (2, 64), (1, 32), (1, 128)])
+@pytest.mark.parametrize("stages", [2, 4])
+@pytest.mark.parametrize("tiles", [1, 2, 7, 30])
+def test_dwpw_protocol_double_barriers(cg, n, stages, tiles):
+    """The even/odd threads with two dw_full / pw_full barriers per buffer,
+    alternating with its use count: a group's wait for tile i then follows
+    the same thread's tile i - 2 NB, which completed before the group's
+    previous tile, so no wait can run ahead."""
+    nb, g = dwpw_shape(cg, n)
+    for seed in range(15):
+        DwPwModel(nb, g, stages, tiles, random.Random(13 * nb + stages + 100 * tiles + seed),
+                  even_odd=True, double=True).run()
+
+
+@pytest.mark.parametrize("cg,n", SHAPES)
+@pytest.mark.parametrize("stages", [2, 3, 4, 5])
+@pytest.mark.parametrize("tiles", [1, 2, 7, 30])
+def test_dwpw_protocol_split_threads(cg, n, stages, tiles):
+    """One MMA thread per half (every tile's depthwise MMAs, every tile's
+    pointwise MMAs): every barrier's phases complete in tile order."""
+    nb, g = dwpw_shape(cg, n)
+    for seed in range(15):
+        DwPwModel(nb, g, stages, tiles,
+                  random.Random(31 * nb + 7 * g + 5 * stages + 1000 * tiles + seed)).run()
+
+
+@pytest.mark.parametrize("nb,g,stages,failure", [
+    (5, 4, 4, r"dw_full.*two ahead"),   # five buffers over four groups
+    (2, 2, 4, "deadlock"),              # two buffers
+    (4, 4, 3, r"in_full.*two ahead"),   # an odd number of input stages
+])
+def test_dwpw_protocol_even_odd_threads_hazards(nb, g, stages, failure):
+    """The hazards of the even/odd threads with one barrier per buffer: a
+    parity wait on dw_full running ahead (buffers not a multiple of the
+    groups), a deadlock of the pointwise-after-next order (two buffers), and
+    an MMA thread's wait on in_full running ahead (odd stage count)."""
+    with pytest.raises(AssertionError, match=failure):
+        for seed in range(300):
+            DwPwModel(nb, g, stages, 30, random.Random(seed), even_odd=True).run()

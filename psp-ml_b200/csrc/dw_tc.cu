@@ -451,7 +451,11 @@ cudaError_t launch_dw_tc_once(const pspml_op_desc& d, const PreparedOp& pp, int6
 
   const int param = static_cast<int>((dw_tc_param_smem(pp.ncls) + 15) / 16 * 16);
   const int overhead = 1024 + kBBytes + param + 64 * 8 + 64;
-  int stages = std::min(8, (kSmemLimit - overhead) / kAStage);
+  // An even count (8 for every shape today): the two MMA threads take
+  // alternate tiles, so each input stage is then always read by the same
+  // thread and its parity waits on the stage run in order.
+  int stages = std::min(8, (kSmemLimit - overhead) / kAStage) & ~1;
+  if (stages < 2) return cudaErrorInvalidValue;
   a.stages = stages;
   const int smem = std::max(overhead + stages * kAStage, 120 * 1024);
 

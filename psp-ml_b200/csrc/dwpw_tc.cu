@@ -424,7 +424,10 @@ cudaError_t launch_shape(const CUtensorMap& m, DwPwArgs a, const DwPwTable& tab,
                          int pwq, int num_sms, cudaStream_t s) {
   using S = DwPwShape<CG, N>;
   const int overhead = 1024 + S::kFixed + 64 * 8 + 64;
-  a.stages = std::min(4, (kSmemLimitF - overhead) / S::kStage);
+  // An even count (4 for both shapes): the two MMA threads take alternate
+  // tiles, so each input stage is then always read by the same thread and
+  // its parity waits on the stage run in order.
+  a.stages = std::min(4, (kSmemLimitF - overhead) / S::kStage) & ~1;
   if (a.stages < 2) return cudaErrorInvalidValue;
   const int smem = std::max(overhead + a.stages * S::kStage, 120 * 1024);
   const int grid = static_cast<int>(std::min<int64_t>(a.tiles, num_sms));

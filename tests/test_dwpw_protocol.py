@@ -244,3 +244,40 @@ def test_dwpw_protocol_even_odd_threads_hazards(nb, g, stages, failure):
     with pytest.raises(AssertionError, match=failure):
         for seed in range(300):
             DwPwModel(nb, g, stages, 30, random.Random(seed), even_odd=True).run()
+
+
+class DwTcModel(DwPwModel):
+    """The halo-row depthwise kernel (csrc/dw_tc.cu, k_dw_tc_s8): the same
+    producer, MMA threads on even and odd tiles committing empty[s] and
+    tfull[b] (no pointwise step), epilogue groups taking tiles in turn and
+    arriving on tempty[b]; eight buffers over four groups."""
+
+    def mma_even_odd(self, k):
+        for i in range(k, self.tiles, 2):
+            s, b = i % self.stages, i % self.nb
+            if i >= self.nb:
+                yield self.wait(self.tmem_empty[b], i // self.nb - 1)
+            yield self.wait(self.in_full[s], i // self.stages)
+            assert self.buf[b] is None, f"buffer {b} reused before its tile was stored"
+            assert self.stage[s] == ("ready", i), f"stage {s}: {self.stage[s]}"
+            self.buf[b] = [i, "dw"]
+            self.stage[s] = ("reading", i)
+            self.pipes[k].append(("in_empty", s, i))
+            self.pipes[k].append(("dw_full", b, i))
+
+    def epilogue(self, grp):
+        for i in range(grp, self.tiles, self.g):
+            b = i % self.nb
+            yield self.wait(*self.full_bar(self.dw_full, i))
+            assert self.buf[b] == [i, "dw done"], f"buffer {b}: {self.buf[b]}, tile {i}"
+            self.out.add(i)
+            self.buf[b] = None
+            self.tmem_empty[b].arrive(4)
+
+
+@pytest.mark.parametrize("stages", [2, 4, 8])
+@pytest.mark.parametrize("tiles", [1, 3, 9, 40])
+def test_dw_tc_protocol_random_schedules(stages, tiles):
+    for seed in range(20):
+        DwTcModel(8, 4, stages, tiles, random.Random(17 * stages + 100 * tiles + seed),
+                  even_odd=True).run()

@@ -148,3 +148,35 @@ def test_gemm_protocol_random_schedules(nb, g, spl, stages, kiters, tiles):
     for seed in range(12):
         GemmModel(nb, g, spl, stages, kiters, tiles,
                   random.Random(97 * nb + 13 * g + 7 * stages + kiters + 1000 * tiles + seed)).run()
+
+
+def test_epi_shape_mirror_matches_the_kernel(tmp_path):
+    """The model's epi_shape agrees with EpiShape<BN, MT, MODE> in
+    csrc/gemm_tc.cuh (compiled here as host code; no GPU needed)."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(nvcc).exists():
+        pytest.skip("nvcc not available")
+    csrc = Path(__file__).resolve().parents[1] / "psp-ml_b200" / "csrc"
+    combos = [(bn, mt, mode) for bn in (32, 64, 128, 256) for mt in (1, 2) for mode in range(4)
+              if not (mt == 2 and bn > 64)]
+    calls = "".join(f"show<{bn}, {mt}, {mode}>();" for bn, mt, mode in combos)
+    src = tmp_path / "shape.cu"
+    src.write_text(
+        '#include <cstdio>\n#include "gemm_tc.cuh"\nusing namespace pspml::tcg;\n'
+        "template <int BN, int MT, int MODE> void show() {\n"
+        "  using S = EpiShape<BN, MT, MODE>;\n"
+        '  std::printf("%d %d %d %d %d %d\\n", BN, MT, MODE, S::kBufs, S::kGroups, S::kSplit);\n'
+        "}\nint main() { " + calls + " return 0; }\n")
+    exe = tmp_path / "shape"
+    subprocess.run([nvcc, "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+                    "-I", str(csrc), str(src), "-o", str(exe)], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    for line in out.split("\n"):
+        if not line:
+            continue
+        bn, mt, mode, bufs, groups, split = map(int, line.split())
+        assert (bufs, groups, split) == epi_shape(bn, mt, mode in (1, 2)), line
